@@ -1,0 +1,527 @@
+// ccb_skel.cuh -- the hand-written sm_100a kernel skeletons.
+//
+// Lowering (lower.cpp) emits, per kernel, one functor struct `F` that carries
+// the fused scalar body of a CUDACaml graph (element loads, the inlined
+// element expression, stores, reduction combiners) and instantiates one of
+// the skeletons below with it. The skeletons own everything that is not the
+// body: loop structure, 128-bit vectorised access, warp-shuffle reductions
+// and scans, the single-pass last-block reduction, decoupled look-back,
+// per-row scheduling, atomics, the tiled product.
+//
+// They replace the per-node kernel templates of the reference compiler
+// (lib/lower/lower.ml:232-958) and its fixed geometry (lib/lower/schedule.ml).
+// The file is compiled by NVRTC for sm_100a only; it uses builtins and no
+// standard headers.
+//
+// Safety: every wait is bounded (a look-back gives up after a fixed number of
+// polls and raises ERR_LOOKBACK in the program's error word), and every
+// data-dependent index is checked (a bad gather or scatter index raises
+// ERR_GATHER_OOB / ERR_SCATTER_OOB and is clamped or skipped instead of
+// being dereferenced). No kernel traps.
+#pragma once
+
+namespace ccb {
+
+typedef unsigned long long u64;
+typedef long long i64;
+
+enum : unsigned { ERR_GATHER_OOB = 1u, ERR_SCATTER_OOB = 2u, ERR_LOOKBACK = 4u };
+constexpr unsigned FULL = 0xffffffffu;
+constexpr unsigned LOOKBACK_SPIN_LIMIT = 1u << 21;
+
+__device__ __forceinline__ void raise_error(unsigned* err, unsigned code) { atomicOr(err, code); }
+
+// A bounds-checked element index: out-of-range indices raise `code` and read
+// element 0 instead (the reference device kernel would read out of bounds).
+__device__ __forceinline__ int checked_index(int j, long long n, unsigned* err, unsigned code) {
+  if ((unsigned)j >= (unsigned long long)n) {
+    raise_error(err, code);
+    return 0;
+  }
+  return j;
+}
+
+// ---------------------------------------------------------------- vectors
+template <class T>
+struct __align__(16) V4 {
+  T v[4];
+};
+template <class T>
+__device__ __forceinline__ V4<T> ld4(const T* p) {
+  return *reinterpret_cast<const V4<T>*>(p);
+}
+template <class T>
+__device__ __forceinline__ void st4(T* p, const V4<T>& x) {
+  *reinterpret_cast<V4<T>*>(p) = x;
+}
+__device__ __forceinline__ bool aligned16(const void* p) { return (reinterpret_cast<u64>(p) & 15ull) == 0; }
+
+template <class T>
+__device__ __forceinline__ T ld_cg(const T* p) {
+  return __ldcg(p);
+}
+__device__ __forceinline__ unsigned ld_volatile(const unsigned* p) { return *(const volatile unsigned*)p; }
+__device__ __forceinline__ void st_volatile(unsigned* p, unsigned v) { *(volatile unsigned*)p = v; }
+
+// ---------------------------------------------------------------- warp/block reductions
+// Increasing shuffle offsets keep lane order: lane 0 ends with
+// v0 (+) v1 (+) ... (+) v31, so a merely associative combiner is respected.
+template <class F, class T>
+__device__ __forceinline__ T warp_reduce(int r, T v) {
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) v = F::combine(r, v, __shfl_down_sync(FULL, v, o));
+  return v;
+}
+
+// ---------------------------------------------------------------- map / map-reduce
+// F provides:
+//   struct P { ...; long long n; acc_t* partials; unsigned* ticket; unsigned* err; }
+//   typedef acc_t; static constexpr int NRED, VEC; static constexpr bool TAIL;
+//   init(acc_t*), identity(r), combine(r,a,b), elem(p,i,acc), elem4(p,i,acc),
+//   vec_ok(p), epilogue(p, const acc_t* res)
+template <class F>
+__device__ __forceinline__ void reduce_finish(const typename F::P& p, typename F::acc_t* acc) {
+  typedef typename F::acc_t T;
+  constexpr int R = F::NRED;
+  __shared__ T sh[R][33];
+  __shared__ int am_last;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    T v = warp_reduce<F>(r, acc[r]);
+    if (lane == 0) sh[r][warp] = v;
+  }
+  __syncthreads();
+  if (warp == 0) {
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      T v = lane < nw ? sh[r][lane] : F::identity(r);
+      v = warp_reduce<F>(r, v);
+      if (lane == 0) p.partials[(u64)blockIdx.x * R + r] = v;
+    }
+  }
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const unsigned t = atomicAdd(p.ticket, 1u);
+    am_last = (t == gridDim.x - 1);
+  }
+  __syncthreads();
+  if (!am_last) return;
+  // Last block: every partial is published. Fold them in a fixed order
+  // (thread t takes blocks t, t+B, ... ascending, then the ordered tree), so
+  // the result is reproducible for a given grid.
+  __threadfence();
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    T v = F::identity(r);
+    for (unsigned b = threadIdx.x; b < gridDim.x; b += blockDim.x) v = F::combine(r, v, ld_cg(&p.partials[(u64)b * R + r]));
+    acc[r] = v;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    T v = warp_reduce<F>(r, acc[r]);
+    if (lane == 0) sh[r][warp] = v;
+  }
+  __syncthreads();
+  if (warp == 0) {
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      T v = lane < nw ? sh[r][lane] : F::identity(r);
+      v = warp_reduce<F>(r, v);
+      if (lane == 0) sh[r][32] = v;
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    T res[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) res[r] = sh[r][32];
+    F::epilogue(p, res);
+    *p.ticket = 0u;  // ready for the next launch
+    __threadfence();
+  }
+}
+
+template <class F>
+__device__ __forceinline__ void map_reduce(const typename F::P& p) {
+  typedef typename F::acc_t T;
+  constexpr int R = F::NRED;
+  T acc[R > 0 ? R : 1];
+  F::init(acc);
+  const int n = (int)p.n;
+  const int tid = blockIdx.x * blockDim.x + threadIdx.x;
+  const int nth = gridDim.x * blockDim.x;
+  if (F::VEC && F::vec_ok(p)) {
+    const int n4 = n >> 2;
+    int g = tid;
+    for (; g + nth < n4; g += 2 * nth) {
+      F::elem4(p, g << 2, acc);
+      F::elem4(p, (g + nth) << 2, acc);
+    }
+    if (g < n4) F::elem4(p, g << 2, acc);
+    for (int i = (n4 << 2) + tid; i < n; i += nth) F::elem(p, i, acc);
+  } else {
+    for (int i = tid; i < n; i += nth) F::elem(p, i, acc);
+  }
+  if constexpr (R > 0) {
+    reduce_finish<F>(p, acc);
+  } else if constexpr (F::TAIL) {
+    if (blockIdx.x == 0 && threadIdx.x == 0) F::epilogue(p, acc);
+  }
+}
+
+// ---------------------------------------------------------------- block scan helpers
+// Inclusive warp scan, order preserving (earlier lanes on the left).
+template <class F, class T>
+__device__ __forceinline__ T warp_scan_incl(T v, int lane) {
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    T y = __shfl_up_sync(FULL, v, o);
+    if (lane >= o) v = F::combine(y, v);
+  }
+  return v;
+}
+
+// Block-wide exclusive scan of one value per thread. Returns the exclusive
+// prefix of this thread; *total receives the block total. BLOCK threads.
+template <class F, int BLOCK, class T>
+__device__ __forceinline__ T block_scan_excl(T v, T* total, T* s_warp /* [BLOCK/32 + 1] */) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  constexpr int NW = BLOCK / 32;
+  T incl = warp_scan_incl<F>(v, lane);
+  T excl_in_warp = __shfl_up_sync(FULL, incl, 1);
+  if (lane == 0) excl_in_warp = F::identity();
+  if (lane == 31) s_warp[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    T w = lane < NW ? s_warp[lane] : F::identity();
+    w = warp_scan_incl<F>(w, lane);
+    if (lane < NW) s_warp[lane] = w;
+  }
+  __syncthreads();
+  const T warp_prefix = warp == 0 ? F::identity() : s_warp[warp - 1];
+  *total = s_warp[NW - 1];
+  return warp == 0 ? excl_in_warp : F::combine(warp_prefix, excl_in_warp);
+}
+
+// ---------------------------------------------------------------- single-pass flat scan
+// Decoupled look-back (Merrill & Garland, "Single-pass Parallel Prefix Scan
+// with Decoupled Look-back", 2016). Tiles are claimed in launch order through
+// p.tile_counter, so a tile only ever waits on tiles that are already running.
+// Status words carry the launch epoch, so no clearing pass is needed between
+// launches. F provides T, identity(), combine(a,b), load(p,i), load4(p,i,T*),
+// store(p,i,v), store4(p,i,const T*), vec_ok(p); P provides n, tile_counter,
+// flags, aggs, incls, epoch, err.
+template <class F>
+__device__ __forceinline__ typename F::T lookback(const typename F::P& p, unsigned tile, typename F::T agg, int lane) {
+  typedef typename F::T T;
+  const unsigned ep = p.epoch << 2;
+  if (tile == 0) {
+    if (lane == 0) {
+      p.incls[0] = agg;
+      __threadfence();
+      st_volatile(&p.flags[0], ep | 2u);
+    }
+    return F::identity();
+  }
+  if (lane == 0) {
+    p.aggs[tile] = agg;
+    __threadfence();
+    st_volatile(&p.flags[tile], ep | 1u);
+  }
+  T prefix = F::identity();
+  long long pred = (long long)tile - 1;
+  unsigned spins = 0;
+  while (true) {
+    const long long idx = pred - lane;
+    unsigned f;
+    while (true) {
+      f = idx >= 0 ? ld_volatile(&p.flags[idx]) : (ep | 2u);
+      const bool valid = (f & ~3u) == ep && (f & 3u) != 0u;
+      if (__all_sync(FULL, valid)) break;
+      if (++spins > LOOKBACK_SPIN_LIMIT) {
+        if (lane == 0) raise_error(p.err, ERR_LOOKBACK);
+        return F::identity();
+      }
+      __nanosleep(20);
+    }
+    __threadfence();
+    T v = F::identity();
+    if (idx >= 0) v = ((f & 3u) == 2u) ? ld_cg(&p.incls[idx]) : ld_cg(&p.aggs[idx]);
+    const unsigned pmask = __ballot_sync(FULL, (f & 3u) == 2u);
+    const int stop = pmask ? __ffs(pmask) - 1 : 31;
+    if (lane > stop) v = F::identity();
+    // Lane l holds tile pred-l: higher lanes are older, so fold right to left.
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      T y = __shfl_down_sync(FULL, v, o);
+      v = F::combine(y, v);
+    }
+    const T window = __shfl_sync(FULL, v, 0);
+    prefix = F::combine(window, prefix);
+    if (pmask) break;
+    pred -= 32;
+  }
+  if (lane == 0) {
+    p.incls[tile] = F::combine(prefix, agg);
+    __threadfence();
+    st_volatile(&p.flags[tile], ep | 2u);
+  }
+  return prefix;
+}
+
+template <class F, int ITEMS>
+__device__ __forceinline__ void scan_flat(const typename F::P& p) {
+  typedef typename F::T T;
+  constexpr int BLOCK = 256;
+  constexpr long long TILE = (long long)BLOCK * ITEMS;
+  __shared__ unsigned s_tile;
+  __shared__ T s_warp[BLOCK / 32 + 1];
+  __shared__ T s_prefix;
+  if (threadIdx.x == 0) s_tile = atomicAdd(p.tile_counter, 1u);
+  __syncthreads();
+  const unsigned tile = s_tile;
+  const long long n = p.n;
+  const long long base = (long long)tile * TILE + (long long)threadIdx.x * ITEMS;
+  T x[ITEMS];
+  const bool full_vec = F::VEC && base + ITEMS <= n && F::vec_ok(p);
+  if (full_vec) {
+#pragma unroll
+    for (int k = 0; k < ITEMS; k += 4) F::load4(p, base + k, &x[k]);
+  } else {
+#pragma unroll
+    for (int k = 0; k < ITEMS; ++k) x[k] = (base + k < n) ? F::load(p, base + k) : F::identity();
+  }
+#pragma unroll
+  for (int k = 1; k < ITEMS; ++k) x[k] = F::combine(x[k - 1], x[k]);
+  T total;
+  const T excl = block_scan_excl<F, BLOCK>(x[ITEMS - 1], &total, s_warp);
+  if ((threadIdx.x >> 5) == 0) {
+    const T prefix = lookback<F>(p, tile, total, threadIdx.x & 31);
+    if (threadIdx.x == 0) s_prefix = prefix;
+  }
+  __syncthreads();
+  const T pre = F::combine(s_prefix, excl);
+#pragma unroll
+  for (int k = 0; k < ITEMS; ++k) x[k] = F::combine(pre, x[k]);
+  if (full_vec) {
+#pragma unroll
+    for (int k = 0; k < ITEMS; k += 4) F::store4(p, base + k, &x[k]);
+  } else {
+#pragma unroll
+    for (int k = 0; k < ITEMS; ++k)
+      if (base + k < n) F::store(p, base + k, x[k]);
+  }
+  // The block holding the last ticket runs after every other block has taken
+  // its ticket, so it can rearm the counter for the next launch.
+  if (threadIdx.x == 0 && tile == gridDim.x - 1) atomicExch(p.tile_counter, 0u);
+}
+
+// ---------------------------------------------------------------- rows
+// Row kernels over [rows; n] (last axis). F provides T, identity(),
+// combine(a,b), load(p,i), load4(p,i,T*), vec_ok(p) and, for reductions,
+// store_row(p,r,v); for scans store(p,i,v), store4(p,i,const T*).
+template <class F>
+__device__ __forceinline__ void reduce_rows_block(const typename F::P& p) {
+  typedef typename F::T T;
+  __shared__ T sh[33];
+  const long long n = p.n;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  const bool vec = F::VEC && (n & 3) == 0 && F::vec_ok(p);
+  for (long long row = blockIdx.x; row < p.rows; row += gridDim.x) {
+    const long long base = row * n;
+    T acc = F::identity();
+    if (vec) {
+      long long j = (long long)threadIdx.x * 4;
+      const long long step = (long long)blockDim.x * 4;
+      for (; j + step < n; j += 2 * step) {
+        T a[4], b[4];
+        F::load4(p, base + j, a);
+        F::load4(p, base + j + step, b);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) acc = F::combine(acc, a[k]);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) acc = F::combine(acc, b[k]);
+      }
+      if (j < n) {
+        T a[4];
+        F::load4(p, base + j, a);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) acc = F::combine(acc, a[k]);
+      }
+    } else {
+      for (long long j = threadIdx.x; j < n; j += blockDim.x) acc = F::combine(acc, F::load(p, base + j));
+    }
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) acc = F::combine(acc, __shfl_down_sync(FULL, acc, o));
+    if (lane == 0) sh[warp] = acc;
+    __syncthreads();
+    if (warp == 0) {
+      T v = lane < nw ? sh[lane] : F::identity();
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) v = F::combine(v, __shfl_down_sync(FULL, v, o));
+      if (lane == 0) F::store_row(p, row, v);
+    }
+    __syncthreads();
+  }
+}
+
+template <class F>
+__device__ __forceinline__ void reduce_rows_warp(const typename F::P& p) {
+  typedef typename F::T T;
+  const long long n = p.n;
+  const int lane = threadIdx.x & 31;
+  const long long wid = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const long long nwarps = ((long long)gridDim.x * blockDim.x) >> 5;
+  for (long long row = wid; row < p.rows; row += nwarps) {
+    const long long base = row * n;
+    T acc = F::identity();
+    for (long long j = lane; j < n; j += 32) acc = F::combine(acc, F::load(p, base + j));
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) acc = F::combine(acc, __shfl_down_sync(FULL, acc, o));
+    if (lane == 0) F::store_row(p, row, acc);
+  }
+}
+
+// One block per row; the row is walked in chunks of BLOCK*ITEMS with a carry.
+template <class F, int ITEMS>
+__device__ __forceinline__ void scan_rows_block(const typename F::P& p) {
+  typedef typename F::T T;
+  constexpr int BLOCK = 256;
+  __shared__ T s_warp[BLOCK / 32 + 1];
+  const long long n = p.n;
+  const bool vec = F::VEC && (n & 3) == 0 && F::vec_ok(p);
+  for (long long row = blockIdx.x; row < p.rows; row += gridDim.x) {
+    const long long rbase = row * n;
+    T carry = F::identity();
+    for (long long c0 = 0; c0 < n; c0 += (long long)BLOCK * ITEMS) {
+      const long long j0 = c0 + (long long)threadIdx.x * ITEMS;
+      T x[ITEMS];
+      const bool fv = vec && j0 + ITEMS <= n;
+      if (fv) {
+#pragma unroll
+        for (int k = 0; k < ITEMS; k += 4) F::load4(p, rbase + j0 + k, &x[k]);
+      } else {
+#pragma unroll
+        for (int k = 0; k < ITEMS; ++k) x[k] = (j0 + k < n) ? F::load(p, rbase + j0 + k) : F::identity();
+      }
+#pragma unroll
+      for (int k = 1; k < ITEMS; ++k) x[k] = F::combine(x[k - 1], x[k]);
+      T total;
+      const T excl = block_scan_excl<F, BLOCK>(x[ITEMS - 1], &total, s_warp);
+      const T pre = F::combine(carry, excl);
+#pragma unroll
+      for (int k = 0; k < ITEMS; ++k) x[k] = F::combine(pre, x[k]);
+      if (fv) {
+#pragma unroll
+        for (int k = 0; k < ITEMS; k += 4) F::store4(p, rbase + j0 + k, &x[k]);
+      } else {
+#pragma unroll
+        for (int k = 0; k < ITEMS; ++k)
+          if (j0 + k < n) F::store(p, rbase + j0 + k, x[k]);
+      }
+      carry = F::combine(carry, total);
+      __syncthreads();
+    }
+  }
+}
+
+// One warp per row, for rows shorter than a block's chunk.
+template <class F>
+__device__ __forceinline__ void scan_rows_warp(const typename F::P& p) {
+  typedef typename F::T T;
+  const long long n = p.n;
+  const int lane = threadIdx.x & 31;
+  const long long wid = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const long long nwarps = ((long long)gridDim.x * blockDim.x) >> 5;
+  for (long long row = wid; row < p.rows; row += nwarps) {
+    const long long rbase = row * n;
+    T carry = F::identity();
+    for (long long c0 = 0; c0 < n; c0 += 32) {
+      const long long j = c0 + lane;
+      T x = j < n ? F::load(p, rbase + j) : F::identity();
+      T incl = warp_scan_incl<F>(x, lane);
+      T v = F::combine(carry, incl);
+      if (j < n) F::store(p, rbase + j, v);
+      carry = __shfl_sync(FULL, v, 31);
+    }
+  }
+}
+
+// ---------------------------------------------------------------- scatter_add
+// out is zero-filled by the executor (a memset) before this runs; every
+// element lands through an atomic add. F provides T, idx(p,i), val(p,i);
+// P provides n (source elements), m (output elements), out, err.
+template <class F>
+__device__ __forceinline__ void scatter_add(const typename F::P& p) {
+  const long long n = p.n;
+  const long long nth = (long long)gridDim.x * blockDim.x;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += nth) {
+    const int j = F::idx(p, i);
+    const typename F::T v = F::val(p, i);
+    if ((unsigned)j >= (unsigned long long)p.m) {
+      raise_error(p.err, ERR_SCATTER_OOB);
+      continue;
+    }
+    atomicAdd(&p.out[j], v);
+  }
+}
+
+// ---------------------------------------------------------------- matmul (CUDA cores)
+// C[M,N] = A[M,K] . B[K,N], row-major, each output accumulated in ascending k
+// (the reference's contract, lib/ir/tensor.ml:35-40). 64x64 output tile per
+// 256-thread block, 4x4 outputs per thread, K staged 16 at a time through
+// shared memory. F provides T, a(p,row,k), b(p,k,col), store(p,row,col,v);
+// P provides M, N, K.
+template <class F>
+__device__ __forceinline__ void matmul_tiled(const typename F::P& p) {
+  typedef typename F::T T;
+  constexpr int BM = 64, BN = 64, BK = 16;
+  __shared__ T As[BK][BM + 1];
+  __shared__ T Bs[BK][BN + 1];
+  const long long M = p.M, N = p.N, K = p.K;
+  const int tid = threadIdx.x;
+  const int tx = tid & 15, ty = tid >> 4;
+  const long long row0 = (long long)blockIdx.y * BM, col0 = (long long)blockIdx.x * BN;
+  T acc[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j] = T(0);
+  for (long long k0 = 0; k0 < K; k0 += BK) {
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int idx = tid + e * 256;  // 0..1023
+      const int ar = idx >> 4, ak = idx & 15;   // A tile: 64 rows x 16 k
+      const long long gr = row0 + ar, gk = k0 + ak;
+      As[ak][ar] = (gr < M && gk < K) ? F::a(p, gr, gk) : T(0);
+      const int bk = idx >> 6, bc = idx & 63;   // B tile: 16 k x 64 cols
+      const long long gk2 = k0 + bk, gc = col0 + bc;
+      Bs[bk][bc] = (gk2 < K && gc < N) ? F::b(p, gk2, gc) : T(0);
+    }
+    __syncthreads();
+#pragma unroll
+    for (int kk = 0; kk < BK; ++kk) {
+      T a[4], b[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) a[i] = As[kk][ty + 16 * i];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) b[j] = Bs[kk][tx + 16 * j];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] += a[i] * b[j];
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const long long r = row0 + ty + 16 * i, c = col0 + tx + 16 * j;
+      if (r < M && c < N) F::store(p, r, c, acc[i][j]);
+    }
+}
+
+}  // namespace ccb

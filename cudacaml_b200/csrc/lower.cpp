@@ -1,0 +1,1664 @@
+// Graph -> sm_100a kernels + host plan. See lower.hpp.
+//
+// What differs from the reference compiler, by design:
+//  * Materialisation (lib/lower/fusion.ml:54-55 gives a buffer to every node
+//    with fan-out >= 2). Here an element-wise node owns a buffer only when it
+//    is an output; every other use recomputes it inline, and within one kernel
+//    the fused expression DAG is hash-consed so a shared node is computed once
+//    per element. A Philox normal feeding three consumers is generated once
+//    in registers instead of round-tripping through HBM.
+//  * Horizontal fusion. Kernel roots that range over the same index space and
+//    do not depend on each other's results share one "map-reduce" launch: any
+//    number of element-wise stores and flat reductions in one pass (saxpy's r
+//    and sum r; the Greeks' four path sums; the cells of a skinny product).
+//  * Invariant factoring. A flat add-reduction whose element is c * g(i), with
+//    c loop-invariant but dependent on another reduction of the same pass, is
+//    accumulated as sum g(i) and multiplied by c after the pass (sum is
+//    linear). This is what lets a Grad-produced adjoint, whose seed is a
+//    broadcast of the forward sum, join the forward sum's pass. Rounding
+//    differs from the interpreter's sequential fold only within tolerance.
+//  * Scalar tails. Outputs of one element that only need this pass's results
+//    (price = mean * discount, the gradients) are evaluated by the last block
+//    after the final fold, not by separate launches.
+#include "lower.hpp"
+
+#include <algorithm>
+#include <cinttypes>
+#include <cmath>
+#include <cstring>
+#include <functional>
+#include <map>
+#include <set>
+#include <sstream>
+#include <stdexcept>
+#include <unordered_map>
+#include <cstdio>
+#include <cstdlib>
+
+#include "common.hpp"
+
+namespace ccb {
+
+int dt_size(Dt d) { return (d == DT_F32 || d == DT_I32) ? 4 : (d == DT_BOOL ? 1 : 8); }
+const char* dt_name(Dt d) {
+  static const char* n[] = {"f32", "f64", "i32", "i64", "bool"};
+  return n[d];
+}
+const char* dt_ctype(Dt d) {
+  static const char* n[] = {"float", "double", "int", "long long", "bool"};
+  return n[d];
+}
+static bool is_float(Dt d) { return d == DT_F32 || d == DT_F64; }
+static bool is_int(Dt d) { return d == DT_I32 || d == DT_I64; }
+
+struct LowerError : std::runtime_error {
+  int code;
+  LowerError(int c, const std::string& m) : std::runtime_error(m), code(c) {}
+};
+static void bad(const std::string& m) { throw LowerError(CCB_ERR_INVALID, m); }
+static void unsupported(const std::string& m) { throw LowerError(CCB_ERR_UNSUPPORTED, m); }
+
+// ===================================================================== parse
+static Dt parse_dt(const std::string& s) {
+  if (s == "f32") return DT_F32;
+  if (s == "f64") return DT_F64;
+  if (s == "i32") return DT_I32;
+  if (s == "i64") return DT_I64;
+  if (s == "bool") return DT_BOOL;
+  bad("wire: unknown dtype " + s);
+  return DT_F32;
+}
+static int lookup(const char* const* names, int n, const std::string& s, const char* what) {
+  for (int k = 0; k < n; ++k)
+    if (s == names[k]) return k;
+  bad(std::string("wire: unknown ") + what + " " + s);
+  return 0;
+}
+static const char* const kBin[] = {"add", "sub", "mul", "div", "min", "max", "bit_and", "bit_or", "bit_xor", "shl", "shr"};
+static const char* const kUn[] = {"neg", "sqrt", "exp", "log", "abs", "sin", "cos", "erf", "erfinv"};
+static const char* const kCmp[] = {"eq", "ne", "lt", "le", "gt", "ge"};
+static const char* const kLogic[] = {"and", "or"};
+static const char* const kTk[] = {"param", "iota", "map", "map2", "reduce", "scan", "gather", "scatter_add", "matmul", "reshape", "broadcast"};
+
+int parse_graph(const char* text, GGraph& g) {
+  try {
+    std::istringstream in(text);
+    std::string line;
+    std::unordered_map<int64_t, int> eidx, tidx;
+    bool header = false, ended = false;
+    auto E = [&](int64_t id) {
+      auto it = eidx.find(id);
+      if (it == eidx.end()) bad("wire: unknown expression id " + std::to_string(id));
+      return it->second;
+    };
+    auto T = [&](int64_t id) {
+      auto it = tidx.find(id);
+      if (it == tidx.end()) bad("wire: unknown tensor id " + std::to_string(id));
+      return it->second;
+    };
+    while (std::getline(in, line)) {
+      if (line.empty()) continue;
+      std::istringstream ls(line);
+      std::string tag;
+      ls >> tag;
+      if (tag == "ccbgraph") {
+        int v = 0;
+        ls >> v;
+        if (v != 1) bad("wire: unsupported version");
+        header = true;
+      } else if (tag == "name") {
+        ls >> g.name;
+      } else if (tag == "e") {
+        int64_t id;
+        std::string dts, kind;
+        ls >> id >> dts >> kind;
+        GExpr e;
+        e.dt = parse_dt(dts);
+        if (kind == "const") {
+          e.kind = E_CONST;
+          std::string v;
+          ls >> v;
+          if (is_float(e.dt)) {
+            uint64_t bits = std::stoull(v, nullptr, 16);
+            std::memcpy(&e.f, &bits, 8);
+          } else {
+            e.i = std::stoll(v);
+          }
+        } else if (kind == "arg") {
+          e.kind = E_ARG;
+          ls >> e.i;
+        } else if (kind == "index") {
+          e.kind = E_INDEX;
+        } else if (kind == "binop" || kind == "cmp" || kind == "logic") {
+          std::string op;
+          int64_t a, b;
+          ls >> op >> a >> b;
+          e.kind = kind == "binop" ? E_BINOP : (kind == "cmp" ? E_CMP : E_LOGIC);
+          e.op = kind == "binop" ? lookup(kBin, 11, op, "binop") : (kind == "cmp" ? lookup(kCmp, 6, op, "cmp") : lookup(kLogic, 2, op, "logic"));
+          e.a = E(a);
+          e.b = E(b);
+        } else if (kind == "unop") {
+          std::string op;
+          int64_t a;
+          ls >> op >> a;
+          e.kind = E_UNOP;
+          e.op = lookup(kUn, 9, op, "unop");
+          e.a = E(a);
+        } else if (kind == "not" || kind == "cast") {
+          int64_t a;
+          ls >> a;
+          e.kind = kind == "not" ? E_NOT : E_CAST;
+          e.a = E(a);
+        } else if (kind == "select") {
+          int64_t c, a, b;
+          ls >> c >> a >> b;
+          e.kind = E_SELECT;
+          e.a = E(c);
+          e.b = E(a);
+          e.c = E(b);
+        } else {
+          bad("wire: unknown expression kind " + kind);
+        }
+        if (ls.fail()) bad("wire: malformed line: " + line);
+        eidx[id] = (int)g.ex.size();
+        g.ex.push_back(e);
+      } else if (tag == "t") {
+        GTensor t;
+        std::string dts, kind;
+        int rank = 0;
+        ls >> t.uid >> dts >> rank;
+        t.dt = parse_dt(dts);
+        t.shape.resize(rank);
+        t.numel = 1;
+        for (int k = 0; k < rank; ++k) {
+          ls >> t.shape[k];
+          t.numel *= t.shape[k];
+        }
+        ls >> kind;
+        t.kind = lookup(kTk, 11, kind, "tensor kind");
+        int64_t a, b, x, y, z, w;
+        switch (t.kind) {
+          case T_PARAM: ls >> t.name; break;
+          case T_IOTA: break;
+          case T_MAP:
+            ls >> a >> x >> z;
+            t.dep0 = T(a);
+            t.arg0 = E(x);
+            t.body = E(z);
+            break;
+          case T_MAP2:
+            ls >> a >> b >> x >> y >> z;
+            t.dep0 = T(a);
+            t.dep1 = T(b);
+            t.arg0 = E(x);
+            t.arg1 = E(y);
+            t.body = E(z);
+            break;
+          case T_REDUCE:
+          case T_SCAN:
+            ls >> a >> x >> y >> z >> w;
+            t.dep0 = T(a);
+            t.arg0 = E(x);
+            t.arg1 = E(y);
+            t.body = E(z);
+            t.init = E(w);
+            break;
+          case T_GATHER:
+          case T_SCATTER:
+          case T_MATMUL:
+            ls >> a >> b;
+            t.dep0 = T(a);
+            t.dep1 = T(b);
+            break;
+          default:
+            ls >> a;
+            t.dep0 = T(a);
+        }
+        if (ls.fail()) bad("wire: malformed line: " + line);
+        if (t.numel >= (int64_t(1) << 31)) unsupported("tensor of " + std::to_string(t.numel) + " elements: indices are int32");
+        tidx[t.uid] = (int)g.ts.size();
+        g.ts.push_back(t);
+      } else if (tag == "o") {
+        std::string nm;
+        int64_t id;
+        ls >> nm >> id;
+        g.outputs.push_back({nm, T(id)});
+      } else if (tag == "end") {
+        ended = true;
+      } else {
+        bad("wire: bad line: " + line);
+      }
+    }
+    if (!header || !ended) bad("wire: truncated graph text");
+  } catch (const LowerError& e) {
+    return fail(e.code, e.what());
+  } catch (const std::exception& e) {
+    return fail(CCB_ERR_INVALID, std::string("wire: ") + e.what());
+  }
+  return CCB_OK;
+}
+
+// ===================================================================== kernel expression IR
+// A hash-consed DAG of scalar operations over loads, the loop index and (in
+// an epilogue) the final values of the pass's reductions.
+enum KOp { K_CONST, K_INDEX, K_LOAD, K_BIN, K_UN, K_CMP, K_LOGIC, K_NOT, K_SELECT, K_CAST, K_REDVAL, K_CHECK, K_ARG };
+
+struct KN {
+  int op = K_CONST;
+  Dt dt = DT_I32;
+  int a = -1, b = -1, c = -1;
+  int sub = 0;
+  double f = 0;
+  int64_t iv = 0;
+  int buf = -1;
+  // properties
+  bool late = false;     // depends on a reduction of this pass (epilogue only)
+  bool variant = false;  // depends on the loop index
+  bool ranged = false;   // integer value range known
+  int64_t lo = 0, hi = 0;
+};
+
+struct KCtx {
+  std::vector<KN> n;
+  std::unordered_map<std::string, int> hc;
+  int64_t ilo = 0, ihi = 0;
+  int index_node = -1;
+
+  static std::string key(const KN& k) {
+    char buf[200];
+    uint64_t fb;
+    std::memcpy(&fb, &k.f, 8);
+    snprintf(buf, sizeof buf, "%d|%d|%d|%d|%d|%d|%" PRIx64 "|%" PRId64 "|%d", k.op, (int)k.dt, k.a, k.b, k.c, k.sub, fb, k.iv, k.buf);
+    return buf;
+  }
+
+  int mk(KN k) {
+    fold(k);
+    if (k.op == K_CONST && is_int(k.dt)) {
+      k.ranged = true;
+      k.lo = k.hi = k.iv;
+    }
+    std::string ky = key(k);
+    auto it = hc.find(ky);
+    if (it != hc.end()) return it->second;
+    props(k);
+    if (k.ranged && k.lo == k.hi && k.dt == DT_I32 && k.op != K_CONST) {
+      KN c;
+      c.op = K_CONST;
+      c.dt = DT_I32;
+      c.iv = k.lo;
+      return mk(c);
+    }
+    int id = (int)n.size();
+    n.push_back(k);
+    hc[ky] = id;
+    return id;
+  }
+
+  int cint(Dt dt, int64_t v) {
+    KN k;
+    k.op = K_CONST;
+    k.dt = dt;
+    k.iv = v;
+    return mk(k);
+  }
+  int cfloat(Dt dt, double v) {
+    KN k;
+    k.op = K_CONST;
+    k.dt = dt;
+    k.f = dt == DT_F32 ? (double)(float)v : v;
+    return mk(k);
+  }
+  int one(Dt dt) { return is_float(dt) ? cfloat(dt, 1.0) : cint(dt, 1); }
+  int index() {
+    if (index_node < 0) {
+      KN k;
+      k.op = K_INDEX;
+      k.dt = DT_I32;
+      index_node = mk(k);
+    }
+    return index_node;
+  }
+  int bin(Dt dt, int op, int a, int b) {
+    KN k;
+    k.op = K_BIN;
+    k.dt = dt;
+    k.sub = op;
+    k.a = a;
+    k.b = b;
+    return mk(k);
+  }
+  int un(Dt dt, int op, int a) {
+    KN k;
+    k.op = K_UN;
+    k.dt = dt;
+    k.sub = op;
+    k.a = a;
+    return mk(k);
+  }
+  int load(Dt dt, int buf, int idx) {
+    KN k;
+    k.op = K_LOAD;
+    k.dt = dt;
+    k.buf = buf;
+    k.a = idx;
+    return mk(k);
+  }
+
+ private:
+  static int64_t wrap(Dt dt, int64_t v) { return dt == DT_I32 ? (int64_t)(int32_t)(uint32_t)(uint64_t)v : v; }
+
+  void fold(KN& k) {
+    // Integer constant folding with the wrapping semantics of the device
+    // code; index arithmetic (transpose, rows_of) collapses this way.
+    if (k.op == K_BIN && is_int(k.dt) && n[k.a].op == K_CONST && n[k.b].op == K_CONST) {
+      const int64_t x = n[k.a].iv, y = n[k.b].iv;
+      const uint64_t ux = (uint64_t)x, uy = (uint64_t)y;
+      int64_t v;
+      bool ok = true;
+      switch (k.sub) {
+        case B_ADD: v = (int64_t)(ux + uy); break;
+        case B_SUB: v = (int64_t)(ux - uy); break;
+        case B_MUL: v = (int64_t)(ux * uy); break;
+        case B_DIV:
+          ok = y != 0 && !(y == -1 && x == (k.dt == DT_I32 ? INT32_MIN : INT64_MIN));
+          v = ok ? x / y : 0;
+          break;
+        case B_MIN: v = x < y ? x : y; break;
+        case B_MAX: v = x > y ? x : y; break;
+        case B_AND: v = x & y; break;
+        case B_OR: v = x | y; break;
+        case B_XOR: v = x ^ y; break;
+        default: ok = false; v = 0;
+      }
+      if (ok) {
+        const Dt dt = k.dt;
+        k = KN();
+        k.op = K_CONST;
+        k.dt = dt;
+        k.iv = wrap(dt, v);
+      }
+    }
+  }
+
+  void props(KN& k) {
+    switch (k.op) {
+      case K_CONST: break;
+      case K_ARG: break;
+      case K_INDEX:
+        k.variant = true;
+        k.ranged = true;
+        k.lo = ilo;
+        k.hi = ihi;
+        break;
+      case K_REDVAL: k.late = true; break;
+      default: {
+        for (int ch : {k.a, k.b, k.c})
+          if (ch >= 0) {
+            k.late = k.late || n[ch].late;
+            k.variant = k.variant || n[ch].variant;
+          }
+      }
+    }
+    if (k.op == K_CHECK) {
+      const KN& a = n[k.a];
+      if (a.ranged && a.lo >= 0 && a.hi < k.iv) {
+        k.ranged = true;
+        k.lo = a.lo;
+        k.hi = a.hi;
+      }
+    }
+    if (k.op == K_BIN && k.dt == DT_I32) {
+      const KN& a = n[k.a];
+      const KN& b = n[k.b];
+      if (a.ranged && b.ranged) {
+        int64_t lo = 0, hi = 0;
+        bool ok = true;
+        switch (k.sub) {
+          case B_ADD: lo = a.lo + b.lo; hi = a.hi + b.hi; break;
+          case B_SUB: lo = a.lo - b.hi; hi = a.hi - b.lo; break;
+          case B_MUL: {
+            int64_t c[4] = {a.lo * b.lo, a.lo * b.hi, a.hi * b.lo, a.hi * b.hi};
+            lo = *std::min_element(c, c + 4);
+            hi = *std::max_element(c, c + 4);
+            ok = std::llabs(a.lo) < (1ll << 31) && std::llabs(a.hi) < (1ll << 31) && std::llabs(b.lo) < (1ll << 31) &&
+                 std::llabs(b.hi) < (1ll << 31);
+            break;
+          }
+          case B_DIV:
+            ok = b.lo == b.hi && b.lo > 0 && a.lo >= 0;
+            if (ok) {
+              lo = a.lo / b.lo;
+              hi = a.hi / b.lo;
+            }
+            break;
+          default: ok = false;
+        }
+        if (ok && lo >= INT32_MIN && hi <= INT32_MAX) {
+          k.ranged = true;
+          k.lo = lo;
+          k.hi = hi;
+        }
+      }
+    }
+  }
+};
+
+// ===================================================================== text helpers
+static std::string lit(const KN& k) {
+  char b[96];
+  switch (k.dt) {
+    case DT_F32: {
+      float v = (float)k.f;
+      if (std::isnan(v)) return "__int_as_float(0x7fc00000)";
+      if (std::isinf(v)) return v > 0 ? "__int_as_float(0x7f800000)" : "__int_as_float((int)0xff800000)";
+      snprintf(b, sizeof b, "(%af)", (double)v);
+      return b;
+    }
+    case DT_F64: {
+      double v = k.f;
+      if (std::isnan(v)) return "__longlong_as_double(0x7ff8000000000000LL)";
+      if (std::isinf(v)) return v > 0 ? "__longlong_as_double(0x7ff0000000000000LL)" : "__longlong_as_double((long long)0xfff0000000000000ULL)";
+      snprintf(b, sizeof b, "(%a)", v);
+      return b;
+    }
+    case DT_I32:
+      if (k.iv == INT32_MIN) return "(-2147483647 - 1)";
+      snprintf(b, sizeof b, "(%" PRId64 ")", k.iv);
+      return b;
+    case DT_I64:
+      if (k.iv == INT64_MIN) return "(-9223372036854775807LL - 1LL)";
+      snprintf(b, sizeof b, "(%" PRId64 "LL)", k.iv);
+      return b;
+    case DT_BOOL: return k.iv ? "true" : "false";
+  }
+  return "0";
+}
+
+// The reference's emitted spellings (lib/backend_cuda/emit.ml:58-159): integer
+// add/sub/mul/neg wrap through the unsigned type, shift counts are masked and
+// Shr is logical, float math keeps its single-precision name for F32.
+static std::string bin_text(Dt dt, int op, const std::string& a, const std::string& b) {
+  const bool i32 = dt == DT_I32, i64 = dt == DT_I64;
+  const char* u = i32 ? "unsigned int" : "unsigned long long";
+  const char* s = i32 ? "int" : "long long";
+  auto wrapping = [&](const char* sym) {
+    if (i32 || i64) return std::string("((") + s + ")((" + u + ")(" + a + ") " + sym + " (" + u + ")(" + b + ")))";
+    return "(" + a + " " + sym + " " + b + ")";
+  };
+  switch (op) {
+    case B_ADD: return wrapping("+");
+    case B_SUB: return wrapping("-");
+    case B_MUL: return wrapping("*");
+    case B_DIV: return "(" + a + " / " + b + ")";
+    case B_MIN:
+      if (dt == DT_F32) return "fminf(" + a + ", " + b + ")";
+      if (dt == DT_F64) return "fmin(" + a + ", " + b + ")";
+      return "((" + a + " < " + b + ") ? " + a + " : " + b + ")";
+    case B_MAX:
+      if (dt == DT_F32) return "fmaxf(" + a + ", " + b + ")";
+      if (dt == DT_F64) return "fmax(" + a + ", " + b + ")";
+      return "((" + a + " > " + b + ") ? " + a + " : " + b + ")";
+    case B_AND: return "(" + a + " & " + b + ")";
+    case B_OR: return "(" + a + " | " + b + ")";
+    case B_XOR: return "(" + a + " ^ " + b + ")";
+    case B_SHL:
+    case B_SHR: {
+      const char* sym = op == B_SHL ? "<<" : ">>";
+      const char* mask = i32 ? "31" : "63";
+      return std::string("((") + s + ")((" + u + ")(" + a + ") " + sym + " ((" + b + ") & " + mask + ")))";
+    }
+  }
+  return "0";
+}
+
+static std::string neg_text(Dt dt, const std::string& a) {
+  if (dt == DT_I32) return "((int)(0u - (unsigned int)(" + a + ")))";
+  if (dt == DT_I64) return "((long long)(0ull - (unsigned long long)(" + a + ")))";
+  return "(-(" + a + "))";
+}
+
+static std::string un_text(Dt dt, int op, const std::string& a) {
+  const bool f32 = dt == DT_F32;
+  auto m = [&](const char* f, const char* d) { return std::string(f32 ? f : d) + "(" + a + ")"; };
+  switch (op) {
+    case U_NEG: return neg_text(dt, a);
+    case U_SQRT: return m("sqrtf", "sqrt");
+    case U_EXP: return m("expf", "exp");
+    case U_LOG: return m("logf", "log");
+    case U_ABS:
+      if (is_float(dt)) return m("fabsf", "fabs");
+      return "((" + a + " < 0) ? " + neg_text(dt, a) + " : " + a + ")";
+    case U_SIN: return m("sinf", "sin");
+    case U_COS: return m("cosf", "cos");
+    case U_ERF: return m("erff", "erf");
+    case U_ERFINV: return m("erfinvf", "erfinv");
+  }
+  return "0";
+}
+
+// Casts follow the interpreter (cudacaml_backend_interp.ml:198-237): floats
+// go to integers through int64 truncation, 64-bit integers reach F32 through
+// double, integers narrow by wrapping, booleans are 0/1.
+static std::string cast_text(Dt from, Dt to, const std::string& a) {
+  if (from == to) return a;
+  if (to == DT_BOOL) return "((" + a + ") != 0)";
+  if (from == DT_BOOL) {
+    if (to == DT_F32) return "((" + a + ") ? 1.0f : 0.0f)";
+    if (to == DT_F64) return "((" + a + ") ? 1.0 : 0.0)";
+    return std::string("((") + a + ") ? (" + dt_ctype(to) + ")1 : (" + dt_ctype(to) + ")0)";
+  }
+  if (is_float(from)) {
+    if (to == DT_F32) return "((float)(" + a + "))";
+    if (to == DT_F64) return "((double)(" + a + "))";
+    if (to == DT_I64) return "((long long)(" + a + "))";
+    return "((int)(unsigned int)(unsigned long long)(long long)(" + a + "))";
+  }
+  // integer source
+  if (to == DT_F32) return from == DT_I64 ? "((float)(double)(" + a + "))" : "((float)(" + a + "))";
+  if (to == DT_F64) return "((double)(" + a + "))";
+  if (to == DT_I32) return "((int)(unsigned int)(unsigned long long)(" + a + "))";
+  return "((long long)(" + a + "))";
+}
+
+static const char* cmp_sym(int op) {
+  static const char* s[] = {"==", "!=", "<", "<=", ">", ">="};
+  return s[op];
+}
+
+// ===================================================================== emitter
+struct Emitter {
+  const KCtx& c;
+  std::ostringstream& o;
+  std::string ind = "    ";
+  std::string index_text = "i";
+  std::string suffix;
+  std::unordered_map<int, std::string> name;
+  std::unordered_map<int, std::string> direct;  // buffer -> lane expression
+  std::vector<std::string> redval;               // REDVAL slot -> name
+  std::string arg_names[2] = {"a", "b"};
+
+  Emitter(const KCtx& cc, std::ostringstream& oo) : c(cc), o(oo) {}
+
+  std::string val(int id) {
+    auto it = name.find(id);
+    if (it != name.end()) return it->second;
+    const KN& k = c.n[id];
+    std::string e;
+    switch (k.op) {
+      case K_CONST: return lit(k);
+      case K_INDEX: return index_text;
+      case K_ARG: return arg_names[k.iv];
+      case K_REDVAL: return redval.at(k.iv);
+      case K_LOAD: {
+        auto d = direct.find(k.buf);
+        if (d != direct.end() && k.a == c.index_node) {
+          e = d->second;
+        } else {
+          e = "p.b" + std::to_string(k.buf) + "[" + val(k.a) + "]";
+        }
+        break;
+      }
+      case K_CHECK:
+        e = "ccb::checked_index(" + val(k.a) + ", " + std::to_string(k.iv) + "LL, p.err, ccb::ERR_GATHER_OOB)";
+        break;
+      case K_BIN: e = bin_text(k.dt, k.sub, val(k.a), val(k.b)); break;
+      case K_UN: e = un_text(k.dt, k.sub, val(k.a)); break;
+      case K_CMP: e = "(" + val(k.a) + " " + cmp_sym(k.sub) + " " + val(k.b) + ")"; break;
+      case K_LOGIC: e = "(" + val(k.a) + (k.sub == 0 ? " && " : " || ") + val(k.b) + ")"; break;
+      case K_NOT: e = "(!" + val(k.a) + ")"; break;
+      case K_SELECT: e = "(" + val(k.a) + " ? " + val(k.b) + " : " + val(k.c) + ")"; break;
+      case K_CAST: e = cast_text(c.n[k.a].dt, k.dt, val(k.a)); break;
+    }
+    std::string nm = "v" + std::to_string(id) + suffix;
+    o << ind << "const " << dt_ctype(k.dt) << " " << nm << " = " << e << ";\n";
+    name[id] = nm;
+    return nm;
+  }
+};
+
+// ===================================================================== lowering
+namespace {
+
+enum GKind { G_MAPRED, G_SCAN_FLAT, G_SCAN_ROWS, G_RED_ROWS, G_SCATTER, G_MATMUL };
+
+struct Red {
+  int t = -1;           // output tensor
+  int64_t elem = 0;     // element of t this accumulator produces
+  Dt dt = DT_F32;
+  int comb_t = -1;      // tensor whose fn2 is the combiner (-1: plain add)
+  int init = -1;        // KNode in the group's ctx (constant)
+  int var = -1;         // accumulated element value
+  int inv = -1;         // invariant factor applied after the pass (-1: none)
+};
+
+struct Group {
+  int kind = G_MAPRED;
+  int64_t domain = 0;
+  KCtx ctx;
+  std::vector<std::pair<int, int>> stores;  // (tensor, value KNode)
+  std::vector<Red> reds;
+  std::vector<std::pair<int, int>> tails;   // (tensor, value KNode)
+  int root = -1;
+  int val = -1, val2 = -1;  // single-root kinds: source / index KNodes
+  int64_t rows = 0, n = 0;  // rows kernels
+  int mm_a = -1, mm_b = -1; // matmul operand KNodes (built with INDEX = flat operand index)
+  KCtx ctx_b;               // matmul: B operand
+};
+
+struct JoinFail {};
+
+class Lowerer {
+ public:
+  const GGraph& g;
+  std::vector<int> uses;
+  std::vector<char> is_out, mat;
+  std::vector<int> group_of;
+  std::vector<Group> groups;
+
+  explicit Lowerer(const GGraph& gg) : g(gg) {}
+
+  void analyse() {
+    const int T = (int)g.ts.size();
+    uses.assign(T, 0);
+    is_out.assign(T, 0);
+    mat.assign(T, 0);
+    group_of.assign(T, -1);
+    for (const auto& t : g.ts) {
+      if (t.dep0 >= 0) uses[t.dep0]++;
+      if (t.dep1 >= 0) uses[t.dep1]++;
+    }
+    for (auto& o : g.outputs) is_out[o.second] = 1;
+    for (int t = 0; t < T; ++t) {
+      const GTensor& x = g.ts[t];
+      const bool barrier = x.kind == T_REDUCE || x.kind == T_SCAN || x.kind == T_SCATTER || x.kind == T_MATMUL;
+      mat[t] = x.kind == T_PARAM || barrier || is_out[t];
+      if (mat[t] && x.dt == DT_BOOL) bad("Value.create: Bool tensors are not storable (node n" + std::to_string(x.uid) + ")");
+    }
+  }
+
+  // ------------------------------------------------------------ element builder
+  struct Build {
+    Lowerer* L;
+    int gi;
+    KCtx* ctx;
+    Group* grp;
+    std::map<std::pair<int, int>, int> memo;
+
+    int elem(int t, int idx) {
+      auto key = std::make_pair(t, idx);
+      auto it = memo.find(key);
+      if (it != memo.end()) return it->second;
+      int r = elem_uncached(t, idx);
+      memo[key] = r;
+      return r;
+    }
+
+    int elem_uncached(int t, int idx) {
+      const GTensor& x = L->g.ts[t];
+      if (L->mat[t]) {
+        const int gt = L->group_of[t];
+        if (x.kind == T_PARAM || (gt >= 0 && gt < gi)) return ctx->load(x.dt, t, idx);
+        if (gt == gi && gt >= 0) {
+          if (x.kind == T_REDUCE || x.kind == T_MATMUL) {
+            // A reduction of this very pass: its value exists only after the
+            // final fold, so it may appear only in invariant position.
+            const KN& ik = ctx->n[idx];
+            if (!(ik.ranged && ik.lo == ik.hi)) throw JoinFail();
+            for (size_t r = 0; r < grp->reds.size(); ++r)
+              if (grp->reds[r].t == t && grp->reds[r].elem == ik.lo) {
+                KN k;
+                k.op = K_REDVAL;
+                k.dt = x.dt;
+                k.iv = (int64_t)r;
+                return ctx->mk(k);
+              }
+            throw JoinFail();
+          }
+          if (x.kind == T_SCAN || x.kind == T_SCATTER) throw JoinFail();
+          // element-wise member of this pass: recompute inline
+        } else if (x.kind != T_PARAM) {
+          throw JoinFail();  // produced by a later kernel
+        }
+      }
+      return inline_node(t, idx);
+    }
+
+    int inline_node(int t, int idx) {
+      const GTensor& x = L->g.ts[t];
+      switch (x.kind) {
+        case T_IOTA: return idx;
+        case T_MAP: {
+          int env[2] = {elem(x.dep0, idx), -1};
+          return expr(x.body, env, idx);
+        }
+        case T_MAP2: {
+          int env[2] = {elem(x.dep0, idx), elem(x.dep1, idx)};
+          return expr(x.body, env, idx);
+        }
+        case T_GATHER: {
+          const int j = elem(x.dep0, idx);
+          KN k;
+          k.op = K_CHECK;
+          k.dt = DT_I32;
+          k.a = j;
+          k.iv = L->g.ts[x.dep1].numel;
+          int jc = ctx->mk(k);
+          if (ctx->n[jc].op == K_CHECK && ctx->n[jc].ranged) jc = j;  // provably in bounds
+          return elem(x.dep1, jc);
+        }
+        case T_RESHAPE: return elem(x.dep0, idx);
+        case T_BROADCAST: return elem(x.dep0, ctx->cint(DT_I32, 0));
+        default: throw LowerError(CCB_ERR_INVALID, "lower: node n" + std::to_string(x.uid) + " must be materialised");
+      }
+    }
+
+    // Instantiate an element function body with its arguments bound.
+    int expr(int e, const int env[2], int idx) {
+      std::unordered_map<int, int> m;
+      std::function<int(int)> go = [&](int id) -> int {
+        auto it = m.find(id);
+        if (it != m.end()) return it->second;
+        const GExpr& x = L->g.ex[id];
+        int r = -1;
+        switch (x.kind) {
+          case E_CONST:
+            r = is_float(x.dt) ? ctx->cfloat(x.dt, x.f) : ctx->cint(x.dt, x.i);
+            break;
+          case E_ARG:
+            if (x.i < 0 || x.i > 1 || env[x.i] < 0) bad("lower: unbound Arg " + std::to_string(x.i));
+            if (ctx->n[env[x.i]].dt != x.dt) bad("lower: Arg dtype mismatch");
+            r = env[x.i];
+            break;
+          case E_INDEX: r = idx; break;
+          case E_BINOP: {
+            if (is_float(x.dt) && x.op >= B_AND) bad(std::string("Emit: ") + kBin[x.op] + " on a float dtype");
+            if (x.dt == DT_BOOL) bad("Emit: arithmetic on bool");
+            const int a = go(x.a), b = go(x.b);
+            r = ctx->bin(x.dt, x.op, a, b);
+            break;
+          }
+          case E_UNOP: {
+            if (!is_float(x.dt) && x.op != U_NEG && x.op != U_ABS) bad(std::string("Emit: ") + kUn[x.op] + " on a non-float dtype");
+            r = ctx->un(x.dt, x.op, go(x.a));
+            break;
+          }
+          case E_CMP: {
+            KN k;
+            k.op = K_CMP;
+            k.dt = DT_BOOL;
+            k.sub = x.op;
+            k.a = go(x.a);
+            k.b = go(x.b);
+            r = ctx->mk(k);
+            break;
+          }
+          case E_LOGIC: {
+            KN k;
+            k.op = K_LOGIC;
+            k.dt = DT_BOOL;
+            k.sub = x.op;
+            k.a = go(x.a);
+            k.b = go(x.b);
+            r = ctx->mk(k);
+            break;
+          }
+          case E_NOT: {
+            KN k;
+            k.op = K_NOT;
+            k.dt = DT_BOOL;
+            k.a = go(x.a);
+            r = ctx->mk(k);
+            break;
+          }
+          case E_SELECT: {
+            KN k;
+            k.op = K_SELECT;
+            k.dt = x.dt;
+            k.a = go(x.a);
+            k.b = go(x.b);
+            k.c = go(x.c);
+            r = ctx->mk(k);
+            break;
+          }
+          case E_CAST: {
+            const int a = go(x.a);
+            if (ctx->n[a].dt == x.dt) {
+              r = a;
+            } else {
+              KN k;
+              k.op = K_CAST;
+              k.dt = x.dt;
+              k.a = a;
+              r = ctx->mk(k);
+            }
+            break;
+          }
+        }
+        m[id] = r;
+        return r;
+      };
+      return go(e);
+    }
+  };
+
+  // ------------------------------------------------------------ factoring
+  // e == inv * var where inv holds every part of e that depends on this
+  // pass's reductions (and is loop-invariant) and var holds the rest; -1
+  // stands for one. Only the late part is pulled out, so constants and other
+  // invariants that are available during the pass stay in var.
+  std::pair<int, int> factor(KCtx& c, int e) {
+    const KN k = c.n[e];
+    if (!k.late) return {-1, e};
+    if (!k.variant) return {e, -1};
+    auto or_one = [&](int v) { return v < 0 ? c.one(k.dt) : v; };
+    if (k.op == K_BIN && is_float(k.dt)) {
+      if (k.sub == B_MUL) {
+        auto fa = factor(c, k.a), fb = factor(c, k.b);
+        return {mul_opt(c, k.dt, fa.first, fb.first), mul_opt(c, k.dt, fa.second, fb.second)};
+      }
+      if (k.sub == B_DIV && !c.n[k.b].variant) {
+        auto fa = factor(c, k.a);
+        if (c.n[k.b].late) return {c.bin(k.dt, B_DIV, or_one(fa.first), k.b), fa.second};
+        return {fa.first, c.bin(k.dt, B_DIV, or_one(fa.second), k.b)};
+      }
+      if (k.sub == B_ADD || k.sub == B_SUB) {
+        auto fa = factor(c, k.a), fb = factor(c, k.b);
+        if (fa.first == fb.first && fa.first >= 0) return {fa.first, c.bin(k.dt, k.sub, or_one(fa.second), or_one(fb.second))};
+        return {-1, e};
+      }
+    }
+    if (k.op == K_UN && k.sub == U_NEG && is_float(k.dt)) {
+      auto fa = factor(c, k.a);
+      return {fa.first, c.un(k.dt, U_NEG, or_one(fa.second))};
+    }
+    if (k.op == K_SELECT && !c.n[k.a].late) {
+      auto fa = factor(c, k.b), fb = factor(c, k.c);
+      if (fa.first == fb.first && fa.first >= 0) {
+        KN s;
+        s.op = K_SELECT;
+        s.dt = k.dt;
+        s.a = k.a;
+        s.b = or_one(fa.second);
+        s.c = or_one(fb.second);
+        return {fa.first, c.mk(s)};
+      }
+    }
+    return {-1, e};
+  }
+
+  static void dump(const KCtx& c, int id, int depth) {
+    if (depth > 14 || id < 0) return;
+    const KN& k = c.n[id];
+    fprintf(stderr, "%*s#%d op=%d sub=%d dt=%d late=%d var=%d buf=%d iv=%lld f=%g\n", depth * 2, "", id, k.op, k.sub, (int)k.dt,
+            (int)k.late, (int)k.variant, k.buf, (long long)k.iv, k.f);
+    if (!k.late) return;
+    dump(c, k.a, depth + 1);
+    dump(c, k.b, depth + 1);
+    dump(c, k.c, depth + 1);
+  }
+
+  static int mul_opt(KCtx& c, Dt dt, int x, int y) {
+    if (x < 0) return y;
+    if (y < 0) return x;
+    return c.bin(dt, B_MUL, x, y);
+  }
+
+  // Is fn2 of tensor t exactly `add (arg0) (arg1)`? (lib/ad/grad.ml:158-166)
+  bool is_plain_add(int t) const {
+    const GTensor& x = g.ts[t];
+    const GExpr& b = g.ex[x.body];
+    if (b.kind != E_BINOP || b.op != B_ADD) return false;
+    const GExpr& ea = g.ex[b.a];
+    const GExpr& eb = g.ex[b.b];
+    return ea.kind == E_ARG && eb.kind == E_ARG && ea.i != eb.i;
+  }
+  bool init_is_zero(int t) const {
+    const GExpr& e = g.ex[g.ts[t].init];
+    if (e.kind != E_CONST) return false;
+    return is_float(e.dt) ? (e.f == 0.0 && !std::signbit(e.f)) : e.i == 0;
+  }
+
+  // ------------------------------------------------------------ joining
+  // Try to add root t to MAPRED group gi. On success the group is updated.
+  bool try_join(int gi, int t) {
+    Group trial = groups[gi];  // copy: a failed join leaves no trace
+    Build B{this, gi, &trial.ctx, &trial, {}};
+    const GTensor& x = g.ts[t];
+    try {
+      if (x.kind == T_REDUCE) {
+        const int src = x.dep0;
+        const int v = B.elem(src, trial.ctx.index());
+        Red r;
+        r.t = t;
+        r.elem = 0;
+        r.dt = x.dt;
+        r.comb_t = t;
+        r.init = init_knode(trial.ctx, t);
+        if (!trial.ctx.n[v].late) {
+          r.var = v;
+        } else {
+          if (!is_float(x.dt) || !is_plain_add(t) || !init_is_zero(t)) throw JoinFail();
+          auto f = factor(trial.ctx, v);
+          if (std::getenv("CCB_DEBUG_LOWER")) {
+            fprintf(stderr, "factor n%lld: inv=%d var=%d\n", (long long)x.uid, f.first, f.second);
+            dump(trial.ctx, v, 0);
+          }
+          if (f.first < 0 || (f.second >= 0 && trial.ctx.n[f.second].late)) throw JoinFail();
+          r.inv = f.first;
+          r.var = f.second < 0 ? trial.ctx.one(x.dt) : f.second;
+        }
+        if (!trial.reds.empty() && trial.reds[0].dt != x.dt) throw JoinFail();
+        trial.reds.push_back(r);
+      } else if (x.kind == T_MATMUL) {
+        // skinny product: one additive accumulator per output cell, INDEX = k
+        const GTensor& A = g.ts[x.dep0];
+        const int64_t M = x.shape[0], N = x.shape[1], K = A.shape[1];
+        if (!trial.reds.empty() && trial.reds[0].dt != x.dt) throw JoinFail();
+        const int k = trial.ctx.index();
+        for (int64_t i = 0; i < M; ++i)
+          for (int64_t j = 0; j < N; ++j) {
+            const int ia = trial.ctx.bin(DT_I32, B_ADD, trial.ctx.cint(DT_I32, i * K), k);
+            const int ib = trial.ctx.bin(DT_I32, B_ADD, trial.ctx.bin(DT_I32, B_MUL, k, trial.ctx.cint(DT_I32, N)),
+                                         trial.ctx.cint(DT_I32, j));
+            const int av = B.elem(x.dep0, ia), bv = B.elem(x.dep1, ib);
+            const int prod = trial.ctx.bin(x.dt, B_MUL, av, bv);
+            if (trial.ctx.n[prod].late) throw JoinFail();
+            Red r;
+            r.t = t;
+            r.elem = i * N + j;
+            r.dt = x.dt;
+            r.comb_t = -1;
+            r.init = is_float(x.dt) ? trial.ctx.cfloat(x.dt, 0.0) : trial.ctx.cint(x.dt, 0);
+            r.var = prod;
+            trial.reds.push_back(r);
+          }
+      } else if (x.numel == 1 && !(trial.domain == 1 && trial.reds.empty())) {
+        // scalar tail, evaluated in the epilogue
+        const int v = B.inline_node(t, trial.ctx.cint(DT_I32, 0));
+        trial.tails.push_back({t, v});
+      } else {
+        if (x.numel != trial.domain) throw JoinFail();
+        const int v = B.inline_node(t, trial.ctx.index());
+        if (trial.ctx.n[v].late) throw JoinFail();
+        trial.stores.push_back({t, v});
+      }
+    } catch (const JoinFail&) {
+      if (std::getenv("CCB_DEBUG_LOWER")) fprintf(stderr, "ccb lower: n%lld cannot join pass %d\n", (long long)x.uid, gi);
+      return false;
+    }
+    if (trial.reds.size() > 64) return false;
+    groups[gi] = std::move(trial);
+    group_of[t] = gi;
+    return true;
+  }
+
+  int init_knode(KCtx& c, int t) {
+    // The identity, evaluated at index 0 as both backends do.
+    Build B{this, -1, &c, nullptr, {}};
+    int env[2] = {-1, -1};
+    return B.expr(g.ts[t].init, env, c.cint(DT_I32, 0));
+  }
+
+  int new_group(int kind, int64_t domain) {
+    Group gr;
+    gr.kind = kind;
+    gr.domain = domain;
+    gr.ctx.ilo = 0;
+    gr.ctx.ihi = domain > 0 ? domain - 1 : 0;
+    groups.push_back(std::move(gr));
+    return (int)groups.size() - 1;
+  }
+
+  void build_single(int gi, int t) {
+    Group& gr = groups[gi];
+    group_of[t] = gi;
+    gr.root = t;
+    const GTensor& x = g.ts[t];
+    Build B{this, gi, &gr.ctx, &gr, {}};
+    try {
+      switch (gr.kind) {
+        case G_SCAN_FLAT:
+        case G_SCAN_ROWS:
+        case G_RED_ROWS:
+          gr.val = B.elem(x.dep0, gr.ctx.index());
+          break;
+        case G_SCATTER:
+          gr.val = B.elem(x.dep0, gr.ctx.index());   // index
+          gr.val2 = B.elem(x.dep1, gr.ctx.index());  // source
+          break;
+        case G_MATMUL: {
+          gr.ctx.ihi = std::max<int64_t>(0, g.ts[x.dep0].numel - 1);
+          gr.ctx_b.ihi = std::max<int64_t>(0, g.ts[x.dep1].numel - 1);
+          gr.mm_a = B.elem(x.dep0, gr.ctx.index());
+          Build Bb{this, gi, &gr.ctx_b, &gr, {}};
+          gr.mm_b = Bb.elem(x.dep1, gr.ctx_b.index());
+          break;
+        }
+      }
+    } catch (const JoinFail&) {
+      throw LowerError(CCB_ERR_INVALID, "lower: internal: unsatisfied dependency");
+    }
+    if (gr.ctx.n[gr.val < 0 ? 0 : gr.val].late) bad("lower: internal: late value in a single kernel");
+  }
+
+  void group_all() {
+    int cur = -1;  // most recent map-reduce group
+    for (int t = 0; t < (int)g.ts.size(); ++t) {
+      if (!mat[t] || g.ts[t].kind == T_PARAM) continue;
+      const GTensor& x = g.ts[t];
+      switch (x.kind) {
+        case T_IOTA:
+        case T_MAP:
+        case T_MAP2:
+        case T_GATHER:
+        case T_RESHAPE:
+        case T_BROADCAST: {
+          if (cur >= 0 && try_join(cur, t)) break;
+          cur = new_group(G_MAPRED, x.numel == 1 ? 1 : x.numel);
+          if (!try_join(cur, t)) bad("lower: internal: cannot start a pass");
+          break;
+        }
+        case T_REDUCE: {
+          const GTensor& src = g.ts[x.dep0];
+          const int64_t n = src.shape.empty() ? 1 : src.shape.back();
+          const int64_t rows = x.numel;
+          if (rows == 1) {
+            if (cur >= 0 && groups[cur].domain == n && try_join(cur, t)) break;
+            cur = new_group(G_MAPRED, n);
+            if (!try_join(cur, t)) bad("lower: internal: cannot start a reduction");
+          } else {
+            const int gi = new_group(G_RED_ROWS, rows * n);
+            groups[gi].rows = rows;
+            groups[gi].n = n;
+            build_single(gi, t);
+          }
+          break;
+        }
+        case T_SCAN: {
+          const GTensor& src = g.ts[x.dep0];
+          const int64_t n = src.shape.empty() ? 1 : src.shape.back();
+          const int64_t rows = n == 0 ? 0 : src.numel / n;
+          const int gi = new_group(rows <= 1 ? G_SCAN_FLAT : G_SCAN_ROWS, src.numel);
+          groups[gi].rows = rows;
+          groups[gi].n = n;
+          build_single(gi, t);
+          break;
+        }
+        case T_SCATTER: {
+          const int gi = new_group(G_SCATTER, g.ts[x.dep0].numel);
+          build_single(gi, t);
+          break;
+        }
+        case T_MATMUL: {
+          const int64_t M = x.shape[0], N = x.shape[1], K = g.ts[x.dep0].shape[1];
+          if (M * N <= 32 && K >= 2048) {
+            if (cur >= 0 && groups[cur].domain == K && try_join(cur, t)) break;
+            cur = new_group(G_MAPRED, K);
+            if (!try_join(cur, t)) bad("lower: internal: cannot start a split-K product");
+          } else {
+            const int gi = new_group(G_MATMUL, M * N);
+            groups[gi].rows = M;
+            groups[gi].n = N;
+            build_single(gi, t);
+          }
+          break;
+        }
+        default: bad("lower: unexpected node kind");
+      }
+    }
+  }
+
+  // ------------------------------------------------------------ code generation
+  Lowered* out = nullptr;
+  std::ostringstream src;
+  std::vector<int> node_buf;  // tensor -> buffer index
+
+  int add_buf(const std::string& label, int elem_bytes, int64_t numel, int role, int node, bool zero) {
+    BufSpec b;
+    b.label = label;
+    b.elem_bytes = elem_bytes;
+    b.numel = numel;
+    b.role = role;
+    b.node = node;
+    b.zero = zero;
+    out->bufs.push_back(b);
+    return (int)out->bufs.size() - 1;
+  }
+
+  // Fields of P: loaded buffers (const), written buffers, then extras.
+  struct Field {
+    std::string decl;
+    Slot slot;
+  };
+
+  static std::set<int> loads_of(const KCtx& c) {
+    std::set<int> s;
+    for (const KN& k : c.n)
+      if (k.op == K_LOAD) s.insert(k.buf);
+    return s;
+  }
+
+  void emit_struct(const std::vector<Field>& f) {
+    src << "  struct P {\n";
+    for (auto& x : f) src << "    " << x.decl << ";\n";
+    src << "  };\n";
+  }
+
+  Field in_field(int t) {
+    Field f;
+    f.decl = std::string("const ") + dt_ctype(g.ts[t].dt) + "* __restrict__ b" + std::to_string(t);
+    f.slot.kind = SL_BUF;
+    f.slot.buf = node_buf[t];
+    return f;
+  }
+  Field out_field(int t) {
+    Field f;
+    f.decl = std::string(dt_ctype(g.ts[t].dt)) + "* __restrict__ o" + std::to_string(t);
+    f.slot.kind = SL_BUF;
+    f.slot.buf = node_buf[t];
+    return f;
+  }
+  static Field buf_field(const std::string& decl, int buf) {
+    Field f;
+    f.decl = decl;
+    f.slot.kind = SL_BUF;
+    f.slot.buf = buf;
+    return f;
+  }
+  static Field i64_field(const std::string& nm, int64_t v) {
+    Field f;
+    f.decl = "long long " + nm;
+    f.slot.kind = SL_I64;
+    f.slot.val = v;
+    return f;
+  }
+
+  LaunchSpec& add_launch(const std::string& fn, const std::vector<Field>& fields) {
+    LaunchSpec l;
+    l.fn = fn;
+    for (auto& f : fields) l.slots.push_back(f.slot);
+    out->launches.push_back(l);
+    OpSpec op;
+    op.kind = OP_LAUNCH;
+    op.launch = (int)out->launches.size() - 1;
+    out->ops.push_back(op);
+    out->num_kernels++;
+    return out->launches.back();
+  }
+
+  // Direct loads: LOAD(buf, INDEX) of 4- or 8-byte elements in the cone of roots.
+  std::vector<int> direct_loads(const KCtx& c, const std::vector<int>& roots) {
+    std::vector<char> seen(c.n.size(), 0);
+    std::set<int> bufs;
+    std::function<void(int)> walk = [&](int id) {
+      if (id < 0 || seen[id]) return;
+      seen[id] = 1;
+      const KN& k = c.n[id];
+      if (k.op == K_LOAD && k.a == c.index_node && k.dt != DT_BOOL) bufs.insert(k.buf);
+      walk(k.a);
+      walk(k.b);
+      walk(k.c);
+    };
+    for (int r : roots) walk(r);
+    return std::vector<int>(bufs.begin(), bufs.end());
+  }
+
+  void emit_mapred(int gi) {
+    Group& gr = groups[gi];
+    const std::string F = "F" + std::to_string(gi);
+    const std::string fn = "ccb_mapreduce_" + std::to_string(gi);
+    const int R = (int)gr.reds.size();
+    const Dt acc = R ? gr.reds[0].dt : DT_F32;
+    const char* at = dt_ctype(acc);
+    // buffers for every output of the pass
+    for (auto& s : gr.stores) node_buf[s.first] = add_buf("t" + std::to_string(g.ts[s.first].uid), dt_size(g.ts[s.first].dt), g.ts[s.first].numel, BR_NODE, s.first, false);
+    std::set<int> red_t;
+    for (auto& r : gr.reds)
+      if (!red_t.count(r.t)) {
+        red_t.insert(r.t);
+        node_buf[r.t] = add_buf("t" + std::to_string(g.ts[r.t].uid), dt_size(g.ts[r.t].dt), g.ts[r.t].numel, BR_NODE, r.t, false);
+      }
+    for (auto& s : gr.tails) node_buf[s.first] = add_buf("t" + std::to_string(g.ts[s.first].uid), dt_size(g.ts[s.first].dt), 1, BR_NODE, s.first, false);
+    const int max_grid = 4096;
+    int partials = -1, ticket = -1;
+    if (R) {
+      partials = add_buf("g" + std::to_string(gi) + "_partials", dt_size(acc), (int64_t)max_grid * R, BR_SCRATCH, -1, false);
+      ticket = add_buf("g" + std::to_string(gi) + "_ticket", 4, 1, BR_SCRATCH, -1, true);
+    }
+    std::vector<Field> fields;
+    for (int b : loads_of(gr.ctx)) fields.push_back(in_field(b));
+    for (auto& s : gr.stores) fields.push_back(out_field(s.first));
+    for (int t : red_t) fields.push_back(out_field(t));
+    for (auto& s : gr.tails) fields.push_back(out_field(s.first));
+    fields.push_back(buf_field(std::string(at) + "* partials", partials));
+    fields.push_back(buf_field("unsigned* ticket", ticket));
+    fields.push_back(buf_field("unsigned* err", out->err_buf));
+    fields.push_back(i64_field("n", gr.domain));
+
+    src << "// pass " << gi << ": " << gr.stores.size() << " element stores, " << R << " reductions, " << gr.tails.size()
+        << " scalar tails over " << gr.domain << " elements\n";
+    src << "struct " << F << " {\n";
+    emit_struct(fields);
+    src << "  typedef " << at << " acc_t;\n";
+    src << "  static constexpr int NRED = " << R << ";\n  static constexpr int VEC = 1;\n";
+    src << "  static constexpr bool TAIL = " << (gr.tails.empty() ? "false" : "true") << ";\n";
+    // identity / combine
+    src << "  static __device__ __forceinline__ acc_t identity(int r) {\n    switch (r) {\n";
+    for (int r = 0; r < R; ++r) {
+      std::ostringstream tmp;
+      Emitter e(gr.ctx, tmp);
+      std::string v = e.val(gr.reds[r].init);
+      src << "      case " << r << ": {\n" << tmp.str() << "        return " << v << "; }\n";
+    }
+    src << "    }\n    return acc_t(0);\n  }\n";
+    src << "  static __device__ __forceinline__ void init(acc_t* acc) {\n";
+    for (int r = 0; r < R; ++r) src << "    acc[" << r << "] = identity(" << r << ");\n";
+    src << "  }\n";
+    src << "  static __device__ __forceinline__ acc_t combine(int r, acc_t a, acc_t b) {\n    switch (r) {\n";
+    for (int r = 0; r < R; ++r) {
+      src << "      case " << r << ": {\n";
+      if (gr.reds[r].comb_t < 0 || is_plain_add(gr.reds[r].comb_t)) {
+        src << "        return " << bin_text(acc, B_ADD, "a", "b") << "; }\n";
+      } else {
+        src << combine_body(gr.reds[r].comb_t, "        ");
+      }
+    }
+    src << "    }\n    return a;\n  }\n";
+    // vec_ok
+    std::vector<int> roots;
+    for (auto& s : gr.stores) roots.push_back(s.second);
+    for (auto& r : gr.reds) roots.push_back(r.var);
+    std::vector<int> direct = direct_loads(gr.ctx, roots);
+    src << "  static __device__ __forceinline__ bool vec_ok(const P& p) {\n    return true";
+    for (int b : direct) src << " && ccb::aligned16(p.b" << b << ")";
+    for (auto& s : gr.stores) src << " && ccb::aligned16(p.o" << s.first << ")";
+    src << ";\n  }\n";
+    // elem
+    src << "  static __device__ __forceinline__ void elem(const P& p, int i, acc_t* acc) {\n";
+    {
+      Emitter e(gr.ctx, src);
+      for (auto& s : gr.stores) {
+        std::string v = e.val(s.second);
+        src << "    p.o" << s.first << "[i] = " << v << ";\n";
+      }
+      for (int r = 0; r < R; ++r) {
+        std::string v = e.val(gr.reds[r].var);
+        src << "    acc[" << r << "] = combine(" << r << ", acc[" << r << "], " << v << ");\n";
+      }
+      (void)acc;
+    }
+    src << "  }\n";
+    // elem4
+    src << "  static __device__ __forceinline__ void elem4(const P& p, int i, acc_t* acc) {\n";
+    for (int b : direct) src << "    const ccb::V4<" << dt_ctype(g.ts[b].dt) << "> L" << b << " = ccb::ld4(p.b" << b << " + i);\n";
+    for (auto& s : gr.stores) src << "    ccb::V4<" << dt_ctype(g.ts[s.first].dt) << "> S" << s.first << ";\n";
+    for (int j = 0; j < 4; ++j) {
+      Emitter e(gr.ctx, src);
+      e.suffix = "_" + std::to_string(j);
+      e.index_text = j == 0 ? "i" : "(i + " + std::to_string(j) + ")";
+      for (int b : direct) e.direct[b] = "L" + std::to_string(b) + ".v[" + std::to_string(j) + "]";
+      for (auto& s : gr.stores) {
+        std::string v = e.val(s.second);
+        src << "    S" << s.first << ".v[" << j << "] = " << v << ";\n";
+      }
+      for (int r = 0; r < R; ++r) {
+        std::string v = e.val(gr.reds[r].var);
+        src << "    acc[" << r << "] = combine(" << r << ", acc[" << r << "], " << v << ");\n";
+      }
+    }
+    for (auto& s : gr.stores) src << "    ccb::st4(p.o" << s.first << " + i, S" << s.first << ");\n";
+    src << "  }\n";
+    // epilogue
+    src << "  static __device__ __forceinline__ void epilogue(const P& p, const acc_t* res) {\n";
+    {
+      Emitter e(gr.ctx, src);
+      e.index_text = "0";
+      for (int r = 0; r < R; ++r) {
+        const Red& rd = gr.reds[r];
+        std::string fv = "f" + std::to_string(r);
+        if (rd.inv >= 0) {
+          std::string iv = e.val(rd.inv);
+          src << "    const acc_t " << fv << " = " << bin_text(acc, B_MUL, iv, "res[" + std::to_string(r) + "]") << ";\n";
+        } else {
+          src << "    const acc_t " << fv << " = res[" << r << "];\n";
+        }
+        e.redval.push_back(fv);
+        src << "    p.o" << rd.t << "[" << rd.elem << "] = " << fv << ";\n";
+      }
+      for (auto& s : gr.tails) {
+        std::string v = e.val(s.second);
+        src << "    p.o" << s.first << "[0] = " << v << ";\n";
+      }
+    }
+    src << "  }\n};\n";
+    src << "extern \"C\" __global__ void __launch_bounds__(256) " << fn << "(const " << F << "::P p) { ccb::map_reduce<" << F
+        << ">(p); }\n\n";
+    LaunchSpec& l = add_launch(fn, fields);
+    l.mode = GM_PERSISTENT;
+    l.work = gr.domain;
+    l.per_block = 256 * 8;
+    l.max_grid = R ? max_grid : (1 << 20);
+    if (R == 0 && gr.stores.empty()) {
+      l.work = 1;  // tails only
+    }
+  }
+
+  std::string combine_body(int t, const std::string& ind) {
+    const GTensor& x = g.ts[t];
+    KCtx c;
+    std::ostringstream tmp;
+    Build B{this, -1, &c, nullptr, {}};
+    KN a;
+    a.op = K_ARG;
+    a.dt = x.dt;
+    a.iv = 0;
+    KN b = a;
+    b.iv = 1;
+    int env[2] = {c.mk(a), c.mk(b)};
+    const int v = B.expr(x.body, env, c.cint(DT_I32, 0));
+    Emitter e(c, tmp);
+    e.ind = ind;
+    std::string r = e.val(v);
+    return tmp.str() + ind + "return " + r + "; }\n";
+  }
+
+  // Functor pieces shared by the scan and rows kernels: load/load4 of the
+  // source element, identity and combine of the root's fn2.
+  void emit_source_access(Group& gr, int t, const std::string& T) {
+    const GTensor& x = g.ts[t];
+    {
+      std::ostringstream tmp;
+      KCtx c;
+      int iv = init_knode(c, t);
+      Emitter e(c, tmp);
+      std::string v = e.val(iv);
+      src << "  static __device__ __forceinline__ T identity() {\n" << tmp.str() << "    return " << v << ";\n  }\n";
+    }
+    src << "  static __device__ __forceinline__ T combine(T a, T b) {\n";
+    if (is_plain_add(t))
+      src << "    return " << bin_text(x.dt, B_ADD, "a", "b") << "; }\n";
+    else
+      src << combine_body(t, "    ");
+    std::vector<int> direct = direct_loads(gr.ctx, {gr.val});
+    src << "  static __device__ __forceinline__ T load(const P& p, long long li) {\n    const int i = (int)li;\n";
+    {
+      Emitter e(gr.ctx, src);
+      std::string v = e.val(gr.val);
+      src << "    return " << v << ";\n  }\n";
+    }
+    src << "  static __device__ __forceinline__ void load4(const P& p, long long li, T* x) {\n    const int i = (int)li;\n";
+    for (int b : direct) src << "    const ccb::V4<" << dt_ctype(g.ts[b].dt) << "> L" << b << " = ccb::ld4(p.b" << b << " + i);\n";
+    for (int j = 0; j < 4; ++j) {
+      Emitter e(gr.ctx, src);
+      e.suffix = "_" + std::to_string(j);
+      e.index_text = j == 0 ? "i" : "(i + " + std::to_string(j) + ")";
+      for (int b : direct) e.direct[b] = "L" + std::to_string(b) + ".v[" + std::to_string(j) + "]";
+      std::string v = e.val(gr.val);
+      src << "    x[" << j << "] = " << v << ";\n";
+    }
+    src << "  }\n";
+    src << "  static __device__ __forceinline__ bool vec_ok(const P& p) {\n    return true";
+    for (int b : direct) src << " && ccb::aligned16(p.b" << b << ")";
+    (void)T;
+  }
+
+  void emit_scan(int gi) {
+    Group& gr = groups[gi];
+    const int t = gr.root;
+    const GTensor& x = g.ts[t];
+    const char* T = dt_ctype(x.dt);
+    const std::string F = "F" + std::to_string(gi);
+    const bool flat = gr.kind == G_SCAN_FLAT;
+    const std::string fn = std::string(flat ? "ccb_scan_" : "ccb_scanrows_") + std::to_string(gi);
+    node_buf[t] = add_buf("t" + std::to_string(x.uid), dt_size(x.dt), x.numel, BR_NODE, t, false);
+    const int items = dt_size(x.dt) == 4 ? 16 : 8;
+    const int64_t tile = 256 * items;
+    const int64_t ntiles = std::max<int64_t>(1, (gr.domain + tile - 1) / tile);
+    std::vector<Field> fields;
+    for (int b : loads_of(gr.ctx)) fields.push_back(in_field(b));
+    fields.push_back(out_field(t));
+    fields.push_back(buf_field("unsigned* err", out->err_buf));
+    fields.push_back(i64_field("n", flat ? gr.domain : gr.n));
+    fields.push_back(i64_field("rows", gr.rows));
+    if (flat) {
+      const std::string pre = "g" + std::to_string(gi);
+      fields.push_back(buf_field("unsigned* tile_counter", add_buf(pre + "_tiles", 4, 1, BR_SCRATCH, -1, true)));
+      fields.push_back(buf_field("unsigned* flags", add_buf(pre + "_flags", 4, ntiles, BR_SCRATCH, -1, true)));
+      fields.push_back(buf_field(std::string(T) + "* aggs", add_buf(pre + "_aggs", dt_size(x.dt), ntiles, BR_SCRATCH, -1, false)));
+      fields.push_back(buf_field(std::string(T) + "* incls", add_buf(pre + "_incls", dt_size(x.dt), ntiles, BR_SCRATCH, -1, false)));
+      Field ep;
+      ep.decl = "unsigned long long epoch";
+      ep.slot.kind = SL_EPOCH;
+      fields.push_back(ep);
+    }
+    src << "// " << (flat ? "flat scan" : "row scan") << " " << gi << " over " << gr.domain << " elements\n";
+    src << "struct " << F << " {\n";
+    emit_struct(fields);
+    src << "  typedef " << T << " T;\n  static constexpr int VEC = 1;\n";
+    emit_source_access(gr, t, T);
+    src << " && ccb::aligned16(p.o" << t << ");\n  }\n";
+    src << "  static __device__ __forceinline__ void store(const P& p, long long i, T v) { p.o" << t << "[i] = v; }\n";
+    src << "  static __device__ __forceinline__ void store4(const P& p, long long i, const T* x) {\n"
+        << "    ccb::V4<T> s; s.v[0] = x[0]; s.v[1] = x[1]; s.v[2] = x[2]; s.v[3] = x[3]; ccb::st4(p.o" << t << " + i, s);\n  }\n";
+    src << "};\n";
+    std::string call;
+    if (flat) {
+      call = "ccb::scan_flat<" + F + ", " + std::to_string(items) + ">(p);";
+    } else if (gr.n >= 1024) {
+      call = "ccb::scan_rows_block<" + F + ", " + std::to_string(dt_size(x.dt) == 4 ? 8 : 4) + ">(p);";
+    } else {
+      call = "ccb::scan_rows_warp<" + F + ">(p);";
+    }
+    src << "extern \"C\" __global__ void __launch_bounds__(256) " << fn << "(const " << F << "::P p) { " << call << " }\n\n";
+    LaunchSpec& l = add_launch(fn, fields);
+    if (flat) {
+      l.mode = GM_FIXED;
+      l.gx = ntiles;
+    } else {
+      l.mode = GM_PERSISTENT;
+      l.work = gr.rows;
+      l.per_block = gr.n >= 1024 ? 1 : 8;
+    }
+  }
+
+  void emit_red_rows(int gi) {
+    Group& gr = groups[gi];
+    const int t = gr.root;
+    const GTensor& x = g.ts[t];
+    const char* T = dt_ctype(x.dt);
+    const std::string F = "F" + std::to_string(gi);
+    const std::string fn = "ccb_redrows_" + std::to_string(gi);
+    node_buf[t] = add_buf("t" + std::to_string(x.uid), dt_size(x.dt), x.numel, BR_NODE, t, false);
+    std::vector<Field> fields;
+    for (int b : loads_of(gr.ctx)) fields.push_back(in_field(b));
+    fields.push_back(out_field(t));
+    fields.push_back(buf_field("unsigned* err", out->err_buf));
+    fields.push_back(i64_field("n", gr.n));
+    fields.push_back(i64_field("rows", gr.rows));
+    src << "// row reduction " << gi << ": " << gr.rows << " rows of " << gr.n << "\n";
+    src << "struct " << F << " {\n";
+    emit_struct(fields);
+    src << "  typedef " << T << " T;\n  static constexpr int VEC = 1;\n";
+    emit_source_access(gr, t, T);
+    src << ";\n  }\n";
+    src << "  static __device__ __forceinline__ void store_row(const P& p, long long r, T v) { p.o" << t << "[r] = v; }\n";
+    src << "};\n";
+    const bool block = gr.n >= 1024;
+    src << "extern \"C\" __global__ void __launch_bounds__(256) " << fn << "(const " << F << "::P p) { ccb::"
+        << (block ? "reduce_rows_block" : "reduce_rows_warp") << "<" << F << ">(p); }\n\n";
+    LaunchSpec& l = add_launch(fn, fields);
+    l.mode = GM_PERSISTENT;
+    l.work = gr.rows;
+    l.per_block = block ? 1 : 8;
+  }
+
+  void emit_scatter(int gi) {
+    Group& gr = groups[gi];
+    const int t = gr.root;
+    const GTensor& x = g.ts[t];
+    const char* T = dt_ctype(x.dt);
+    const std::string F = "F" + std::to_string(gi);
+    const std::string fn = "ccb_scatter_" + std::to_string(gi);
+    node_buf[t] = add_buf("t" + std::to_string(x.uid), dt_size(x.dt), x.numel, BR_NODE, t, false);
+    OpSpec z;
+    z.kind = OP_ZERO;
+    z.buf = node_buf[t];
+    out->ops.push_back(z);
+    std::vector<Field> fields;
+    for (int b : loads_of(gr.ctx)) fields.push_back(in_field(b));
+    Field o = out_field(t);
+    o.decl = std::string(T) + "* out";
+    fields.push_back(o);
+    fields.push_back(buf_field("unsigned* err", out->err_buf));
+    fields.push_back(i64_field("n", gr.domain));
+    fields.push_back(i64_field("m", x.numel));
+    src << "// scatter_add " << gi << ": " << gr.domain << " updates into " << x.numel << " bins\n";
+    src << "struct " << F << " {\n";
+    emit_struct(fields);
+    src << "  typedef " << T << " T;\n";
+    src << "  static __device__ __forceinline__ int idx(const P& p, long long li) {\n    const int i = (int)li;\n";
+    {
+      Emitter e(gr.ctx, src);
+      std::string v = e.val(gr.val);
+      src << "    return " << v << ";\n  }\n";
+    }
+    src << "  static __device__ __forceinline__ T val(const P& p, long long li) {\n    const int i = (int)li;\n";
+    {
+      Emitter e(gr.ctx, src);
+      std::string v = e.val(gr.val2);
+      src << "    return " << v << ";\n  }\n";
+    }
+    src << "};\n";
+    src << "extern \"C\" __global__ void __launch_bounds__(256) " << fn << "(const " << F << "::P p) { ccb::scatter_add<" << F
+        << ">(p); }\n\n";
+    LaunchSpec& l = add_launch(fn, fields);
+    l.mode = GM_PERSISTENT;
+    l.work = gr.domain;
+    l.per_block = 256 * 4;
+  }
+
+  void emit_matmul(int gi) {
+    Group& gr = groups[gi];
+    const int t = gr.root;
+    const GTensor& x = g.ts[t];
+    const char* T = dt_ctype(x.dt);
+    const std::string F = "F" + std::to_string(gi);
+    const std::string fn = "ccb_matmul_" + std::to_string(gi);
+    const int64_t M = x.shape[0], N = x.shape[1], K = g.ts[x.dep0].shape[1];
+    node_buf[t] = add_buf("t" + std::to_string(x.uid), dt_size(x.dt), x.numel, BR_NODE, t, false);
+    std::vector<Field> fields;
+    std::set<int> loads = loads_of(gr.ctx);
+    for (int b : loads_of(gr.ctx_b)) loads.insert(b);
+    for (int b : loads) fields.push_back(in_field(b));
+    fields.push_back(out_field(t));
+    fields.push_back(buf_field("unsigned* err", out->err_buf));
+    fields.push_back(i64_field("M", M));
+    fields.push_back(i64_field("N", N));
+    fields.push_back(i64_field("K", K));
+    src << "// matmul " << gi << ": [" << M << "x" << K << "] . [" << K << "x" << N << "]\n";
+    src << "struct " << F << " {\n";
+    emit_struct(fields);
+    src << "  typedef " << T << " T;\n";
+    src << "  static __device__ __forceinline__ T a(const P& p, long long r, long long k) {\n    const int i = (int)(r * p.K + k);\n";
+    {
+      Emitter e(gr.ctx, src);
+      std::string v = e.val(gr.mm_a);
+      src << "    return " << v << ";\n  }\n";
+    }
+    src << "  static __device__ __forceinline__ T b(const P& p, long long k, long long c) {\n    const int i = (int)(k * p.N + c);\n";
+    {
+      Emitter e(gr.ctx_b, src);
+      std::string v = e.val(gr.mm_b);
+      src << "    return " << v << ";\n  }\n";
+    }
+    src << "  static __device__ __forceinline__ void store(const P& p, long long r, long long c, T v) { p.o" << t
+        << "[r * p.N + c] = v; }\n";
+    src << "};\n";
+    src << "extern \"C\" __global__ void __launch_bounds__(256) " << fn << "(const " << F << "::P p) { ccb::matmul_tiled<" << F
+        << ">(p); }\n\n";
+    LaunchSpec& l = add_launch(fn, fields);
+    l.mode = GM_FIXED;
+    l.gx = std::max<int64_t>(1, (N + 63) / 64);
+    l.gy = std::max<int64_t>(1, (M + 63) / 64);
+  }
+
+  void generate(Lowered& o) {
+    out = &o;
+    o.name = g.name;
+    node_buf.assign(g.ts.size(), -1);
+    o.err_buf = add_buf("err", 4, 1, BR_SCRATCH, -1, true);
+    // params first, in graph order (lib/lower/lower.ml:977-987)
+    std::set<std::string> seen;
+    for (int t = 0; t < (int)g.ts.size(); ++t) {
+      const GTensor& x = g.ts[t];
+      if (x.kind != T_PARAM) continue;
+      if (seen.count(x.name)) bad("Graph.create: two Param nodes named " + x.name);
+      seen.insert(x.name);
+      if (x.dt == DT_BOOL) bad("param " + x.name + ": Bool tensors are not storable");
+      node_buf[t] = add_buf("p_" + x.name, dt_size(x.dt), x.numel, BR_PARAM, t, false);
+      IOSpec io;
+      io.name = x.name;
+      io.dt = x.dt;
+      io.shape = x.shape;
+      io.buf = node_buf[t];
+      io.bytes = x.numel * dt_size(x.dt);
+      o.params.push_back(io);
+    }
+    src << "// generated by cudacaml-b200 for sm_100a: " << g.name << "\n#include \"ccb_skel.cuh\"\n\n";
+    for (int gi = 0; gi < (int)groups.size(); ++gi) {
+      switch (groups[gi].kind) {
+        case G_MAPRED: emit_mapred(gi); break;
+        case G_SCAN_FLAT:
+        case G_SCAN_ROWS: emit_scan(gi); break;
+        case G_RED_ROWS: emit_red_rows(gi); break;
+        case G_SCATTER: emit_scatter(gi); break;
+        case G_MATMUL: emit_matmul(gi); break;
+      }
+    }
+    for (auto& op : g.outputs) {
+      const GTensor& x = g.ts[op.second];
+      IOSpec io;
+      io.name = op.first;
+      io.dt = x.dt;
+      io.shape = x.shape;
+      io.buf = node_buf[op.second];
+      io.bytes = x.numel * dt_size(x.dt);
+      if (io.buf < 0) bad("lower: internal: output " + op.first + " has no buffer");
+      o.outputs.push_back(io);
+    }
+    o.source = src.str();
+    // plan text
+    std::ostringstream pt;
+    for (size_t b = 0; b < o.bufs.size(); ++b) {
+      const BufSpec& s = o.bufs[b];
+      pt << "alloc " << s.label << " " << (s.role == BR_PARAM ? "param" : s.role == BR_NODE ? "node" : "scratch") << " "
+         << s.numel << "x" << s.elem_bytes << "B" << (s.zero ? " zero" : "") << "\n";
+    }
+    for (auto& p : o.params) pt << "upload " << p.name << " -> " << o.bufs[p.buf].label << "\n";
+    for (auto& op : o.ops) {
+      if (op.kind == OP_ZERO) pt << "zero " << o.bufs[op.buf].label << "\n";
+      else pt << "launch " << o.launches[op.launch].fn << "\n";
+    }
+    for (auto& p : o.outputs) pt << "download " << o.bufs[p.buf].label << " -> " << p.name << "\n";
+    o.plan_text = pt.str();
+  }
+};
+
+}  // namespace
+
+int lower_graph(const GGraph& g, Lowered& out) {
+  try {
+    Lowerer L(g);
+    L.analyse();
+    L.group_all();
+    L.generate(out);
+  } catch (const LowerError& e) {
+    return fail(e.code, e.what());
+  } catch (const std::exception& e) {
+    return fail(CCB_ERR_INVALID, std::string("lower: ") + e.what());
+  }
+  return CCB_OK;
+}
+
+}  // namespace ccb

@@ -1,0 +1,114 @@
+// Graph wire format -> kernels + host plan.
+//
+// The replacement of the reference compiler: lib/lower/fusion.ml (which nodes
+// own a buffer), lib/lower/lower.ml (per-root kernels and the host plan) and
+// lib/backend_cuda/emit.ml (CUDA text). It targets the skeletons of skel.cuh.
+#pragma once
+#include <cstdint>
+#include <string>
+#include <vector>
+
+namespace ccb {
+
+enum Dt : int { DT_F32 = 0, DT_F64 = 1, DT_I32 = 2, DT_I64 = 3, DT_BOOL = 4 };
+int dt_size(Dt d);
+const char* dt_name(Dt d);
+const char* dt_ctype(Dt d);
+
+// Expression and tensor kinds of the wire format (lib/ir/expr.ml, lib/ir/tensor.ml).
+enum EKind { E_CONST, E_ARG, E_INDEX, E_BINOP, E_UNOP, E_CMP, E_LOGIC, E_NOT, E_SELECT, E_CAST };
+enum TKind { T_PARAM, T_IOTA, T_MAP, T_MAP2, T_REDUCE, T_SCAN, T_GATHER, T_SCATTER, T_MATMUL, T_RESHAPE, T_BROADCAST };
+enum BinOp { B_ADD, B_SUB, B_MUL, B_DIV, B_MIN, B_MAX, B_AND, B_OR, B_XOR, B_SHL, B_SHR };
+enum UnOp { U_NEG, U_SQRT, U_EXP, U_LOG, U_ABS, U_SIN, U_COS, U_ERF, U_ERFINV };
+enum CmpOp { C_EQ, C_NE, C_LT, C_LE, C_GT, C_GE };
+
+struct GExpr {
+  Dt dt;
+  int kind;
+  int op = 0;
+  int a = -1, b = -1, c = -1;
+  double f = 0.0;   // float constant (exact double of the wire)
+  int64_t i = 0;    // integer / bool constant, or Arg position
+};
+
+struct GTensor {
+  int64_t uid;
+  Dt dt;
+  std::vector<int64_t> shape;
+  int kind;
+  std::string name;  // params
+  int dep0 = -1, dep1 = -1;
+  int arg0 = -1, arg1 = -1, body = -1, init = -1;
+  int64_t numel = 1;
+};
+
+struct GGraph {
+  std::string name;
+  std::vector<GExpr> ex;
+  std::vector<GTensor> ts;
+  std::vector<std::pair<std::string, int>> outputs;
+};
+
+// Status code (CCB_*) and message through ccb::fail on error.
+int parse_graph(const char* text, GGraph& g);
+
+// ------------------------------------------------------------ lowered program
+enum BufRole { BR_PARAM = 0, BR_NODE = 1, BR_SCRATCH = 2 };
+struct BufSpec {
+  std::string label;
+  int elem_bytes = 4;
+  int64_t numel = 0;
+  int role = BR_SCRATCH;
+  int node = -1;      // tensor index for params and nodes
+  bool zero = false;  // zero-filled once at allocation
+};
+
+enum SlotKind { SL_BUF = 0, SL_I64 = 1, SL_EPOCH = 2 };
+struct Slot {
+  int kind = SL_BUF;
+  int buf = -1;
+  int64_t val = 0;
+};
+
+enum GridMode { GM_FIXED = 0, GM_PERSISTENT = 1 };
+struct LaunchSpec {
+  std::string fn;
+  int mode = GM_FIXED;
+  int64_t gx = 1, gy = 1;
+  int64_t work = 0;            // persistent: work items
+  int64_t per_block = 1;       // persistent: items one block iteration covers
+  int64_t max_grid = 1 << 30;  // persistent: cap (scratch is sized for it)
+  int block = 256;
+  std::vector<Slot> slots;
+};
+
+enum OpKind { OP_LAUNCH = 0, OP_ZERO = 1 };
+struct OpSpec {
+  int kind = OP_LAUNCH;
+  int launch = -1;
+  int buf = -1;
+};
+
+struct IOSpec {
+  std::string name;
+  Dt dt;
+  std::vector<int64_t> shape;
+  int buf = -1;
+  int64_t bytes = 0;
+};
+
+struct Lowered {
+  std::string name;
+  std::string source;
+  std::vector<BufSpec> bufs;
+  std::vector<LaunchSpec> launches;
+  std::vector<OpSpec> ops;
+  std::vector<IOSpec> params, outputs;
+  int err_buf = -1;
+  int num_kernels = 0;
+  std::string plan_text;
+};
+
+int lower_graph(const GGraph& g, Lowered& out);
+
+}  // namespace ccb

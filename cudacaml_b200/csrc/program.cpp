@@ -1,0 +1,351 @@
+// Compiled programs: NVRTC + module load + per-lane buffer pools, and the
+// stream-ordered execution of the host plan. Replaces the reference's
+// Backend_cuda.compile_on (lib/backend_cuda/cudacaml_backend_cuda.ml:30-43) and
+// Executor (lib/backend_cuda/executor.ml:72-244).
+#include <algorithm>
+#include <cstring>
+#include <memory>
+#include <unordered_map>
+
+#include "common.hpp"
+#include "lower.hpp"
+
+namespace ccb {
+void live_add(long long d);
+}
+
+namespace {
+using namespace ccb;
+
+struct Lane {
+  CUstream stream = nullptr;
+  CUevent done = nullptr;
+  std::vector<CUdeviceptr> bufs;
+  unsigned* host_err = nullptr;  // pinned slot the error word is copied to
+  uint64_t epoch = 0;
+};
+
+struct Program {
+  Lowered L;
+  int device = -1;
+  CUmodule mod = nullptr;
+  std::vector<CUfunction> fns;
+  std::vector<unsigned> gx, gy;
+  std::vector<Lane> lanes;
+  int num_launch_ops = 0;
+};
+
+int lane_check(Program& P, int lane) {
+  const unsigned e = *P.lanes[lane].host_err;
+  if (e == 0) return CCB_OK;
+  std::string m = "device check failed:";
+  if (e & 1u) m += " gather index out of bounds;";
+  if (e & 2u) m += " scatter_add index out of bounds;";
+  if (e & 4u) m += " scan look-back wait gave up (bounded spin exhausted);";
+  *P.lanes[lane].host_err = 0;
+  return fail(CCB_ERR_DEVICE_CHECK, m);
+}
+
+int64_t buf_bytes(const BufSpec& b) { return b.numel * (int64_t)b.elem_bytes; }
+
+int destroy(Program* P) {
+  if (!P) return CCB_OK;
+  if (P->device >= 0 && driver().ok && ensure_context(P->device) == CCB_OK) {
+    const Driver& d = driver();
+    for (Lane& l : P->lanes) {
+      if (l.stream) d.cuStreamSynchronize(l.stream);
+      for (CUdeviceptr b : l.bufs)
+        if (b) {
+          d.cuMemFree(b);
+          live_add(-1);
+        }
+      if (l.host_err) d.cuMemFreeHost(l.host_err);
+      if (l.done) d.cuEventDestroy(l.done);
+      if (l.stream) d.cuStreamDestroy(l.stream);
+    }
+    if (P->mod) d.cuModuleUnload(P->mod);
+  }
+  delete P;
+  return CCB_OK;
+}
+
+// Issue one run on `stream`: uploads (host runs), zero fills and launches,
+// downloads (host runs) and the error-word readback.
+int issue(Program& P, int lane, const void* const* h_in, void* const* h_out, const void* const* d_in, void* const* d_out,
+          CUstream stream) {
+  const Driver& d = driver();
+  Lane& ln = P.lanes[lane];
+  std::vector<CUdeviceptr> ptr = ln.bufs;
+  std::vector<char> overridden(ptr.size(), 0);
+  if (d_in) {
+    for (size_t i = 0; i < P.L.params.size(); ++i) {
+      ptr[P.L.params[i].buf] = (CUdeviceptr)d_in[i];
+      overridden[P.L.params[i].buf] = 1;
+    }
+  }
+  // Resident outputs are written in place; an output whose buffer is already
+  // bound (a param, or a second name for one node) is copied afterwards.
+  std::vector<std::pair<CUdeviceptr, int>> copies;  // (dst, buf)
+  if (d_out) {
+    for (size_t j = 0; j < P.L.outputs.size(); ++j) {
+      const int b = P.L.outputs[j].buf;
+      if (overridden[b]) {
+        copies.push_back({(CUdeviceptr)d_out[j], b});
+      } else {
+        ptr[b] = (CUdeviceptr)d_out[j];
+        overridden[b] = 1;
+      }
+    }
+  }
+  if (h_in) {
+    for (size_t i = 0; i < P.L.params.size(); ++i) {
+      const IOSpec& p = P.L.params[i];
+      if (p.bytes) CCB_CU(d.cuMemcpyHtoDAsync(ptr[p.buf], h_in[i], p.bytes, stream));
+    }
+  }
+  ln.epoch = ln.epoch % ((1u << 30) - 2) + 1;
+  std::vector<uint64_t> blk;
+  for (const OpSpec& op : P.L.ops) {
+    if (op.kind == OP_ZERO) {
+      const int64_t n = buf_bytes(P.L.bufs[op.buf]);
+      if (n) CCB_CU(d.cuMemsetD8Async(ptr[op.buf], 0, n, stream));
+      continue;
+    }
+    const LaunchSpec& l = P.L.launches[op.launch];
+    blk.assign(l.slots.size(), 0);
+    for (size_t s = 0; s < l.slots.size(); ++s) {
+      const Slot& sl = l.slots[s];
+      blk[s] = sl.kind == SL_BUF ? (uint64_t)ptr[sl.buf] : sl.kind == SL_I64 ? (uint64_t)sl.val : ln.epoch;
+    }
+    void* args[] = {blk.data()};
+    CCB_CU(d.cuLaunchKernel(P.fns[op.launch], P.gx[op.launch], P.gy[op.launch], 1, l.block, 1, 1, 0, stream, args, nullptr));
+  }
+  for (auto& c : copies) {
+    const int64_t n = buf_bytes(P.L.bufs[c.second]);
+    if (n) CCB_CU(d.cuMemcpyDtoDAsync(c.first, ptr[c.second], n, stream));
+  }
+  if (h_out) {
+    for (size_t j = 0; j < P.L.outputs.size(); ++j) {
+      const IOSpec& o = P.L.outputs[j];
+      if (o.bytes) CCB_CU(d.cuMemcpyDtoHAsync(h_out[j], ptr[o.buf], o.bytes, stream));
+    }
+  }
+  CCB_CU(d.cuMemcpyDtoHAsync(ln.host_err, ln.bufs[P.L.err_buf], 4, stream));
+  CCB_CU(d.cuMemsetD8Async(ln.bufs[P.L.err_buf], 0, 4, stream));
+  CCB_CU(d.cuEventRecord(ln.done, stream));
+  return CCB_OK;
+}
+
+Program* as_prog(ccb_program_t p) { return static_cast<Program*>(p); }
+
+int need_device(Program* P) {
+  if (!P) return fail(CCB_ERR_INVALID, "null program");
+  if (P->device < 0) return fail(CCB_ERR_INVALID, "program was lowered without a device (ccb_program_lower)");
+  return ensure_context(P->device);
+}
+
+int check_lane(Program* P, int lane) {
+  if (lane < 0 || lane >= (int)P->lanes.size())
+    return fail(CCB_ERR_INVALID, "lane " + std::to_string(lane) + " out of range (" + std::to_string(P->lanes.size()) + " lanes)");
+  return CCB_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int ccb_program_lower(const char* graph, ccb_program_t* prog) {
+  if (!graph || !prog) return fail(CCB_ERR_INVALID, "ccb_program_lower: null argument");
+  GGraph g;
+  CCB_TRY(parse_graph(graph, g));
+  auto P = std::make_unique<Program>();
+  CCB_TRY(lower_graph(g, P->L));
+  for (auto& op : P->L.ops)
+    if (op.kind == OP_LAUNCH) P->num_launch_ops++;
+  *prog = P.release();
+  return CCB_OK;
+}
+
+int ccb_program_create(const char* graph, int device, int lanes, ccb_program_t* prog) {
+  if (lanes < 1) return fail(CCB_ERR_INVALID, "Backend_cuda.compile_on: streams must be >= 1");
+  ccb_program_t h = nullptr;
+  CCB_TRY(ccb_program_lower(graph, &h));
+  Program* P = as_prog(h);
+  int rc = ensure_context(device);
+  if (rc != CCB_OK) {
+    destroy(P);
+    return rc;
+  }
+  P->device = device;
+  const Driver& d = driver();
+  auto cleanup = [&](int code) {
+    destroy(P);
+    return code;
+  };
+  std::string cubin, log;
+  rc = nvrtc_compile(P->L.source, P->L.name.empty() ? "ccb" : P->L.name, cubin, log);
+  if (rc != CCB_OK) return cleanup(rc);
+  CUresult r = d.cuModuleLoadData(&P->mod, cubin.data());
+  if (r != CUDA_SUCCESS) return cleanup(cu_fail(r, "cuModuleLoadData"));
+  int sms = 0;
+  CUdevice dev;
+  d.cuDeviceGet(&dev, device);
+  d.cuDeviceGetAttribute(&sms, CU_DEVICE_ATTRIBUTE_MULTIPROCESSOR_COUNT, dev);
+  for (auto& l : P->L.launches) {
+    CUfunction f;
+    r = d.cuModuleGetFunction(&f, P->mod, l.fn.c_str());
+    if (r != CUDA_SUCCESS) return cleanup(cu_fail(r, "cuModuleGetFunction"));
+    P->fns.push_back(f);
+    int64_t gx = l.gx, gy = l.gy;
+    if (l.mode == GM_PERSISTENT) {
+      int occ = 1;
+      d.cuOccupancyMaxActiveBlocksPerMultiprocessor(&occ, f, l.block, 0);
+      const int64_t cap = std::min<int64_t>(l.max_grid, (int64_t)std::max(1, sms) * std::max(1, occ));
+      const int64_t want = (l.work + l.per_block - 1) / std::max<int64_t>(1, l.per_block);
+      gx = std::max<int64_t>(1, std::min(want, cap));
+      gy = 1;
+    }
+    if (gx > 0x7fffffff || gy > 65535) return cleanup(fail(CCB_ERR_UNSUPPORTED, "launch grid too large for " + l.fn));
+    P->gx.push_back((unsigned)gx);
+    P->gy.push_back((unsigned)gy);
+  }
+  P->lanes.resize(lanes);
+  for (Lane& ln : P->lanes) {
+    r = d.cuStreamCreate(&ln.stream, CU_STREAM_NON_BLOCKING);
+    if (r != CUDA_SUCCESS) return cleanup(cu_fail(r, "cuStreamCreate"));
+    r = d.cuEventCreate(&ln.done, CU_EVENT_DISABLE_TIMING);
+    if (r != CUDA_SUCCESS) return cleanup(cu_fail(r, "cuEventCreate"));
+    r = d.cuMemHostAlloc((void**)&ln.host_err, 64, CU_MEMHOSTALLOC_PORTABLE);
+    if (r != CUDA_SUCCESS) return cleanup(cu_fail(r, "cuMemHostAlloc"));
+    *ln.host_err = 0;
+    ln.bufs.assign(P->L.bufs.size(), 0);
+    for (size_t b = 0; b < P->L.bufs.size(); ++b) {
+      const int64_t n = std::max<int64_t>(buf_bytes(P->L.bufs[b]), 16);
+      r = d.cuMemAlloc(&ln.bufs[b], (size_t)n);
+      if (r != CUDA_SUCCESS) return cleanup(cu_fail(r, ("cuMemAlloc (" + P->L.bufs[b].label + ")").c_str()));
+      live_add(1);
+      if (P->L.bufs[b].zero) {
+        r = d.cuMemsetD8Async(ln.bufs[b], 0, (size_t)n, ln.stream);
+        if (r != CUDA_SUCCESS) return cleanup(cu_fail(r, "cuMemsetD8Async"));
+      }
+    }
+    r = d.cuStreamSynchronize(ln.stream);
+    if (r != CUDA_SUCCESS) return cleanup(cu_fail(r, "cuStreamSynchronize"));
+  }
+  *prog = P;
+  return CCB_OK;
+}
+
+int ccb_program_destroy(ccb_program_t prog) { return destroy(as_prog(prog)); }
+
+int ccb_program_source(ccb_program_t prog, const char** source) {
+  if (!prog) return fail(CCB_ERR_INVALID, "null program");
+  *source = as_prog(prog)->L.source.c_str();
+  return CCB_OK;
+}
+
+int ccb_program_device(ccb_program_t prog, int* device) {
+  if (!prog) return fail(CCB_ERR_INVALID, "null program");
+  *device = as_prog(prog)->device;
+  return CCB_OK;
+}
+
+int ccb_program_num_kernels(ccb_program_t prog, int* n) {
+  if (!prog) return fail(CCB_ERR_INVALID, "null program");
+  *n = as_prog(prog)->L.num_kernels;
+  return CCB_OK;
+}
+
+int ccb_program_num_launches(ccb_program_t prog, int* n) {
+  if (!prog) return fail(CCB_ERR_INVALID, "null program");
+  *n = as_prog(prog)->num_launch_ops;
+  return CCB_OK;
+}
+
+int ccb_program_plan(ccb_program_t prog, const char** text) {
+  if (!prog) return fail(CCB_ERR_INVALID, "null program");
+  *text = as_prog(prog)->L.plan_text.c_str();
+  return CCB_OK;
+}
+
+int ccb_program_num_params(ccb_program_t prog, int* n) {
+  if (!prog) return fail(CCB_ERR_INVALID, "null program");
+  *n = (int)as_prog(prog)->L.params.size();
+  return CCB_OK;
+}
+
+int ccb_program_param(ccb_program_t prog, int i, const char** name, int* dtype, int* rank, const long long** dims) {
+  Program* P = as_prog(prog);
+  if (!P || i < 0 || i >= (int)P->L.params.size()) return fail(CCB_ERR_INVALID, "ccb_program_param: bad index");
+  const IOSpec& s = P->L.params[i];
+  *name = s.name.c_str();
+  *dtype = (int)s.dt;
+  *rank = (int)s.shape.size();
+  *dims = (const long long*)s.shape.data();
+  return CCB_OK;
+}
+
+int ccb_program_num_outputs(ccb_program_t prog, int* n) {
+  if (!prog) return fail(CCB_ERR_INVALID, "null program");
+  *n = (int)as_prog(prog)->L.outputs.size();
+  return CCB_OK;
+}
+
+int ccb_program_output(ccb_program_t prog, int i, const char** name, int* dtype, int* rank, const long long** dims) {
+  Program* P = as_prog(prog);
+  if (!P || i < 0 || i >= (int)P->L.outputs.size()) return fail(CCB_ERR_INVALID, "ccb_program_output: bad index");
+  const IOSpec& s = P->L.outputs[i];
+  *name = s.name.c_str();
+  *dtype = (int)s.dt;
+  *rank = (int)s.shape.size();
+  *dims = (const long long*)s.shape.data();
+  return CCB_OK;
+}
+
+int ccb_program_enqueue(ccb_program_t prog, int lane, const void* const* inputs, void* const* outputs) {
+  Program* P = as_prog(prog);
+  CCB_TRY(need_device(P));
+  CCB_TRY(check_lane(P, lane));
+  return issue(*P, lane, inputs, outputs, nullptr, nullptr, P->lanes[lane].stream);
+}
+
+int ccb_program_wait(ccb_program_t prog, int lane) {
+  Program* P = as_prog(prog);
+  CCB_TRY(need_device(P));
+  CCB_TRY(check_lane(P, lane));
+  CCB_CU(driver().cuEventSynchronize(P->lanes[lane].done));
+  return lane_check(*P, lane);
+}
+
+int ccb_program_run(ccb_program_t prog, const void* const* inputs, void* const* outputs) {
+  CCB_TRY(ccb_program_enqueue(prog, 0, inputs, outputs));
+  return ccb_program_wait(prog, 0);
+}
+
+int ccb_program_run_device(ccb_program_t prog, int lane, const void* const* inputs, void* const* outputs,
+                           ccb_stream_t stream) {
+  Program* P = as_prog(prog);
+  CCB_TRY(need_device(P));
+  CCB_TRY(check_lane(P, lane));
+  if (!P->L.params.empty() && !inputs) return fail(CCB_ERR_INVALID, "run_device: inputs required");
+  if (!outputs) return fail(CCB_ERR_INVALID, "run_device: outputs required");
+  return issue(*P, lane, nullptr, nullptr, inputs, outputs, stream ? (CUstream)stream : P->lanes[lane].stream);
+}
+
+int ccb_program_check(ccb_program_t prog, int lane, ccb_stream_t stream) {
+  Program* P = as_prog(prog);
+  CCB_TRY(need_device(P));
+  CCB_TRY(check_lane(P, lane));
+  CCB_CU(driver().cuStreamSynchronize(stream ? (CUstream)stream : P->lanes[lane].stream));
+  return lane_check(*P, lane);
+}
+
+int ccb_program_lane_stream(ccb_program_t prog, int lane, ccb_stream_t* stream) {
+  Program* P = as_prog(prog);
+  CCB_TRY(need_device(P));
+  CCB_TRY(check_lane(P, lane));
+  *stream = P->lanes[lane].stream;
+  return CCB_OK;
+}
+
+}  // extern "C"

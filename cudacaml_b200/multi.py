@@ -1,0 +1,196 @@
+"""Data-parallel runs across the GPUs of one box, restating CUDACaml's
+``Multi`` (lib/backend_cuda/multi.mli:14-64, multi.ml:123-174).
+
+``Multi(devices, n, build)`` compiles ``build(n // d)`` once per device;
+``run`` slices every input whose leading dimension is ``n`` (a view, no host
+copy), issues all devices before waiting on any, and returns one output list
+per device. ``concat`` and ``mean_scalar`` combine on the host as the
+reference does.
+
+Two additions, both opt-in:
+
+* ``counter_key="seed"`` splits a Monte-Carlo graph by *counter range* with the
+  same seed (device d draws Philox counters [d*n/D, (d+1)*n/D)), so D devices
+  compute exactly the paths one device would. The reference instead asks the
+  caller to reseed each device (multi.mli:39-44). The graph is rewritten to
+  add a scalar ``__ctr_base`` parameter to every Rng counter.
+* ``allreduce_mean(names, inputs)`` recombines scalar outputs with one NCCL
+  all-reduce over NVLink instead of a host loop.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+
+from . import backend_cuda as B
+from . import dsl as D
+from . import runtime as R
+from .ir import I32, Graph, Tensor, Value, numel
+
+CTR_BASE = "__ctr_base"
+
+
+def offset_counters(g: Graph, key: str) -> Graph:
+    """Rewrite every Rng.u32 counter ``map2 f (iota s) (broadcast s key)`` to
+    count from a scalar parameter ``__ctr_base`` (rng.ml:49-59)."""
+    base = D.scalar(CTR_BASE, I32)
+    memo = {}
+
+    def is_counter(t: Tensor) -> bool:
+        if t.kind != "map2":
+            return False
+        i, k = t.deps
+        return (i.kind == "iota" and k.kind == "broadcast" and k.deps[0].kind == "param"
+                and k.deps[0].name == key)
+
+    def go(t: Tensor) -> Tensor:
+        if t.uid in memo:
+            return memo[t.uid]
+        deps = [go(d) for d in t.deps]
+        if is_counter(t):
+            it = t.deps[0]
+            deps[0] = D.map2(D.add, it, D.broadcast(it.shape, base))
+        if all(a is b for a, b in zip(deps, t.deps)):
+            new = t
+        else:
+            new = Tensor(t.dtype, t.shape, t.kind, deps=deps, name=t.name, fn=t.fn, init=t.init)
+        memo[t.uid] = new
+        return new
+
+    return Graph(g.name, [(n, go(t)) for n, t in g.outputs])
+
+
+def concat(values):
+    """Concatenate along the leading axis (multi.ml:51-92)."""
+    if not values:
+        raise ValueError("Multi.concat: no values to concatenate")
+    first = values[0]
+    if len(first.shape) == 0:
+        raise ValueError("Multi.concat: a rank-0 value has no leading axis")
+    rest = first.shape[1:]
+    for v in values:
+        if v.dtype is not first.dtype:
+            raise ValueError(f"Multi.concat: dtype {v.dtype.value} does not match {first.dtype.value}")
+        if len(v.shape) == 0 or v.shape[1:] != rest:
+            raise ValueError(f"Multi.concat: shape {list(v.shape)} does not match {list(first.shape)} outside the leading axis")
+    lead = sum(v.shape[0] for v in values)
+    return Value(first.dtype, (lead,) + tuple(rest), np.concatenate([v.data for v in values]))
+
+
+def mean_scalar(values) -> float:
+    """Plain mean of per-device scalars (multi.ml:105-109)."""
+    if not values:
+        raise ValueError("Multi.mean_scalar: no values to average")
+    for v in values:
+        if v.numel != 1:
+            raise ValueError(f"Multi.mean_scalar: {list(v.shape)} is not a scalar")
+    return sum(float(v.data[0]) for v in values) / len(values)
+
+
+class Multi:
+    def __init__(self, devices, n: int, build, counter_key: str | None = None):
+        devices = list(devices)
+        d = len(devices)
+        if d == 0:
+            raise ValueError("Multi.create: devices must not be empty")
+        if n % d != 0:
+            raise ValueError(f"Multi.create: n = {n} is not divisible by {d} devices")
+        self.devices = devices
+        self.n = n
+        self.per = n // d
+        self.counter_key = counter_key
+        self.released = False
+        self.slots = []
+        for ordinal in devices:
+            g = build(self.per)
+            if counter_key is not None:
+                g = offset_counters(g, counter_key)
+            self.slots.append(B.compile_on(ordinal, g))
+        self._comms = None
+
+    def _inputs_for(self, i: int, inputs):
+        out = []
+        for name, v in inputs:
+            if len(v.shape) and v.shape[0] == self.n:
+                rest = v.shape[1:]
+                stride = numel(rest)
+                data = v.data[i * self.per * stride:(i + 1) * self.per * stride]
+                out.append((name, Value(v.dtype, (self.per,) + tuple(rest), data)))
+            else:
+                out.append((name, v))
+        if self.counter_key is not None:
+            out.append((CTR_BASE, Value.of_list(I32, (), [i * self.per])))
+        return out
+
+    def run_per_device(self, inputs_fn):
+        if self.released:
+            raise RuntimeError("Multi.run: this Multi.t has been released")
+        jobs = [B.run_async(c, inputs_fn(i)) for i, c in enumerate(self.slots)]
+        return [B.wait(j) for j in jobs]
+
+    def run(self, inputs):
+        inputs = list(inputs)
+        return self.run_per_device(lambda i: self._inputs_for(i, inputs))
+
+    def allreduce_mean(self, names, inputs):
+        """Run every device resident, all-reduce the named scalar outputs with
+        NCCL (sum) across devices, and return {name: sum / d}. Needs distinct
+        device ordinals (NCCL puts one rank on each GPU)."""
+        if len(set(self.devices)) != len(self.devices):
+            raise ValueError("Multi.allreduce_mean: NCCL needs distinct devices; use mean_scalar for repeats")
+        L = R.lib()
+        d = len(self.devices)
+        if self._comms is None:
+            arr = (ctypes.c_int * d)(*self.devices)
+            comms = (ctypes.c_void_p * d)()
+            R.check(L.ccb_comm_init_all(d, arr, comms))
+            self._comms = [comms[i] for i in range(d)]
+        inputs = list(inputs)
+        outs_dev = []
+        keep = []
+        for i, c in enumerate(self.slots):
+            with R.with_device(c.device):
+                bound = dict(self._inputs_for(i, inputs))
+                in_bufs = []
+                for pname, dt, shape in c.params:
+                    buf = R.Buffer(bound[pname].byte_size)
+                    buf.upload(bound[pname].data)
+                    in_bufs.append(buf)
+                out_bufs = [R.Buffer(numel(shape) * dt.size_in_bytes) for _, dt, shape in c.outputs]
+                B.run_device_ptrs(c, [b.ptr for b in in_bufs], [b.ptr for b in out_bufs], c.lane_stream(0))
+                keep.append((in_bufs, out_bufs))
+                outs_dev.append(out_bufs)
+        result = {}
+        for name in names:
+            j = [k for k, (n, _, _) in enumerate(self.slots[0].outputs) if n == name][0]
+            _, dt, shape = self.slots[0].outputs[j]
+            R.check(L.ccb_group_start())
+            for i, c in enumerate(self.slots):
+                R.check(L.ccb_allreduce(self._comms[i], outs_dev[i][j].ptr, outs_dev[i][j].ptr, numel(shape),
+                                        R.DT_CODE[dt.value], 0, c.lane_stream(0)))
+            R.check(L.ccb_group_end())
+        for i, c in enumerate(self.slots):
+            B.check_device(c, c.lane_stream(0))
+        for name in names:
+            j = [k for k, (n, _, _) in enumerate(self.slots[0].outputs) if n == name][0]
+            _, dt, shape = self.slots[0].outputs[j]
+            host = np.empty(numel(shape), dtype=dt.np)
+            with R.with_device(self.slots[0].device):
+                outs_dev[0][j].download(host)
+            result[name] = float(host[0]) / d
+        for c, (ib, ob) in zip(self.slots, keep):
+            with R.with_device(c.device):
+                for b in ib + ob:
+                    b.free()
+        return result
+
+    def release(self):
+        if not self.released:
+            self.released = True
+            for c in self.slots:
+                B.release(c)
+            if self._comms:
+                for h in self._comms:
+                    R.lib().ccb_comm_destroy(h)
+                self._comms = None

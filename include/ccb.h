@@ -1,0 +1,173 @@
+/* ccb.h -- the C-ABI of libccb.so, the B200-native execution backend for
+ * CUDACaml graphs.
+ *
+ * Every entry point takes plain pointers, sizes and opaque handles, returns an
+ * int status (CCB_OK = 0) and, on failure, leaves a message readable through
+ * ccb_last_error() on the calling thread. The reference's OCaml runtime binds
+ * the CUDA driver and NVRTC through the third-party `cudajit` package; each
+ * group below names the reference interface (file:line in sinj3d/CUDACaml)
+ * that its functions replace, so an OCaml `ctypes` binding can swap one for
+ * the other. libccb.so opens libcuda.so.1, libnvrtc and libnccl lazily, so it
+ * loads on a machine without a GPU; only the calls that need a device fail.
+ */
+#ifndef CCB_H
+#define CCB_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---------------------------------------------------------------- status */
+enum {
+  CCB_OK = 0,
+  CCB_ERR_INVALID = 1,     /* caller mistake: Invalid_argument on the OCaml side */
+  CCB_ERR_NO_DEVICE = 2,   /* no driver, no device, or an ordinal out of range   */
+  CCB_ERR_DRIVER = 3,      /* a CUDA driver call failed                           */
+  CCB_ERR_COMPILE = 4,     /* NVRTC rejected the generated source                 */
+  CCB_ERR_NCCL = 5,        /* an NCCL call failed                                  */
+  CCB_ERR_DEVICE_CHECK = 6,/* a kernel raised its error word (index out of bounds,
+                              a bounded wait ran out); the message says which     */
+  CCB_ERR_UNSUPPORTED = 7  /* a graph feature this backend does not lower         */
+};
+
+/* Message of the last failing call on this thread ("" if none).
+ * Replaces the exception text cudajit raises (lib/runtime/jit.ml:16-23). */
+const char* ccb_last_error(void);
+/* Library version string, e.g. "ccb 0.1 sm_100a". */
+const char* ccb_version(void);
+
+/* ---------------------------------------------------------------- devices
+ * Replaces lib/runtime/device.mli (available/init/count/with_device/info). */
+typedef struct {
+  char name[256];
+  int cc_major, cc_minor;     /* compute capability, (10, 0) on B200 */
+  int multiprocessors;
+  long long total_memory_bytes;
+} ccb_device_info_t;
+
+int ccb_available(void);                     /* 1 if a driver and >= 1 device; never fails  */
+int ccb_init(void);                          /* cuInit + primary context of device 0         */
+int ccb_device_count(int* count);
+int ccb_set_device(int ordinal);             /* primary context current on this thread       */
+int ccb_get_device(int* ordinal);
+int ccb_device_info(int ordinal, ccb_device_info_t* info);
+int ccb_device_synchronize(void);
+
+/* ---------------------------------------------------------------- memory
+ * Replaces lib/runtime/buffer.mli (alloc/free/upload/download/copy_device,
+ * live_count) and lib/runtime/pinned.mli (page-locked host memory). All act
+ * on the current device. A 0-byte request still returns a valid pointer
+ * (lib/runtime/buffer.ml:16-18). */
+typedef void* ccb_stream_t;   /* NULL = the legacy default stream */
+typedef void* ccb_event_t;
+
+int ccb_malloc(size_t bytes, void** dptr);
+int ccb_free(void* dptr);
+int ccb_live_count(long long* count);        /* allocations minus frees */
+int ccb_memcpy_h2d(void* dst, const void* src, size_t bytes, ccb_stream_t s);   /* async on s */
+int ccb_memcpy_d2h(void* dst, const void* src, size_t bytes, ccb_stream_t s);   /* async on s */
+int ccb_memcpy_d2d(void* dst, const void* src, size_t bytes, ccb_stream_t s);   /* async on s */
+int ccb_memset_d8(void* dst, unsigned char v, size_t bytes, ccb_stream_t s);
+int ccb_host_alloc(size_t bytes, void** hptr);   /* pinned, portable, zero-filled */
+int ccb_host_free(void* hptr);
+
+/* ---------------------------------------------------------------- streams/events
+ * Replaces lib/runtime/stream.mli and lib/runtime/event.mli. */
+int ccb_stream_create(ccb_stream_t* s);      /* non-blocking (lib/runtime/stream.ml:13-15) */
+int ccb_stream_destroy(ccb_stream_t s);
+int ccb_stream_synchronize(ccb_stream_t s);
+int ccb_stream_query(ccb_stream_t s, int* idle);
+int ccb_event_create(ccb_event_t* e);
+int ccb_event_destroy(ccb_event_t e);
+int ccb_event_record(ccb_event_t e, ccb_stream_t s);
+int ccb_event_synchronize(ccb_event_t e);
+int ccb_event_elapsed_ms(ccb_event_t start, ccb_event_t end, float* ms);
+int ccb_stream_wait_event(ccb_stream_t s, ccb_event_t e);
+
+/* ---------------------------------------------------------------- modules
+ * Replaces lib/runtime/jit.mli and lib/runtime/launch.mli: NVRTC for sm_100a
+ * with the skeleton header on the include path, cuModuleLoadData, and a
+ * launch that takes a by-value argument block. */
+typedef void* ccb_module_t;
+typedef void* ccb_function_t;
+int ccb_module_compile(const char* source, const char* name, ccb_module_t* mod, char** log);
+int ccb_module_unload(ccb_module_t mod);
+int ccb_module_get_function(ccb_module_t mod, const char* name, ccb_function_t* fn);
+int ccb_launch(ccb_function_t fn, unsigned gx, unsigned gy, unsigned gz, unsigned bx, unsigned by,
+               unsigned bz, unsigned smem, ccb_stream_t s, void** args);
+/* Compile source to an sm_100a CUBIN without loading it (works without a GPU). */
+int ccb_nvrtc_check(const char* source, const char* name, size_t* cubin_bytes, char** log);
+void ccb_free_string(char* s);
+
+/* ---------------------------------------------------------------- programs
+ * One compiled graph: the replacement of lib/lower (Fusion.plan, Lower.program),
+ * lib/backend_cuda/emit.ml (Emit.program), lib/runtime/jit.ml (Jit.compile) and
+ * lib/backend_cuda/executor.ml (Executor.create_on/run_async/run/run_resident).
+ *
+ * `graph` is the text wire format (cudacaml_b200/wire.py documents it).
+ * A program is compiled for one device and owns `lanes` executors, each with
+ * its own non-blocking stream and buffer pool (compile_with ~streams,
+ * lib/backend_cuda/cudacaml_backend_cuda.mli:28). */
+typedef void* ccb_program_t;
+
+int ccb_program_create(const char* graph, int device, int lanes, ccb_program_t* prog);
+/* Lower and emit only: no device needed. `source` is owned by the program. */
+int ccb_program_lower(const char* graph, ccb_program_t* prog);
+int ccb_program_destroy(ccb_program_t prog);                      /* Backend_cuda.release */
+int ccb_program_source(ccb_program_t prog, const char** source);  /* Backend_cuda.source  */
+int ccb_program_device(ccb_program_t prog, int* device);          /* Backend_cuda.device_of */
+/* Structure, for tests: kernels emitted, launches per run, plan text. */
+int ccb_program_num_kernels(ccb_program_t prog, int* n);
+int ccb_program_num_launches(ccb_program_t prog, int* n);
+int ccb_program_plan(ccb_program_t prog, const char** text);
+
+/* Params and outputs in graph order. dtype codes: 0 f32, 1 f64, 2 i32, 3 i64. */
+int ccb_program_num_params(ccb_program_t prog, int* n);
+int ccb_program_param(ccb_program_t prog, int i, const char** name, int* dtype, int* rank,
+                      const long long** dims);
+int ccb_program_num_outputs(ccb_program_t prog, int* n);
+int ccb_program_output(ccb_program_t prog, int i, const char** name, int* dtype, int* rank,
+                       const long long** dims);
+
+/* Host in, host out. `inputs[i]` is the host storage of param i (graph param
+ * order), `outputs[j]` receives output j. enqueue issues the uploads, the
+ * launches and the downloads on lane `lane`'s stream and returns at once
+ * (Executor.run_async, lib/backend_cuda/executor.ml:109-165); the host
+ * buffers must stay alive until ccb_program_wait(lane) returns. wait blocks,
+ * then checks the lane's device error word. run = enqueue + wait on lane 0. */
+int ccb_program_enqueue(ccb_program_t prog, int lane, const void* const* inputs, void* const* outputs);
+int ccb_program_wait(ccb_program_t prog, int lane);
+int ccb_program_run(ccb_program_t prog, const void* const* inputs, void* const* outputs);
+
+/* Device in, device out, zero-copy (Executor.run_resident,
+ * lib/backend_cuda/executor.ml:181-244): kernels read `inputs[i]` and write
+ * `outputs[j]` (caller-owned device pointers of the exact byte size) directly.
+ * Issued on `stream` (NULL: the lane's own stream); it does not synchronise.
+ * ccb_program_check then synchronises that stream and reads the error word. */
+int ccb_program_run_device(ccb_program_t prog, int lane, const void* const* inputs,
+                           void* const* outputs, ccb_stream_t stream);
+int ccb_program_check(ccb_program_t prog, int lane, ccb_stream_t stream);
+/* Kernel launches per run (for the bench's gpu_launches count). */
+int ccb_program_lane_stream(ccb_program_t prog, int lane, ccb_stream_t* stream);
+
+/* ---------------------------------------------------------------- NCCL
+ * New: the reference has no collective (lib/backend_cuda/multi.ml:51-109
+ * combines on the host). Multi recombines per-device partial results with an
+ * all-reduce over NVLink. dtype codes as above; op 0 = sum, 1 = max, 2 = min. */
+typedef void* ccb_comm_t;
+int ccb_comm_init_all(int ndev, const int* devices, ccb_comm_t* comms);  /* one process, ndev comms */
+int ccb_comm_unique_id(unsigned char id[128]);
+int ccb_comm_init_rank(int nranks, const unsigned char id[128], int rank, ccb_comm_t* comm);
+int ccb_comm_destroy(ccb_comm_t comm);
+int ccb_allreduce(ccb_comm_t comm, const void* send, void* recv, size_t count, int dtype, int op,
+                  ccb_stream_t s);
+int ccb_group_start(void);
+int ccb_group_end(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* CCB_H */

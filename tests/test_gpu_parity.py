@@ -1,0 +1,294 @@
+"""GPU parity: the CUDA path through libccb.so against the oracle (the C++
+restatement of the reference interpreter), in the manner of the reference's
+gated system suite (test/system/test_system.ml S1-S19), plus the
+benchmark-configuration graphs at sizes the oracle finishes in seconds.
+
+Tolerances are the reference's: Differential's default 1e-5 relative-plus-
+absolute band, 1e-3 for long F32 sums (S3, S10), 1e-4/1e-9 for F32/F64
+products (S11), 1e-6 for the F64 Greeks (S13). Integer and Philox u32 outputs
+are bit-exact.
+"""
+import json
+import os
+
+import numpy as np
+import pytest
+
+from cudacaml_b200 import backend_cuda as cuda
+from cudacaml_b200 import differential as Diff
+from cudacaml_b200 import dsl as D
+from cudacaml_b200 import examples as X
+from cudacaml_b200 import rng as Rng
+from cudacaml_b200 import runtime as R
+from cudacaml_b200.ir import F32, F64, I32, Graph, Value
+from oracle import interp
+
+pytestmark = pytest.mark.gpu
+GOLD = json.load(open(os.path.join(os.path.dirname(__file__), "golden", "reference_kats.json")))
+
+
+def diff(g, inputs, tol=1e-5):
+    err = Diff.check(interp, cuda, g, inputs, tolerance=tol)
+    assert err is None, err
+
+
+def f32s(n, f):
+    return Value.of_array(F32, (n,), np.array([f(i) for i in range(n)], dtype=np.float32))
+
+
+def test_native_library_is_the_path():
+    assert R.available(), R.lib().ccb_last_error().decode()
+    info = R.info(0)
+    assert info["compute_capability"][0] >= 10, info
+
+
+@pytest.mark.parametrize("prog", X.PROGRAMS, ids=lambda p: p.name)
+def test_s1_examples(prog):
+    diff(prog.graph(), prog.inputs())
+
+
+@pytest.mark.parametrize("n", GOLD["saxpy_edge_sizes"]["n"])
+def test_s2_saxpy_edge_sizes(n):
+    x = Value.of_array(F32, (n,), np.arange(n, dtype=np.float32))
+    y = Value.of_array(F32, (n,), (n - np.arange(n)).astype(np.float32))
+    diff(X.saxpy(n, 3.0), [("x", x), ("y", y)])
+
+
+def test_s3_sum_4m():
+    n = 1 << 22
+    x = Value.of_array(F32, (n,), (np.arange(n) % 7 - 3.0).astype(np.float32))
+    diff(X.reduce_flat(n, F32), [("x", x)], tol=1e-3)
+
+
+def test_s6_i32_arithmetic():
+    x = D.param("x", I32, (9,))
+    r = D.map(lambda e: D.div(D.sub(e, D.const(I32, 4)), D.const(I32, 2)), x)
+    diff(Graph("i32", [("r", r)]), [("x", Value.of_array(I32, (9,), np.arange(9, dtype=np.int32)))])
+
+
+def test_s8_u32_bit_exact():
+    g = Graph("u32", [("r", Rng.u32(D.scalar("seed", I32), (1 << 20,)))])
+    diff(g, [("seed", Value.of_list(I32, (), [12345]))], tol=0.0)
+
+
+def test_uniform_f32_f64_bit_exact():
+    for dt in (F32, F64):
+        g = Graph("u", [("r", Rng.uniform(dt, D.scalar("seed", I32), (1 << 18,)))])
+        diff(g, [("seed", Value.of_list(I32, (), [5]))], tol=0.0)
+
+
+def test_s9_normal_f32_moments_and_parity():
+    g = Graph("n", [("z", Rng.normal(F32, D.scalar("seed", I32), (1 << 20,)))])
+    c = cuda.compile(g)
+    z = dict(cuda.run(c, [("seed", Value.of_list(I32, (), [99]))]))["z"].data
+    assert abs(z.mean()) < 0.01 and abs(z.var() - 1.0) < 0.02
+    # erfinvf on the device vs the interpreter's Newton-refined erfinv:
+    # within a few single-precision ulps
+    diff(Graph("n", [("z", Rng.normal(F32, D.scalar("seed", I32), (1 << 16,)))]),
+         [("seed", Value.of_list(I32, (), [99]))], tol=2e-6)
+
+
+def test_s10_rows():
+    dims = (1024, 4096)
+    x = D.param("x", F32, dims)
+    zero = D.const(F32, 0.0)
+    g = Graph("rows", [("r", D.reduce_rows(D.add, zero, x)), ("p", D.scan_rows(D.add, zero, x))])
+    v = Value.of_array(F32, dims, (np.arange(dims[0] * dims[1]) % 11 - 5.0).astype(np.float32))
+    diff(g, [("x", v)], tol=1e-3)
+
+
+def test_rows_short_and_max_bit_exact():
+    x = D.param("x", F32, (300, 16))
+    v = Value.of_array(F32, (300, 16), X.philox_normal(3, 300 * 16))
+    g = Graph("r", [("m", D.reduce_rows(D.max, D.const(F32, -3e38), x)),
+                    ("p", D.scan_rows(D.add, D.const(F32, 0.0), x))])
+    diff(g, [("x", v)], tol=1e-5)
+    diff(Graph("m", [("m", D.reduce_rows(D.max, D.const(F32, -3e38), x))]), [("x", v)], tol=0.0)
+
+
+def test_s11_matmul():
+    def mm(dt):
+        a = D.param("a", dt, (256, 192))
+        b = D.param("b", dt, (192, 128))
+        return Graph("mm", [("c", D.matmul(a, b))])
+
+    fa = lambda i: (i % 13) / 7.0 - 0.9  # noqa: E731
+    fb = lambda i: (i % 17) / 5.0 - 1.6  # noqa: E731
+    for dt, tol in ((F32, 1e-4), (F64, 1e-9)):
+        a = Value.of_array(dt, (256, 192), np.array([fa(i) for i in range(256 * 192)], dtype=dt.np))
+        b = Value.of_array(dt, (192, 128), np.array([fb(i) for i in range(192 * 128)], dtype=dt.np))
+        diff(mm(dt), [("a", a), ("b", b)], tol=tol)
+
+
+def test_matmul_transposed_operands_and_skinny():
+    a = D.param("a", F64, (300, 5))
+    b = D.param("b", F64, (300, 3))
+    g = Graph("t", [("ata", D.matmul(D.transpose(a), a)), ("atb", D.matmul(D.transpose(a), b))])
+    va = Value.of_array(F64, (300, 5), X.philox_normal(4, 1500, np.float64))
+    vb = Value.of_array(F64, (300, 3), X.philox_normal(5, 900, np.float64))
+    diff(g, [("a", va), ("b", vb)], tol=1e-9)
+    # the split-K path (k >= 2048, m*n <= 32)
+    n = 1 << 14
+    a = D.param("a", F64, (n, 4))
+    b = D.param("b", F64, (n, 1))
+    g = Graph("t", [("xtx", D.matmul(D.transpose(a), a)), ("xty", D.matmul(D.transpose(a), b))])
+    va = Value.of_array(F64, (n, 4), X.philox_normal(6, 4 * n, np.float64))
+    vb = Value.of_array(F64, (n, 1), X.philox_normal(7, n, np.float64))
+    diff(g, [("a", va), ("b", vb)], tol=1e-9)
+
+
+def test_s12_scatter():
+    n = 100_000
+    idx = Value.of_array(I32, (n,), (np.arange(n) % 7).astype(np.int32))
+    gi = Graph("hi", [("h", D.scatter_add(D.param("idx", I32, (n,)), D.param("s", I32, (n,)), (7,)))])
+    diff(gi, [("idx", idx), ("s", Value.of_array(I32, (n,), np.ones(n, dtype=np.int32)))], tol=0.0)
+    gf = Graph("hf", [("h", D.scatter_add(D.param("idx", I32, (n,)), D.param("s", F32, (n,)), (7,)))])
+    diff(gf, [("idx", idx), ("s", Value.of_array(F32, (n,), ((np.arange(n) % 13) / 4.0).astype(np.float32)))], tol=1e-4)
+
+
+def test_scatter_zipf_and_gather_config():
+    n, bins = 1 << 20, 1 << 16
+    idx = Value.of_array(I32, (n,), X.zipf_indices(4, n, bins))
+    v = Value.of_array(F32, (n,), X.philox_uniform(3, n, np.float32))
+    diff(X.scatter(n, bins), [("idx", idx), ("v", v)], tol=1e-4)
+    tbl = 1 << 16
+    gi = Value.of_array(I32, (n,), (X.philox_word0(4, n) % tbl).astype(np.int32))
+    t = Value.of_array(F32, (tbl,), X.philox_normal(3, tbl))
+    diff(X.gather(n, tbl), [("idx", gi), ("table", t)], tol=0.0)
+
+
+def test_out_of_bounds_gather_is_reported():
+    idx = D.param("idx", I32, (4,))
+    t = D.param("t", F32, (4,))
+    c = cuda.compile(Graph("g", [("g", D.gather(idx, t))]))
+    with pytest.raises(R.CcbError):
+        cuda.run(c, [("idx", Value.of_list(I32, (4,), [0, 1, 7, 2])), ("t", Value.of_list(F32, (4,), [1, 2, 3, 4]))])
+    # the program stays usable after the error
+    out = dict(cuda.run(c, [("idx", Value.of_list(I32, (4,), [3, 2, 1, 0])), ("t", Value.of_list(F32, (4,), [1, 2, 3, 4]))]))
+    assert out["g"].to_list() == [4, 3, 2, 1]
+
+
+def test_s13_greeks_f64_65536():
+    diff(X.call_greeks(65536, F64), X.bs_inputs(F64, seed=7), tol=1e-6)
+
+
+def test_s14_greeks_f32_2p20_vs_closed_form():
+    b = GOLD["bs_greeks_f32_2p20_bands"]
+    cf = X.analytic()
+    c = cuda.compile(X.call_greeks(1 << 20, F32))
+    o = cuda.run(c, X.bs_inputs(F32, seed=b["seed"]))
+    assert abs(X.scalar_out(o, "price") - cf["price"]) <= b["price"]
+    assert abs(X.scalar_out(o, "dprice/ds0") - cf["delta"]) <= b["delta"]
+    assert abs(X.scalar_out(o, "dprice/dvol") - cf["vega"]) <= b["vega"]
+    assert abs(X.scalar_out(o, "dprice/drate") - cf["rho"]) <= b["rho"]
+
+
+def test_greeks_f32_vs_oracle():
+    diff(X.call_greeks(1 << 18, F32), X.bs_inputs(F32, seed=42), tol=2e-4)
+
+
+def test_reduce_scan_config_small():
+    n = 1 << 20
+    xf = Value.of_array(F32, (n,), X.philox_normal(3, n))
+    diff(X.reduce_scan_flat(n, F32), [("x", xf)], tol=2e-3)
+    xi = Value.of_array(I32, (n,), (X.philox_word0(3, n) & 15).astype(np.int32))
+    diff(X.reduce_scan_flat(n, I32), [("x", xi)], tol=0.0)
+
+
+def test_reduce_scan_i32_full_size_exact():
+    # 2^28 I32 U[0,16): exact integer sums, checked against exact host
+    # arithmetic (the scan's last element is the total; prefix sums are
+    # non-decreasing).
+    n = 1 << 28
+    gen = cuda.compile(Graph("gen", [("x", D.map(lambda w: D.bit_and(w, D.const(I32, 15)),
+                                                 Rng.u32(D.scalar("seed", I32), (n,))))]))
+    xi = dict(cuda.run(gen, [("seed", Value.of_list(I32, (), [3]))]))["x"].data
+    cuda.release(gen)
+    assert xi.min() >= 0 and xi.max() <= 15
+    c = cuda.compile(X.reduce_scan_flat(n, I32))
+    o = dict(cuda.run(c, [("x", Value.of_array(I32, (n,), xi))]))
+    total = int(xi.astype(np.int64).sum())
+    assert o["s"].get(0) == total
+    p = o["p"].data
+    assert int(p[-1]) == total
+    assert np.array_equal(p, np.cumsum(xi, dtype=np.int64).astype(np.int32))
+    cuda.release(c)
+
+
+def test_s15_async_streams():
+    n = 1 << 16
+    g = X.saxpy(n, 2.0)
+    c = cuda.compile_with(4, g)
+
+    def inputs(k):
+        return [("x", Value.of_array(F32, (n,), ((np.arange(n) + k) % 1000).astype(np.float32))),
+                ("y", Value.of_array(F32, (n,), np.ones(n, dtype=np.float32)))]
+
+    jobs = [(k, cuda.run_async(c, inputs(k))) for k in range(16)]
+    for k, j in jobs:
+        got = dict(cuda.wait(j))
+        want = dict(cuda.run(c, inputs(k)))
+        assert got["s"].get(0) == want["s"].get(0)
+        assert np.array_equal(got["r"].data, want["r"].data)
+    cuda.release(c)
+
+
+def test_s16_resident_chain_sum():
+    n = 4096
+    chain = X.find("chain")
+    gc = chain.graph()
+    gs = X.reduce_flat(n, F32)
+    cc = cuda.compile(gc)
+    cs = cuda.compile(gs)
+    rx = cuda.upload(dict(chain.inputs())["x"])
+    r = dict(cuda.run_resident(cc, [("x", rx)]))["r"]
+    s = dict(cuda.run_resident(cs, [("x", r)]))["s"]
+    got = cuda.download(s).get(0)
+    ri = dict(interp.run(interp.compile(gc), chain.inputs()))["r"]
+    want = dict(interp.run(interp.compile(gs), [("x", ri)]))["s"].get(0)
+    assert abs(got - want) <= 1e-5 * (1 + abs(want))
+    for v in (rx, r, s):
+        cuda.free_resident(v)
+    cuda.release(cc)
+    cuda.release(cs)
+
+
+def test_s5_pool_stable():
+    n = 4096
+    c = cuda.compile(X.saxpy(n, 2.0))
+    live = R.live_count()
+    for k in range(1, 51):
+        x = Value.of_array(F32, (n,), (np.arange(n) + k).astype(np.float32))
+        y = Value.of_array(F32, (n,), np.ones(n, dtype=np.float32))
+        s = X.scalar_out(cuda.run(c, [("x", x), ("y", y)]), "s")
+        expect = float(np.sum(2.0 * (np.arange(n) + k) + 1.0))
+        assert abs(s - expect) <= expect * 1e-4
+        assert R.live_count() == live
+    cuda.release(c)
+
+
+def test_s19_multi_same_device_and_counter_split():
+    from cudacaml_b200 import multi as M
+    n = 1 << 16
+    saxpy = lambda n: X.saxpy(n, 2.0)  # noqa: E731
+    x = Value.of_array(F32, (n,), np.arange(n, dtype=np.float32))
+    y = Value.of_array(F32, (n,), np.ones(n, dtype=np.float32))
+    c = cuda.compile(saxpy(n))
+    single = dict(cuda.run(c, [("x", x), ("y", y)]))
+    cuda.release(c)
+    devices = [0, 0] if R.count() < 2 else [0, 1]
+    for devs in ([0, 0], devices):
+        t = M.Multi(devs, n, saxpy)
+        per = t.run([("x", x), ("y", y)])
+        assert np.array_equal(M.concat([dict(o)["r"] for o in per]).data, single["r"].data)
+        t.release()
+    # same seed, split counter range: D devices compute one device's paths
+    m = 1 << 18
+    g1 = cuda.compile(X.call_mc(m, F64))
+    p1 = X.scalar_out(cuda.run(g1, X.bs_inputs(F64, seed=42)), "price")
+    cuda.release(g1)
+    t = M.Multi([0, 0, 0, 0], m, lambda k: X.call_mc(k, F64), counter_key="seed")
+    per = t.run(X.bs_inputs(F64, seed=42))
+    pm = M.mean_scalar([dict(o)["price"] for o in per])
+    t.release()
+    assert abs(pm - p1) <= 1e-9 * (1 + abs(p1))

@@ -1,0 +1,116 @@
+"""CPU-only checks of the product: libccb.so loads and exports every entry
+point include/ccb.h declares; lowering makes the expected kernels (the
+reference's structural tests, test/unit/test_lower.ml, test_multikernel.ml);
+every generated program compiles under NVRTC for sm_100a; errors surface as
+the reference's exception classes."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from cudacaml_b200 import backend_cuda as B
+from cudacaml_b200 import dsl as D
+from cudacaml_b200 import examples as X
+from cudacaml_b200 import runtime as R
+from cudacaml_b200.ir import BOOL, F32, F64, I32, Graph
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def header_symbols():
+    text = open(os.path.join(ROOT, "include", "ccb.h")).read()
+    return sorted(set(re.findall(r"\b(ccb_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_library_exports_every_header_symbol():
+    L = ctypes.CDLL(R.LIB_PATH)
+    missing = [s for s in header_symbols() if not hasattr(L, s)]
+    assert not missing, missing
+    assert set(header_symbols()) <= set(R.exported_symbols())
+
+
+def test_library_loads_without_gpu():
+    assert R.lib().ccb_version().decode().startswith("ccb")
+    # no crash, a clean status, whatever the machine
+    assert R.lib().ccb_available() in (0, 1)
+
+
+def nvrtc_ok(src: str, name: str) -> int:
+    sz = ctypes.c_size_t()
+    log = ctypes.c_void_p()
+    rc = R.lib().ccb_nvrtc_check(src.encode(), name.encode(), ctypes.byref(sz), ctypes.byref(log))
+    if log.value:
+        R.lib().ccb_free_string(log)
+    assert rc == 0, R.lib().ccb_last_error().decode()[:4000]
+    return sz.value
+
+
+@pytest.mark.parametrize("prog", X.PROGRAMS, ids=lambda p: p.name)
+def test_examples_compile_for_sm100a(prog):
+    info = B.lower_info(prog.graph())
+    assert nvrtc_ok(info["source"], prog.name) > 0
+
+
+def test_config_graphs_compile():
+    for g in (X.call_greeks(1 << 20, F32), X.call_greeks(1 << 20, F64), X.reduce_scan_flat(1 << 20, F32),
+              X.reduce_scan_flat(1 << 20, I32), X.rows(64, 4096), X.rows(100, 16), X.scatter(1000, 7),
+              X.gather(1000, 100), X.saxpy(1000, 2.0, F64)):
+        assert nvrtc_ok(B.lower_info(g)["source"], g.name) > 0
+
+
+def test_structure():
+    k = lambda g: B.lower_info(g)["kernels"]  # noqa: E731
+    # saxpy: the map, the stored r and the sum share one pass (12 B/elem)
+    assert k(X.saxpy(4096, 2.0)) == 1
+    # five chained maps: one kernel (S4)
+    assert k(X.find("chain").graph()) == 1
+    # s = x*x used three times: recomputed, one pass for a, b and c
+    assert k(X.find("fanout").graph()) == 1
+    # Grad-produced Greeks: forward sum, three adjoint sums, four scalar
+    # outputs -- one launch (the reference makes 25)
+    assert k(X.call_greeks(1 << 20, F32)) == 1
+    assert k(X.call_greeks(4096, F64)) == 1
+    # scan_rows then gather-of-last-column into the mean: 2
+    assert k(X.call_mc_paths(512, 16, F64)) == 2
+    # reduce + scan over one vector: a pass and a look-back scan
+    assert k(X.reduce_scan_flat(1 << 20, F32)) == 2
+    # a skinny product (LSM normal equations) is a one-pass split-K reduction
+    a = D.param("a", F64, (4, 1 << 14))
+    b = D.param("b", F64, (1 << 14, 4))
+    assert k(Graph("mm", [("c", D.matmul(a, b))])) == 1
+    assert "ccb_mapreduce_0" in B.lower_info(Graph("mm", [("c", D.matmul(a, b))]))["source"]
+
+
+def test_plan_mentions_params_and_outputs():
+    plan = B.lower_info(X.saxpy(8, 2.0))["plan"]
+    assert "upload x" in plan and "upload y" in plan
+    assert "-> r" in plan and "-> s" in plan
+
+
+def test_uniform_graph_has_one_param():
+    from cudacaml_b200 import rng as Rng
+    g = Graph("u", [("r", Rng.uniform(F32, D.scalar("seed", I32), (16,)))])
+    assert [n for n, _ in g.params] == ["seed"]
+    assert B.lower_info(g)["plan"].count("upload") == 1
+
+
+def test_bool_output_rejected():
+    x = D.param("x", F32, (4,))
+    g = Graph("b", [("r", D.map(lambda e: D.lt(e, D.const(F32, 0.0)), x))])
+    with pytest.raises(ValueError):
+        B.lower_info(g)
+
+
+def test_malformed_wire_rejected():
+    h = ctypes.c_void_p()
+    rc = R.lib().ccb_program_lower(b"ccbgraph 1\nname x\nt 1 f32 1 4 frobnicate\nend\n", ctypes.byref(h))
+    assert rc == 1
+    assert "unknown tensor kind" in R.lib().ccb_last_error().decode()
+
+
+def test_no_device_is_reported_not_crashed():
+    if R.available():
+        pytest.skip("a device is present")
+    with pytest.raises(R.CcbError):
+        B.compile(X.saxpy(8, 2.0))
