@@ -1,7 +1,9 @@
 #!/usr/bin/env python3
 """Benchmark: Black-Scholes Monte-Carlo price with pathwise Greeks (Grad.grad
-wrt s0, vol, rate), 2^28 paths per GPU, F32 -- the configuration the reference
-metric "MC paths/s" is quoted on. One step = one run of
+wrt s0, vol, rate), 2^28 paths per GPU, F64 (F32 reported alongside) -- the
+configuration the reference metric "MC paths/s" is quoted on (BASELINE
+configs[1]). F64 is the headline because at 2^28 paths the reference's own F32
+normal generator produces a few infinite normals (see "secondary"). One step = one run of
 the Greeks graph (one fused forward+adjoint launch) over 2^28 paths, plus, on
 N > 1 GPUs, the NCCL all-reduce that recombines the four scalar outputs.
 
@@ -33,7 +35,7 @@ sys.path.insert(0, ROOT)
 
 PATHS = 1 << 28
 SEED = 42
-SLOTS_PER_PATH = 150  # algorithmic issue slots per path (Philox, uniform, erfinv, exp, adjoint, sums)
+SLOTS_PER_PATH_F64 = 300  # FP32-issue-slot equivalents per F64 path (Philox ~100 int, ~100 FP64 ops x2)
 
 
 def peaks():
@@ -99,15 +101,17 @@ class ClockSampler:
 # reference arm: the oracle on the host cores
 # ---------------------------------------------------------------------------
 def _oracle_worker(args):
-    n, base = args
+    n, base, dts = args
     sys.path.insert(0, ROOT)
     from cudacaml_b200 import examples as X
     from cudacaml_b200 import multi as M
     from cudacaml_b200.ir import F32, I32, Value
     from oracle import interp as I
-    g = M.offset_counters(X.call_greeks(n, F32), "seed")
+    from cudacaml_b200.ir import F64
+    dt = F64 if dts == "f64" else F32
+    g = M.offset_counters(X.call_greeks(n, dt), "seed")
     c = I.compile(g)
-    ins = X.bs_inputs(F32, seed=SEED) + [(M.CTR_BASE, Value.of_list(I32, (), [base]))]
+    ins = X.bs_inputs(dt, seed=SEED) + [(M.CTR_BASE, Value.of_list(I32, (), [base]))]
     t = time.perf_counter()
     out = dict(I.run(c, ins))
     return time.perf_counter() - t, out["price"].get(0)
@@ -125,7 +129,7 @@ def run_reference(args):
     with ctx.Pool(cores) as pool:
         for step in range(args.warmup + args.steps):
             t0 = time.perf_counter()
-            pool.map(_oracle_worker, [(per, (step * cores + w) * per) for w in range(cores)])
+            pool.map(_oracle_worker, [(per, (step * cores + w) * per, "f64") for w in range(cores)])
             dt = time.perf_counter() - t0
             if step >= args.warmup:
                 times.append(dt)
@@ -135,8 +139,8 @@ def run_reference(args):
         "impl": "reference", "metric": "MC paths/s (Black-Scholes price + pathwise Greeks)", "value": value,
         "unit": "paths/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": 1e3 * total / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "f32", "data": "synthetic (Philox normals, seed 42)",
-        "config": {"workload": "bs_greeks_f32", "paths_per_step": cores * per, "note": "bounded host sample"},
+        "dtype": "f64", "data": "synthetic (Philox normals, seed 42)",
+        "config": {"workload": "bs_greeks_f64 (BASELINE configs[1])", "paths_per_step": cores * per, "note": "bounded host sample"},
         "cpu_baseline": {"value": value, "unit": "paths/s", "cores": cores, "kind": "port",
                          "sample": f"{cores} processes x {per} paths per step, oracle (C++ restatement of the reference interpreter)"},
         "e2e": {"value": value, "unit": "paths/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -151,9 +155,9 @@ def run_reference(args):
 def cpu_baseline_sample():
     """The oracle (port) on one core over a bounded sample of the workload."""
     n = 1 << 20
-    t, _ = _oracle_worker((n, 0))
+    t, _ = _oracle_worker((n, 0, "f64"))
     return {"value": n / t, "unit": "paths/s", "cores": 1, "kind": "port",
-            "sample": f"{n} paths of the same Greeks graph (F32, seed {SEED}) on 1 core, oracle = C++ restatement of the reference interpreter"}
+            "sample": f"{n} paths of the same Greeks graph (F64, seed {SEED}) on 1 core, oracle = C++ restatement of the reference interpreter"}
 
 
 def secondary_hbm(dev, stream_h, flush, pk):
@@ -193,80 +197,53 @@ def secondary_hbm(dev, stream_h, flush, pk):
     return res
 
 
-def run_ours(args):
+def measure_greeks(args, dtype, rank, world, local, dist, comm, flush):
+    """Device-timed and end-to-end paths/s of the Greeks graph in `dtype`."""
     import numpy as np
     from cudacaml_b200 import backend_cuda as B
     from cudacaml_b200 import examples as X
     from cudacaml_b200 import multi as M
     from cudacaml_b200 import runtime as R
-    from cudacaml_b200.ir import F32, I32
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    dist = None
-    if world > 1:
-        import datetime
-        import torch
-        import torch.distributed as dist
-        torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=torch.device("cuda", local))
-    R.set_device(local)
-    pk = peaks()
-
-    g = X.call_greeks(PATHS, F32)
+    g = X.call_greeks(PATHS, dtype)
     if world > 1:
         g = M.offset_counters(g, "seed")
     c = B.compile_on(local, g)
-    n_launch = c.num_launches()
     stream = c.lane_stream(0)
-
-    # resident inputs (param order) and outputs
-    host_in = {"s0": np.array([100.0], np.float32), "vol": np.array([0.2], np.float32),
-               "rate": np.array([0.05], np.float32), "seed": np.array([SEED], np.int32),
-               M.CTR_BASE: np.array([rank * PATHS], np.int32)}
+    fnp = dtype.np
+    esz = np.dtype(fnp).itemsize
+    host_in = {"s0": np.array([100.0], fnp), "vol": np.array([0.2], fnp), "rate": np.array([0.05], fnp),
+               "seed": np.array([SEED], np.int32), M.CTR_BASE: np.array([rank * PATHS], np.int32)}
     in_bufs = []
-    for name, dt, shape in c.params:
+    for name, _, _ in c.params:
         b = R.Buffer(host_in[name].nbytes)
         b.upload(host_in[name])
         in_bufs.append(b)
-    out_bufs = [R.Buffer(4) for _ in c.outputs]
-    comm = None
-    if world > 1:
-        import ctypes
-        uid = (ctypes.c_ubyte * 128)()
-        if rank == 0:
-            R.check(R.lib().ccb_comm_unique_id(uid))
-        obj = [bytes(uid)]
-        dist.broadcast_object_list(obj, src=0)
-        uid = (ctypes.c_ubyte * 128).from_buffer_copy(obj[0])
-        h = ctypes.c_void_p()
-        R.check(R.lib().ccb_comm_init_rank(world, uid, rank, ctypes.byref(h)))
-        comm = h.value
-    red = R.Buffer(16)  # the 4 F32 outputs gathered contiguously for one all-reduce
+    red = R.Buffer(4 * esz)  # the four scalar outputs, contiguous: one all-reduce
+    out_ptrs = [red.ptr + j * esz for j in range(len(c.outputs))]
+    dt_code = R.DT_CODE[dtype.value]
 
     def step():
-        B.run_device_ptrs(c, [b.ptr for b in in_bufs], [b.ptr for b in out_bufs], stream)
+        B.run_device_ptrs(c, [b.ptr for b in in_bufs], out_ptrs, stream)
         if comm is not None:
-            for j, ob in enumerate(out_bufs):
-                R.check(R.lib().ccb_memcpy_d2d(red.ptr + 4 * j, ob.ptr, 4, stream))
-            R.check(R.lib().ccb_allreduce(comm, red.ptr, red.ptr, 4, 0, 0, stream))
-
-    flush_buf = R.Buffer(256 << 20)
-
-    def flush(s):
-        R.check(R.lib().ccb_memset_d8(flush_buf.ptr, 0, 256 << 20, s))
+            R.check(R.lib().ccb_allreduce(comm, red.ptr, red.ptr, 4, dt_code, 0, stream))
 
     def barrier():
         if dist is not None:
             dist.barrier()
 
+    def max_over_ranks(t):
+        if dist is None:
+            return t
+        import torch
+        x = torch.tensor([t], dtype=torch.float64, device=f"cuda:{local}")
+        dist.all_reduce(x, op=dist.ReduceOp.MAX)
+        return float(x.item())
+
     for _ in range(args.warmup):
         flush(stream)
         step()
     B.check_device(c, stream)
-
     evs = [(R.Event(), R.Event()) for _ in range(args.steps)]
     barrier()
     R.check(R.lib().ccb_stream_synchronize(stream))
@@ -282,33 +259,19 @@ def run_ours(args):
     clk = clocks.stop()
     barrier()
     B.check_device(c, stream)
-    t_dev = sum(a.elapsed_ms(b) for a, b in evs) * 1e-3
-    if dist is not None:
-        import torch
-        t = torch.tensor([t_dev], dtype=torch.float64, device=f"cuda:{local}")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        t_dev = float(t.item())
-    value = world * PATHS * args.steps / t_dev
+    t_dev = max_over_ranks(sum(a.elapsed_ms(b) for a, b in evs) * 1e-3)
+    h = np.empty(4, fnp)
+    red.download(h)
+    div = world if comm is not None else 1
+    outs = {name: float(v) / div for (name, _, _), v in zip(c.outputs, h)}
 
-    # read the result once (correctness guard on the timed configuration)
-    outs = {}
-    for (name, _, _), ob in zip(c.outputs, out_bufs):
-        h = np.empty(1, np.float32)
-        ob.download(h)
-        outs[name] = float(h[0])
-    if comm is not None:
-        h = np.empty(4, np.float32)
-        red.download(h)
-        outs = {name: float(v) / world for (name, _, _), v in zip(c.outputs, h)}
-    cf = X.analytic()
-    assert abs(outs["price"] - cf["price"]) < 0.05, outs
-
-    # e2e: host inputs in pinned memory -> H2D, launch, (all-reduce), D2H of
-    # the four results, every step, device-timed on the launching stream.
+    # e2e through the C-ABI with host buffers: pinned inputs are copied in,
+    # the program runs (and, on N > 1, all-reduces), the four results are
+    # read back, every step, device-timed on the launching stream.
     pin_in = [R.pinned_empty(host_in[name].shape, host_in[name].dtype) for name, _, _ in c.params]
     for a, (name, _, _) in zip(pin_in, c.params):
         a[...] = host_in[name]
-    pin_out = R.pinned_empty((4,), np.float32)
+    pin_out = R.pinned_empty((4,), fnp)
     h2d = sum(a.nbytes for a in pin_in)
     e2e_evs = [(R.Event(), R.Event()) for _ in range(args.steps)]
     for k in range(args.warmup + args.steps):
@@ -318,57 +281,131 @@ def run_ours(args):
         for a, b in zip(pin_in, in_bufs):
             R.check(R.lib().ccb_memcpy_h2d(b.ptr, a.ctypes.data, a.nbytes, stream))
         step()
-        src = red if comm is not None else None
-        for j, ob in enumerate(out_bufs):
-            R.check(R.lib().ccb_memcpy_d2h(pin_out.ctypes.data + 4 * j, (src.ptr + 4 * j) if src else ob.ptr, 4, stream))
+        R.check(R.lib().ccb_memcpy_d2h(pin_out.ctypes.data, red.ptr, 4 * esz, stream))
         if k >= args.warmup:
             e2e_evs[k - args.warmup][1].record(stream)
     R.check(R.lib().ccb_stream_synchronize(stream))
-    t_e2e = sum(a.elapsed_ms(b) for a, b in e2e_evs) * 1e-3
-    if dist is not None:
+    B.check_device(c, stream)
+    t_e2e = max_over_ranks(sum(a.elapsed_ms(b) for a, b in e2e_evs) * 1e-3)
+    n_launch = c.num_launches()
+    for b in in_bufs:
+        b.free()
+    red.free()
+    B.release(c)
+    return {"value": world * PATHS * args.steps / t_dev, "t_dev": t_dev, "ms_per_step": 1e3 * t_dev / args.steps,
+            "e2e": world * PATHS * args.steps / t_e2e, "h2d": h2d, "d2h": 4 * esz, "outs": outs, "clocks": clk,
+            "launches": n_launch}
+
+
+def run_ours(args):
+    from cudacaml_b200 import examples as X
+    from cudacaml_b200 import runtime as R
+    from cudacaml_b200.ir import F32, F64
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dist = None
+    if world > 1:
+        import datetime
         import torch
-        t = torch.tensor([t_e2e], dtype=torch.float64, device=f"cuda:{local}")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        t_e2e = float(t.item())
-    e2e = world * PATHS * args.steps / t_e2e
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    R.set_device(local)
+    pk = peaks()
+    comm = None
+    if world > 1:
+        import ctypes
+        uid = (ctypes.c_ubyte * 128)()
+        if rank == 0:
+            R.check(R.lib().ccb_comm_unique_id(uid))
+        obj = [bytes(uid)]
+        dist.broadcast_object_list(obj, src=0)
+        uid = (ctypes.c_ubyte * 128).from_buffer_copy(obj[0])
+        h = ctypes.c_void_p()
+        R.check(R.lib().ccb_comm_init_rank(world, uid, rank, ctypes.byref(h)))
+        comm = h.value
+    flush_buf = R.Buffer(256 << 20)
 
-    avg_launch = t_dev / args.steps
-    issue_peak = 148 * 128 * pk["sm_max_mhz"] * 1e6
-    achieved = SLOTS_PER_PATH * PATHS / avg_launch
-    roofline = {"bound": "issue", "achieved": achieved / 1e9, "peak": issue_peak / 1e9, "unit": "Gslot/s",
-                "frac": achieved / issue_peak, "traffic": None,
-                "note": f"MC moves ~0 algorithmic bytes; {SLOTS_PER_PATH} issue slots/path x 2^28 paths per launch "
-                        f"against 148 SMs x 128 lanes x {pk['sm_max_mhz']:.0f} MHz ({pk['src']} clock)"}
+    def flush(s):
+        R.check(R.lib().ccb_memset_d8(flush_buf.ptr, 0, 256 << 20, s))
 
+    head = measure_greeks(args, F64, rank, world, local, dist, comm, flush)
+    cf = X.analytic()
+    ok = abs(head["outs"]["price"] - cf["price"]) < 0.02
+    f32 = None
+    if world == 1 and not args.no_secondary:
+        f32 = measure_greeks(args, F32, rank, world, local, dist, comm, flush)
     secondary = None
     if rank == 0 and world == 1 and not args.no_secondary:
-        secondary = secondary_hbm(local, stream, flush, pk)
+        secondary = secondary_hbm(local, None, flush, pk)
+        secondary["bs_greeks_f32_2p28"] = {
+            "value": f32["value"], "unit": "paths/s", "e2e": f32["e2e"], "ms_per_step": f32["ms_per_step"],
+            "result": f32["outs"],
+            "note": "the reference's F32 generator rounds (w + 0.5) * 2^-32 to 1.0f for w >= 2^32 - 2^7 "
+                    "(expected ~8 of 2^28 paths) and erfinv(1) = inf, so the F32 price is inf at this size in the "
+                    "reference interpreter too (cudacaml_backend_interp.ml:130); throughput only"}
 
+    avg_launch = head["t_dev"] / args.steps
+    issue_peak = 148 * 128 * pk["sm_max_mhz"] * 1e6
+    achieved = SLOTS_PER_PATH_F64 * PATHS / avg_launch
+    roofline = {"bound": "issue", "achieved": achieved / 1e9, "peak": issue_peak / 1e9, "unit": "Gslot/s",
+                "frac": achieved / issue_peak, "traffic": None,
+                "note": f"Monte Carlo moves ~0 algorithmic bytes; {SLOTS_PER_PATH_F64} FP32-issue-slot equivalents per "
+                        f"F64 path (FP64 and conversions count 2) x 2^28 paths per launch, against 148 SMs x 128 lanes x "
+                        f"{pk['sm_max_mhz']:.0f} MHz ({pk['src']} clock)"}
     if rank == 0:
         line = {
-            "metric": "MC paths/s (Black-Scholes price + pathwise Greeks)", "value": value, "unit": "paths/s",
-            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * t_dev / args.steps,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "metric": "MC paths/s (Black-Scholes price + pathwise Greeks)", "value": head["value"], "unit": "paths/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": head["ms_per_step"],
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
             "data": "synthetic (Philox normals generated in registers, seed 42)",
-            "config": {"workload": "bs_greeks_f32 (BASELINE configs[1])", "paths_per_gpu": PATHS,
-                       "parallelism": f"dp{world} (counter-range split, NCCL all-reduce of 4 scalars)" if world > 1 else "dp1",
+            "config": {"workload": "bs_greeks_f64 (BASELINE configs[1]; F32 under secondary)", "paths_per_gpu": PATHS,
+                       "parallelism": f"dp{world} (counter-range split, NCCL all-reduce of 4 scalars per step)" if world > 1 else "dp1",
                        "l2": "flushed (256 MiB memset) before every timed step", "market": "S0=100 K=100 r=0.05 sigma=0.2 T=1"},
-            "result": outs, "closed_form": cf,
-            "gpu_launches": n_launch * args.steps,
+            "result": head["outs"], "result_ok_vs_closed_form": ok, "closed_form": cf,
+            "gpu_launches": head["launches"] * args.steps,
             "roofline": roofline,
-            "clocks": clk,
-            "e2e": {"value": e2e, "unit": "paths/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 16},
+            "clocks": head["clocks"],
+            "e2e": {"value": head["e2e"], "unit": "paths/s", "h2d_bytes_per_step": head["h2d"],
+                    "d2h_bytes_per_step": head["d2h"]},
         }
         if world == 1:
             line["cpu_baseline"] = cpu_baseline_sample()
         if secondary:
             line["secondary"] = secondary
-        print(json.dumps(line))
+        print(json.dumps(line), flush=True)
     if dist is not None:
         dist.barrier()
         if comm is not None:
             R.lib().ccb_comm_destroy(comm)
         dist.destroy_process_group()
+    return 0 if ok else 1
+
+
+def run_profile_case(args):
+    """A small fixed case for ncu captures: a couple of launches of one kernel."""
+    import numpy as np
+    from cudacaml_b200 import backend_cuda as B
+    from cudacaml_b200 import examples as X
+    from cudacaml_b200 import runtime as R
+    from cudacaml_b200.ir import F32, F64
+    R.set_device(0)
+    n = args.size
+    if args.profile in ("greeks64", "greeks32"):
+        dt = F64 if args.profile == "greeks64" else F32
+        c = B.compile(X.call_greeks(n, dt))
+        ins = X.bs_inputs(dt, seed=SEED)
+    else:
+        g = {"reduce": X.reduce_flat(n, F32), "scan": X.scan_flat(n, F32)}[args.profile]
+        c = B.compile(g)
+        from cudacaml_b200.ir import Value
+        ins = [("x", Value.of_array(F32, (n,), np.full(n, 0.5, np.float32)))]
+    for _ in range(3):
+        out = B.run(c, ins)
+    print(json.dumps({k: float(v.data[0]) for k, v in out if v.numel == 1}))
     return 0
 
 
@@ -379,7 +416,12 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-secondary", action="store_true")
+    ap.add_argument("--profile", default=None, choices=["greeks64", "greeks32", "reduce", "scan"],
+                    help="run a small fixed case (3 launches) for an ncu capture, no timing")
+    ap.add_argument("--size", type=int, default=1 << 24, help="paths/elements of the --profile case")
     args = ap.parse_args()
+    if args.profile:
+        return run_profile_case(args)
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":

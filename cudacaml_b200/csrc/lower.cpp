@@ -348,12 +348,24 @@ struct KCtx {
  private:
   static int64_t wrap(Dt dt, int64_t v) { return dt == DT_I32 ? (int64_t)(int32_t)(uint32_t)(uint64_t)v : v; }
 
+  // Exact integer simplification only (float folding is left to the device
+  // compiler, which rounds exactly as the device does).
   void fold(KN& k) {
-    // Integer constant folding with the wrapping semantics of the device
-    // code; index arithmetic (transpose, rows_of) collapses this way.
-    if (k.op == K_BIN && is_int(k.dt) && n[k.a].op == K_CONST && n[k.b].op == K_CONST) {
+    auto is_c = [&](int id, int64_t v) { return id >= 0 && n[id].op == K_CONST && is_int(n[id].dt) && n[id].iv == v; };
+    if (k.op == K_CAST && n[k.a].op == K_CONST && is_int(k.dt) && is_int(n[k.a].dt)) {
+      const Dt dt = k.dt;
+      const int64_t v = n[k.a].iv;
+      k = KN();
+      k.op = K_CONST;
+      k.dt = dt;
+      k.iv = wrap(dt, v);
+      return;
+    }
+    if (k.op != K_BIN || !is_int(k.dt)) return;
+    if (n[k.a].op == K_CONST && n[k.b].op == K_CONST) {
       const int64_t x = n[k.a].iv, y = n[k.b].iv;
       const uint64_t ux = (uint64_t)x, uy = (uint64_t)y;
+      const int bits = k.dt == DT_I32 ? 32 : 64;
       int64_t v;
       bool ok = true;
       switch (k.sub) {
@@ -369,6 +381,12 @@ struct KCtx {
         case B_AND: v = x & y; break;
         case B_OR: v = x | y; break;
         case B_XOR: v = x ^ y; break;
+        case B_SHL:
+          v = bits == 32 ? (int64_t)(int32_t)((uint32_t)x << (y & 31)) : (int64_t)(ux << (y & 63));
+          break;
+        case B_SHR:
+          v = bits == 32 ? (int64_t)(int32_t)((uint32_t)x >> (y & 31)) : (int64_t)(ux >> (y & 63));
+          break;
         default: ok = false; v = 0;
       }
       if (ok) {
@@ -378,7 +396,47 @@ struct KCtx {
         k.dt = dt;
         k.iv = wrap(dt, v);
       }
+      return;
     }
+    // identities: x+0, x-0, x*1, x^0, x|0, x<<0, x>>0 -> x; x*0, x&0 -> 0
+    int keep = -1;
+    switch (k.sub) {
+      case B_ADD:
+      case B_OR:
+      case B_XOR:
+        if (is_c(k.b, 0)) keep = k.a;
+        else if (is_c(k.a, 0)) keep = k.b;
+        break;
+      case B_SUB:
+      case B_SHL:
+      case B_SHR:
+        if (is_c(k.b, 0)) keep = k.a;
+        break;
+      case B_MUL:
+        if (is_c(k.b, 1)) keep = k.a;
+        else if (is_c(k.a, 1)) keep = k.b;
+        else if (is_c(k.a, 0) || is_c(k.b, 0)) {
+          const Dt dt = k.dt;
+          k = KN();
+          k.op = K_CONST;
+          k.dt = dt;
+          return;
+        }
+        break;
+      case B_AND:
+        if (is_c(k.a, 0) || is_c(k.b, 0)) {
+          const Dt dt = k.dt;
+          k = KN();
+          k.op = K_CONST;
+          k.dt = dt;
+          return;
+        }
+        if (is_c(k.b, -1)) keep = k.a;
+        else if (is_c(k.a, -1)) keep = k.b;
+        break;
+      default: break;
+    }
+    if (keep >= 0) k = n[keep];
   }
 
   void props(KN& k) {
@@ -580,6 +638,32 @@ struct Emitter {
 
   Emitter(const KCtx& cc, std::ostringstream& oo) : c(cc), o(oo) {}
 
+  // I64 value that is the zero extension of an I32 value: text of the I32.
+  bool zext32(int id, std::string& out) {
+    const KN& k = c.n[id];
+    if (k.op == K_CONST && k.dt == DT_I64 && k.iv >= 0 && k.iv <= 0xFFFFFFFFLL) {
+      KN t = k;
+      t.dt = DT_I32;
+      t.iv = (int64_t)(int32_t)(uint32_t)k.iv;
+      out = lit(t);
+      return true;
+    }
+    if (k.op == K_BIN && k.sub == B_AND && k.dt == DT_I64 && c.n[k.b].op == K_CONST && c.n[k.b].iv == 0xFFFFFFFFLL &&
+        c.n[k.a].op == K_CAST && c.n[c.n[k.a].a].dt == DT_I32) {
+      out = val(c.n[k.a].a);
+      return true;
+    }
+    return false;
+  }
+  // SHR(MUL(zext a, zext b), 32) in I64
+  bool mulhi_operands(int id, std::string& a, std::string& b) {
+    const KN& s = c.n[id];
+    if (!(s.op == K_BIN && s.sub == B_SHR && s.dt == DT_I64 && c.n[s.b].op == K_CONST && c.n[s.b].iv == 32)) return false;
+    const KN& m = c.n[s.a];
+    if (!(m.op == K_BIN && m.sub == B_MUL && m.dt == DT_I64)) return false;
+    return zext32(m.a, a) && zext32(m.b, b);
+  }
+
   std::string val(int id) {
     auto it = name.find(id);
     if (it != name.end()) return it->second;
@@ -608,7 +692,17 @@ struct Emitter {
       case K_LOGIC: e = "(" + val(k.a) + (k.sub == 0 ? " && " : " || ") + val(k.b) + ")"; break;
       case K_NOT: e = "(!" + val(k.a) + ")"; break;
       case K_SELECT: e = "(" + val(k.a) + " ? " + val(k.b) + " : " + val(k.c) + ")"; break;
-      case K_CAST: e = cast_text(c.n[k.a].dt, k.dt, val(k.a)); break;
+      case K_CAST: {
+        // (int)(((u64)zext(a) * (u64)zext(b)) >> 32) is the high word of the
+        // 32x32 product: spell it __umulhi so it maps to one multiply.
+        std::string ua, ub;
+        if (k.dt == DT_I32 && mulhi_operands(k.a, ua, ub)) {
+          e = "((int)__umulhi((unsigned int)(" + ua + "), (unsigned int)(" + ub + ")))";
+          break;
+        }
+        e = cast_text(c.n[k.a].dt, k.dt, val(k.a));
+        break;
+      }
     }
     std::string nm = "v" + std::to_string(id) + suffix;
     o << ind << "const " << dt_ctype(k.dt) << " " << nm << " = " << e << ";\n";
@@ -658,6 +752,15 @@ class Lowerer {
 
   explicit Lowerer(const GGraph& gg) : g(gg) {}
 
+  // A product with a tiny inner dimension (LSM's X . beta, K = 3 or 4) is an
+  // element-wise dot product: it fuses into its consumer like a map instead
+  // of costing a tiled launch. Ascending k, as both reference backends sum.
+  static constexpr int64_t kSmallK = 8;
+  bool small_k(int t) const {
+    const GTensor& x = g.ts[t];
+    return x.kind == T_MATMUL && g.ts[x.dep0].shape.size() == 2 && g.ts[x.dep0].shape[1] <= kSmallK;
+  }
+
   void analyse() {
     const int T = (int)g.ts.size();
     uses.assign(T, 0);
@@ -671,7 +774,8 @@ class Lowerer {
     for (auto& o : g.outputs) is_out[o.second] = 1;
     for (int t = 0; t < T; ++t) {
       const GTensor& x = g.ts[t];
-      const bool barrier = x.kind == T_REDUCE || x.kind == T_SCAN || x.kind == T_SCATTER || x.kind == T_MATMUL;
+      const bool barrier = x.kind == T_REDUCE || x.kind == T_SCAN || x.kind == T_SCATTER ||
+                           (x.kind == T_MATMUL && !small_k(t));
       mat[t] = x.kind == T_PARAM || barrier || is_out[t];
       if (mat[t] && x.dt == DT_BOOL) bad("Value.create: Bool tensors are not storable (node n" + std::to_string(x.uid) + ")");
     }
@@ -700,7 +804,7 @@ class Lowerer {
         const int gt = L->group_of[t];
         if (x.kind == T_PARAM || (gt >= 0 && gt < gi)) return ctx->load(x.dt, t, idx);
         if (gt == gi && gt >= 0) {
-          if (x.kind == T_REDUCE || x.kind == T_MATMUL) {
+          if (x.kind == T_REDUCE || (x.kind == T_MATMUL && !L->small_k(t))) {
             // A reduction of this very pass: its value exists only after the
             // final fold, so it may appear only in invariant position.
             const KN& ik = ctx->n[idx];
@@ -749,8 +853,22 @@ class Lowerer {
         }
         case T_RESHAPE: return elem(x.dep0, idx);
         case T_BROADCAST: return elem(x.dep0, ctx->cint(DT_I32, 0));
-        default: throw LowerError(CCB_ERR_INVALID, "lower: node n" + std::to_string(x.uid) + " must be materialised");
+        case T_MATMUL: {
+          if (!L->small_k(t)) break;
+          const int64_t N = x.shape[1], K = L->g.ts[x.dep0].shape[1];
+          const int row = ctx->bin(DT_I32, B_DIV, idx, ctx->cint(DT_I32, N));
+          const int col = ctx->bin(DT_I32, B_SUB, idx, ctx->bin(DT_I32, B_MUL, row, ctx->cint(DT_I32, N)));
+          int acc = is_float(x.dt) ? ctx->cfloat(x.dt, 0.0) : ctx->cint(x.dt, 0);
+          for (int64_t k = 0; k < K; ++k) {
+            const int ia = ctx->bin(DT_I32, B_ADD, ctx->bin(DT_I32, B_MUL, row, ctx->cint(DT_I32, K)), ctx->cint(DT_I32, k));
+            const int ib = ctx->bin(DT_I32, B_ADD, ctx->cint(DT_I32, k * N), col);
+            acc = ctx->bin(x.dt, B_ADD, acc, ctx->bin(x.dt, B_MUL, elem(x.dep0, ia), elem(x.dep1, ib)));
+          }
+          return acc;
+        }
+        default: break;
       }
+      throw LowerError(CCB_ERR_INVALID, "lower: node n" + std::to_string(x.uid) + " must be materialised");
     }
 
     // Instantiate an element function body with its arguments bound.
@@ -950,7 +1068,7 @@ class Lowerer {
         }
         if (!trial.reds.empty() && trial.reds[0].dt != x.dt) throw JoinFail();
         trial.reds.push_back(r);
-      } else if (x.kind == T_MATMUL) {
+      } else if (x.kind == T_MATMUL && !small_k(t)) {
         // skinny product: one additive accumulator per output cell, INDEX = k
         const GTensor& A = g.ts[x.dep0];
         const int64_t M = x.shape[0], N = x.shape[1], K = A.shape[1];
@@ -1092,6 +1210,12 @@ class Lowerer {
         }
         case T_MATMUL: {
           const int64_t M = x.shape[0], N = x.shape[1], K = g.ts[x.dep0].shape[1];
+          if (small_k(t)) {  // an output: an element-wise store
+            if (cur >= 0 && try_join(cur, t)) break;
+            cur = new_group(G_MAPRED, x.numel == 1 ? 1 : x.numel);
+            if (!try_join(cur, t)) bad("lower: internal: cannot start a pass");
+            break;
+          }
           if (M * N <= 32 && K >= 2048) {
             if (cur >= 0 && groups[cur].domain == K && try_join(cur, t)) break;
             cur = new_group(G_MAPRED, K);
