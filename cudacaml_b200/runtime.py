@@ -109,6 +109,8 @@ def _declare(L):
         "ccb_comm_init_rank": (I, [I, c.POINTER(c.c_ubyte), I, c.POINTER(P)]),
         "ccb_comm_destroy": (I, [P]),
         "ccb_allreduce": (I, [P, P, P, SZ, I, I, P]),
+        "ccb_sum_f32_noalloc": (I, [P, c.c_longlong, P, P]),
+        "ccb_noalloc_last_error": (c.c_char_p, []),
         "ccb_group_start": (I, []),
         "ccb_group_end": (I, []),
     }

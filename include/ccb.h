@@ -153,6 +153,24 @@ int ccb_program_check(ccb_program_t prog, int lane, ccb_stream_t stream);
 /* Kernel launches per run (for the bench's gpu_launches count). */
 int ccb_program_lane_stream(ccb_program_t prog, int lane, ccb_stream_t* stream);
 
+/* ---------------------------------------------------------------- no-allocation sum
+ * No counterpart in the reference. For callers that cannot allocate device
+ * memory (inside someone else's stream capture, under an application-owned
+ * memory pool, in a real-time path that must not take the driver's
+ * allocation locks, or in a plugin handed device pointers but no allocator):
+ * the flat F32 sum that a `reduce add` graph lowers to, with its reduction
+ * scratch in one file-scope __device__ array instead of an allocation.
+ * out[0] = sum of x[0..n). Allocates nothing; issued on `stream` (a
+ * cudaStream_t, NULL = legacy default) on the current device, not
+ * synchronised. n must be in [0, 2^31 - 1]. The scratch (4096 block partials
+ * plus a ticket, about 16 KiB) is held by every GPU that loads the library
+ * until exit and is shared by all calls on a device: calls that overlap on
+ * the GPU race and give wrong sums. The first call on a device does that
+ * device's set-up; make it before any stream capture. Errors: 1 invalid
+ * argument, 2 no device, 3 CUDA error; message in ccb_noalloc_last_error(). */
+int ccb_sum_f32_noalloc(const float* x, long long n, float* out, void* stream);
+const char* ccb_noalloc_last_error(void);
+
 /* ---------------------------------------------------------------- NCCL
  * New: the reference has no collective (lib/backend_cuda/multi.ml:51-109
  * combines on the host). Multi recombines per-device partial results with an
