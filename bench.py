@@ -12,7 +12,8 @@ same seed, so N GPUs price N*2^28 distinct paths.
 
 Also measured in the same run (reported under "secondary"): the flat reduce
 and inclusive scan over 2^28 F32 values (HBM GB/s as a fraction of the
-measured copy peak), the other half of the reference metric.
+measured copy peak), the other half of the reference metric. L2 is flushed
+before every timed step by a read-only pass over 256 MiB (twice the L2).
 
 --impl reference times the reference algorithm on the host cores: the oracle
 (the C++ restatement of the reference interpreter, the only runnable form of
@@ -327,10 +328,20 @@ def run_ours(args):
         h = ctypes.c_void_p()
         R.check(R.lib().ccb_comm_init_rank(world, uid, rank, ctypes.byref(h)))
         comm = h.value
-    flush_buf = R.Buffer(256 << 20)
+    # L2 flush between timed steps: a read-only pass over 256 MiB (twice the
+    # 126 MB L2) with the allocation-free sum kernel. A write-based flush (a
+    # memset) would leave ~126 MB of dirty lines whose write-back then
+    # competes with the next timed kernel.
+    flush_n = 64 << 20
+    flush_buf = R.Buffer(4 * flush_n)
+    R.check(R.lib().ccb_memset_d8(flush_buf.ptr, 0, 4 * flush_n, None))
+    flush_out = R.Buffer(4)
+    R.check(R.lib().ccb_stream_synchronize(None))
 
     def flush(s):
-        R.check(R.lib().ccb_memset_d8(flush_buf.ptr, 0, 256 << 20, s))
+        rc = R.lib().ccb_sum_f32_noalloc(flush_buf.ptr, flush_n, flush_out.ptr, s)
+        if rc != 0:
+            raise RuntimeError(R.lib().ccb_noalloc_last_error().decode())
 
     head = measure_greeks(args, F64, rank, world, local, dist, comm, flush)
     cf = X.analytic()
@@ -364,7 +375,7 @@ def run_ours(args):
             "data": "synthetic (Philox normals generated in registers, seed 42)",
             "config": {"workload": "bs_greeks_f64 (BASELINE configs[1]; F32 under secondary)", "paths_per_gpu": PATHS,
                        "parallelism": f"dp{world} (counter-range split, NCCL all-reduce of 4 scalars per step)" if world > 1 else "dp1",
-                       "l2": "flushed (256 MiB memset) before every timed step", "market": "S0=100 K=100 r=0.05 sigma=0.2 T=1"},
+                       "l2": "flushed before every timed step (read-only pass over 256 MiB, twice L2)", "market": "S0=100 K=100 r=0.05 sigma=0.2 T=1"},
             "result": head["outs"], "result_ok_vs_closed_form": ok, "closed_form": cf,
             "gpu_launches": head["launches"] * args.steps,
             "roofline": roofline,

@@ -76,7 +76,7 @@ __device__ __forceinline__ T warp_reduce(int r, T v) {
 // ---------------------------------------------------------------- map / map-reduce
 // F provides:
 //   struct P { ...; long long n; acc_t* partials; unsigned* ticket; unsigned* err; }
-//   typedef acc_t; static constexpr int NRED, VEC; static constexpr bool TAIL;
+//   typedef acc_t; static constexpr int NRED, VEC, UNROLL; static constexpr bool TAIL;
 //   init(acc_t*), identity(r), combine(r,a,b), elem(p,i,acc), elem4(p,i,acc),
 //   vec_ok(p), epilogue(p, const acc_t* res)
 template <class F>
@@ -153,13 +153,14 @@ __device__ __forceinline__ void map_reduce(const typename F::P& p) {
   const int tid = blockIdx.x * blockDim.x + threadIdx.x;
   const int nth = gridDim.x * blockDim.x;
   if (F::VEC && F::vec_ok(p)) {
+    constexpr int U = F::UNROLL;
     const int n4 = n >> 2;
     int g = tid;
-    for (; g + nth < n4; g += 2 * nth) {
-      F::elem4(p, g << 2, acc);
-      F::elem4(p, (g + nth) << 2, acc);
+    for (; g + (U - 1) * nth < n4; g += U * nth) {
+#pragma unroll
+      for (int u = 0; u < U; ++u) F::elem4(p, (g + u * nth) << 2, acc);
     }
-    if (g < n4) F::elem4(p, g << 2, acc);
+    for (; g < n4; g += nth) F::elem4(p, g << 2, acc);
     for (int i = (n4 << 2) + tid; i < n; i += nth) F::elem(p, i, acc);
   } else {
     for (int i = tid; i < n; i += nth) F::elem(p, i, acc);
@@ -210,65 +211,166 @@ __device__ __forceinline__ T block_scan_excl(T v, T* total, T* s_warp /* [BLOCK/
 // with Decoupled Look-back", 2016). Tiles are claimed in launch order through
 // p.tile_counter, so a tile only ever waits on tiles that are already running.
 // Status words carry the launch epoch, so no clearing pass is needed between
-// launches. F provides T, identity(), combine(a,b), load(p,i), load4(p,i,T*),
+// launches. Each poll inspects LB_WINDOWS x 32 predecessors at once, so the
+// frontier of inclusive prefixes advances 128 tiles per L2 round trip.
+//
+// 4-byte T: one 64-bit status word per tile, [epoch:30 | flag:2 | value:32],
+// written and read with single relaxed 64-bit accesses (no fence needed:
+// flag and value arrive together). 8-byte T: a 32-bit [epoch | flag] word plus
+// separate aggregate / inclusive arrays, ordered with fences.
+//
+// F provides T, identity(), combine(a,b), load(p,i), load4(p,i,T*),
 // store(p,i,v), store4(p,i,const T*), vec_ok(p); P provides n, tile_counter,
-// flags, aggs, incls, epoch, err.
+// status (u64, 4-byte T) or flags + aggs + incls (8-byte T), epoch, err.
+constexpr int LB_WINDOWS = 4;
+
+__device__ __forceinline__ u64 ld_relaxed_u64(const u64* p) {
+  u64 v;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_relaxed_u64(u64* p, u64 v) {
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+template <class T>
+__device__ __forceinline__ unsigned to_bits32(T v) {
+  union {
+    T t;
+    unsigned u;
+  } x;
+  x.t = v;
+  return x.u;
+}
+template <class T>
+__device__ __forceinline__ T from_bits32(unsigned u) {
+  union {
+    T t;
+    unsigned u;
+  } x;
+  x.u = u;
+  return x.t;
+}
+
+// Fold one window of 32 predecessors (lane l = tile pred - l, older to the
+// left) into prefix; returns true when an inclusive prefix ended the walk.
+template <class F>
+__device__ __forceinline__ bool fold_window(typename F::T v, bool is_p, typename F::T& prefix, int lane) {
+  typedef typename F::T T;
+  const unsigned pmask = __ballot_sync(FULL, is_p);
+  const int stop = pmask ? __ffs(pmask) - 1 : 31;
+  if (lane > stop) v = F::identity();
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    T y = __shfl_down_sync(FULL, v, o);
+    v = F::combine(y, v);
+  }
+  prefix = F::combine(__shfl_sync(FULL, v, 0), prefix);
+  return pmask != 0;
+}
+
 template <class F>
 __device__ __forceinline__ typename F::T lookback(const typename F::P& p, unsigned tile, typename F::T agg, int lane) {
   typedef typename F::T T;
-  const unsigned ep = p.epoch << 2;
-  if (tile == 0) {
-    if (lane == 0) {
-      p.incls[0] = agg;
-      __threadfence();
-      st_volatile(&p.flags[0], ep | 2u);
-    }
-    return F::identity();
-  }
-  if (lane == 0) {
-    p.aggs[tile] = agg;
-    __threadfence();
-    st_volatile(&p.flags[tile], ep | 1u);
-  }
   T prefix = F::identity();
-  long long pred = (long long)tile - 1;
   unsigned spins = 0;
-  while (true) {
-    const long long idx = pred - lane;
-    unsigned f;
+  if constexpr (sizeof(T) == 4) {
+    const u64 ep = (u64)p.epoch << 34;
+    const u64 FA = 1ull << 32, FP = 2ull << 32;
+    if (tile == 0) {
+      if (lane == 0) st_relaxed_u64(&p.status[0], ep | FP | to_bits32(agg));
+      return prefix;
+    }
+    if (lane == 0) st_relaxed_u64(&p.status[tile], ep | FA | to_bits32(agg));
+    long long pred = (long long)tile - 1;
+    const u64 sentinel = ep | FP | to_bits32(F::identity());
     while (true) {
-      f = idx >= 0 ? ld_volatile(&p.flags[idx]) : (ep | 2u);
-      const bool valid = (f & ~3u) == ep && (f & 3u) != 0u;
-      if (__all_sync(FULL, valid)) break;
-      if (++spins > LOOKBACK_SPIN_LIMIT) {
-        if (lane == 0) raise_error(p.err, ERR_LOOKBACK);
-        return F::identity();
-      }
-      __nanosleep(20);
-    }
-    __threadfence();
-    T v = F::identity();
-    if (idx >= 0) v = ((f & 3u) == 2u) ? ld_cg(&p.incls[idx]) : ld_cg(&p.aggs[idx]);
-    const unsigned pmask = __ballot_sync(FULL, (f & 3u) == 2u);
-    const int stop = pmask ? __ffs(pmask) - 1 : 31;
-    if (lane > stop) v = F::identity();
-    // Lane l holds tile pred-l: higher lanes are older, so fold right to left.
+      u64 s[LB_WINDOWS];
 #pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      T y = __shfl_down_sync(FULL, v, o);
-      v = F::combine(y, v);
+      for (int j = 0; j < LB_WINDOWS; ++j) {
+        const long long idx = pred - lane - 32 * j;
+        s[j] = idx >= 0 ? ld_relaxed_u64(&p.status[idx]) : sentinel;
+      }
+      while (true) {
+        bool ok = true;
+#pragma unroll
+        for (int j = 0; j < LB_WINDOWS; ++j) ok = ok && (s[j] >> 34) == (u64)p.epoch && ((s[j] >> 32) & 3u) != 0;
+        if (__all_sync(FULL, ok)) break;
+        if (++spins > LOOKBACK_SPIN_LIMIT) {
+          if (lane == 0) raise_error(p.err, ERR_LOOKBACK);
+          return F::identity();
+        }
+        __nanosleep(16);
+#pragma unroll
+        for (int j = 0; j < LB_WINDOWS; ++j) {
+          const long long idx = pred - lane - 32 * j;
+          const bool vj = (s[j] >> 34) == (u64)p.epoch && ((s[j] >> 32) & 3u) != 0;
+          if (!vj && idx >= 0) s[j] = ld_relaxed_u64(&p.status[idx]);
+        }
+      }
+      bool done = false;
+#pragma unroll
+      for (int j = 0; j < LB_WINDOWS; ++j) {
+        if (!done) done = fold_window<F>(from_bits32<T>((unsigned)s[j]), ((s[j] >> 32) & 3u) == 2u, prefix, lane);
+      }
+      if (done) break;
+      pred -= 32 * LB_WINDOWS;
     }
-    const T window = __shfl_sync(FULL, v, 0);
-    prefix = F::combine(window, prefix);
-    if (pmask) break;
-    pred -= 32;
+    if (lane == 0) st_relaxed_u64(&p.status[tile], ep | FP | to_bits32(F::combine(prefix, agg)));
+    return prefix;
+  } else {
+    const unsigned ep = ((unsigned)p.epoch) << 2;
+    if (tile == 0) {
+      if (lane == 0) {
+        p.incls[0] = agg;
+        __threadfence();
+        st_volatile(&p.flags[0], ep | 2u);
+      }
+      return prefix;
+    }
+    if (lane == 0) {
+      p.aggs[tile] = agg;
+      __threadfence();
+      st_volatile(&p.flags[tile], ep | 1u);
+    }
+    long long pred = (long long)tile - 1;
+    while (true) {
+      unsigned f[LB_WINDOWS];
+      while (true) {
+        bool ok = true;
+#pragma unroll
+        for (int j = 0; j < LB_WINDOWS; ++j) {
+          const long long idx = pred - lane - 32 * j;
+          f[j] = idx >= 0 ? ld_volatile(&p.flags[idx]) : (ep | 2u);
+          ok = ok && (f[j] & ~3u) == ep && (f[j] & 3u) != 0u;
+        }
+        if (__all_sync(FULL, ok)) break;
+        if (++spins > LOOKBACK_SPIN_LIMIT) {
+          if (lane == 0) raise_error(p.err, ERR_LOOKBACK);
+          return F::identity();
+        }
+        __nanosleep(16);
+      }
+      __threadfence();
+      bool done = false;
+#pragma unroll
+      for (int j = 0; j < LB_WINDOWS; ++j) {
+        if (!done) {
+          const long long idx = pred - lane - 32 * j;
+          T v = F::identity();
+          if (idx >= 0) v = ((f[j] & 3u) == 2u) ? ld_cg(&p.incls[idx]) : ld_cg(&p.aggs[idx]);
+          done = fold_window<F>(v, (f[j] & 3u) == 2u, prefix, lane);
+        }
+      }
+      if (done) break;
+      pred -= 32 * LB_WINDOWS;
+    }
+    if (lane == 0) {
+      p.incls[tile] = F::combine(prefix, agg);
+      __threadfence();
+      st_volatile(&p.flags[tile], ep | 2u);
+    }
+    return prefix;
   }
-  if (lane == 0) {
-    p.incls[tile] = F::combine(prefix, agg);
-    __threadfence();
-    st_volatile(&p.flags[tile], ep | 2u);
-  }
-  return prefix;
 }
 
 template <class F, int ITEMS>

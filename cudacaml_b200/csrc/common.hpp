@@ -2,6 +2,7 @@
 // by the runtime, the program executor and the NCCL wrappers.
 #pragma once
 #include <string>
+#include <vector>
 
 #include "../../include/ccb.h"
 #include "dyn.hpp"
@@ -21,6 +22,8 @@ int current_device();
 // NVRTC: compile `source` to an sm_100a CUBIN with the skeleton header on
 // the include path. Returns CCB_OK or CCB_ERR_COMPILE (log in `log`).
 int nvrtc_compile(const std::string& source, const std::string& name, std::string& cubin, std::string& log);
+int nvrtc_compile_opts(const std::string& source, const std::string& name, const std::vector<std::string>& extra,
+                       std::string& cubin, std::string& log);
 
 const char* skeleton_header();
 

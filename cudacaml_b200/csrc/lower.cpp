@@ -32,6 +32,7 @@
 #include <sstream>
 #include <stdexcept>
 #include <unordered_map>
+#include <cctype>
 #include <cstdio>
 #include <cstdlib>
 
@@ -1298,6 +1299,15 @@ class Lowerer {
     return f;
   }
 
+  // "_<graph name>" restricted to identifier characters: kernels of different
+  // graphs are told apart in profiles.
+  std::string kname_suffix() const {
+    std::string s = "_";
+    for (char ch : g.name)
+      if (s.size() < 40 && (std::isalnum((unsigned char)ch) || ch == '_')) s += ch;
+    return s.size() > 1 ? s : "";
+  }
+
   LaunchSpec& add_launch(const std::string& fn, const std::vector<Field>& fields) {
     LaunchSpec l;
     l.fn = fn;
@@ -1331,7 +1341,7 @@ class Lowerer {
   void emit_mapred(int gi) {
     Group& gr = groups[gi];
     const std::string F = "F" + std::to_string(gi);
-    const std::string fn = "ccb_mapreduce_" + std::to_string(gi);
+    const std::string fn = "ccb_mapreduce_" + std::to_string(gi) + kname_suffix();
     const int R = (int)gr.reds.size();
     const Dt acc = R ? gr.reds[0].dt : DT_F32;
     const char* at = dt_ctype(acc);
@@ -1365,7 +1375,14 @@ class Lowerer {
     src << "struct " << F << " {\n";
     emit_struct(fields);
     src << "  typedef " << at << " acc_t;\n";
+    std::vector<int> roots;
+    for (auto& s : gr.stores) roots.push_back(s.second);
+    for (auto& r : gr.reds) roots.push_back(r.var);
+    std::vector<int> direct = direct_loads(gr.ctx, roots);
     src << "  static constexpr int NRED = " << R << ";\n  static constexpr int VEC = 1;\n";
+    // Passes that stream data keep 4 vector steps in flight; compute-bound
+    // passes (Philox Monte Carlo) unroll 2 to keep the body small.
+    src << "  static constexpr int UNROLL = " << (direct.empty() ? 2 : 4) << ";\n";
     src << "  static constexpr bool TAIL = " << (gr.tails.empty() ? "false" : "true") << ";\n";
     // identity / combine
     src << "  static __device__ __forceinline__ acc_t identity(int r) {\n    switch (r) {\n";
@@ -1390,10 +1407,6 @@ class Lowerer {
     }
     src << "    }\n    return a;\n  }\n";
     // vec_ok
-    std::vector<int> roots;
-    for (auto& s : gr.stores) roots.push_back(s.second);
-    for (auto& r : gr.reds) roots.push_back(r.var);
-    std::vector<int> direct = direct_loads(gr.ctx, roots);
     src << "  static __device__ __forceinline__ bool vec_ok(const P& p) {\n    return true";
     for (int b : direct) src << " && ccb::aligned16(p.b" << b << ")";
     for (auto& s : gr.stores) src << " && ccb::aligned16(p.o" << s.first << ")";
@@ -1456,8 +1469,12 @@ class Lowerer {
       }
     }
     src << "  }\n};\n";
-    src << "extern \"C\" __global__ void __launch_bounds__(256) " << fn << "(const " << F << "::P p) { ccb::map_reduce<" << F
-        << ">(p); }\n\n";
+    // Ask for 8 resident blocks (32 registers); the program builder drops the
+    // bound for a kernel whose ptxas report shows spills (CCB_MINB_<pass>=1).
+    const std::string mb = "CCB_MINB_" + fn.substr(14);
+    src << "#ifndef " << mb << "\n#define " << mb << " 8\n#endif\n";
+    src << "extern \"C\" __global__ void __launch_bounds__(256, " << mb << ") " << fn << "(const " << F
+        << "::P p) { ccb::map_reduce<" << F << ">(p); }\n\n";
     LaunchSpec& l = add_launch(fn, fields);
     l.mode = GM_PERSISTENT;
     l.work = gr.domain;
@@ -1534,7 +1551,7 @@ class Lowerer {
     const char* T = dt_ctype(x.dt);
     const std::string F = "F" + std::to_string(gi);
     const bool flat = gr.kind == G_SCAN_FLAT;
-    const std::string fn = std::string(flat ? "ccb_scan_" : "ccb_scanrows_") + std::to_string(gi);
+    const std::string fn = std::string(flat ? "ccb_scan_" : "ccb_scanrows_") + std::to_string(gi) + kname_suffix();
     node_buf[t] = add_buf("t" + std::to_string(x.uid), dt_size(x.dt), x.numel, BR_NODE, t, false);
     const int items = dt_size(x.dt) == 4 ? 16 : 8;
     const int64_t tile = 256 * items;
@@ -1548,9 +1565,14 @@ class Lowerer {
     if (flat) {
       const std::string pre = "g" + std::to_string(gi);
       fields.push_back(buf_field("unsigned* tile_counter", add_buf(pre + "_tiles", 4, 1, BR_SCRATCH, -1, true)));
-      fields.push_back(buf_field("unsigned* flags", add_buf(pre + "_flags", 4, ntiles, BR_SCRATCH, -1, true)));
-      fields.push_back(buf_field(std::string(T) + "* aggs", add_buf(pre + "_aggs", dt_size(x.dt), ntiles, BR_SCRATCH, -1, false)));
-      fields.push_back(buf_field(std::string(T) + "* incls", add_buf(pre + "_incls", dt_size(x.dt), ntiles, BR_SCRATCH, -1, false)));
+      if (dt_size(x.dt) == 4) {
+        // one packed [epoch | flag | value] word per tile
+        fields.push_back(buf_field("unsigned long long* status", add_buf(pre + "_status", 8, ntiles, BR_SCRATCH, -1, true)));
+      } else {
+        fields.push_back(buf_field("unsigned* flags", add_buf(pre + "_flags", 4, ntiles, BR_SCRATCH, -1, true)));
+        fields.push_back(buf_field(std::string(T) + "* aggs", add_buf(pre + "_aggs", dt_size(x.dt), ntiles, BR_SCRATCH, -1, false)));
+        fields.push_back(buf_field(std::string(T) + "* incls", add_buf(pre + "_incls", dt_size(x.dt), ntiles, BR_SCRATCH, -1, false)));
+      }
       Field ep;
       ep.decl = "unsigned long long epoch";
       ep.slot.kind = SL_EPOCH;
@@ -1592,7 +1614,7 @@ class Lowerer {
     const GTensor& x = g.ts[t];
     const char* T = dt_ctype(x.dt);
     const std::string F = "F" + std::to_string(gi);
-    const std::string fn = "ccb_redrows_" + std::to_string(gi);
+    const std::string fn = "ccb_redrows_" + std::to_string(gi) + kname_suffix();
     node_buf[t] = add_buf("t" + std::to_string(x.uid), dt_size(x.dt), x.numel, BR_NODE, t, false);
     std::vector<Field> fields;
     for (int b : loads_of(gr.ctx)) fields.push_back(in_field(b));
@@ -1623,7 +1645,7 @@ class Lowerer {
     const GTensor& x = g.ts[t];
     const char* T = dt_ctype(x.dt);
     const std::string F = "F" + std::to_string(gi);
-    const std::string fn = "ccb_scatter_" + std::to_string(gi);
+    const std::string fn = "ccb_scatter_" + std::to_string(gi) + kname_suffix();
     node_buf[t] = add_buf("t" + std::to_string(x.uid), dt_size(x.dt), x.numel, BR_NODE, t, false);
     OpSpec z;
     z.kind = OP_ZERO;
@@ -1668,7 +1690,7 @@ class Lowerer {
     const GTensor& x = g.ts[t];
     const char* T = dt_ctype(x.dt);
     const std::string F = "F" + std::to_string(gi);
-    const std::string fn = "ccb_matmul_" + std::to_string(gi);
+    const std::string fn = "ccb_matmul_" + std::to_string(gi) + kname_suffix();
     const int64_t M = x.shape[0], N = x.shape[1], K = g.ts[x.dep0].shape[1];
     node_buf[t] = add_buf("t" + std::to_string(x.uid), dt_size(x.dt), x.numel, BR_NODE, t, false);
     std::vector<Field> fields;

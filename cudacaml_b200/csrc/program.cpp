@@ -3,6 +3,7 @@
 // Backend_cuda.compile_on (lib/backend_cuda/cudacaml_backend_cuda.ml:30-43) and
 // Executor (lib/backend_cuda/executor.ml:72-244).
 #include <algorithm>
+#include <cstdlib>
 #include <cstring>
 #include <memory>
 #include <unordered_map>
@@ -138,6 +139,51 @@ int issue(Program& P, int lane, const void* const* h_in, void* const* h_out, con
 
 Program* as_prog(ccb_program_t p) { return static_cast<Program*>(p); }
 
+// Kernels whose ptxas report (NVRTC log with -v) shows spill stores.
+std::vector<std::string> spilling_kernels(const std::string& log) {
+  std::vector<std::string> out;
+  size_t pos = 0;
+  const std::string tag = "Function properties for ";
+  while ((pos = log.find(tag, pos)) != std::string::npos) {
+    pos += tag.size();
+    const size_t eol = log.find('\n', pos);
+    const std::string fn = log.substr(pos, eol - pos);
+    const size_t next = log.find('\n', eol + 1);
+    const std::string props = log.substr(eol + 1, next - eol - 1);
+    const size_t sp = props.find(" bytes spill stores");
+    if (sp != std::string::npos) {
+      size_t b = props.rfind(',', sp);
+      b = (b == std::string::npos) ? 0 : b + 1;
+      if (std::atol(props.substr(b, sp - b).c_str()) > 0) out.push_back(fn);
+    }
+    pos = eol;
+  }
+  return out;
+}
+
+// Compile with the occupancy bounds the generator asked for; recompile
+// without the bound for any map-reduce pass that would spill. CCB_MINB=<n>
+// in the environment forces one bound for every pass (a tuning aid).
+int compile_tuned(const Lowered& L, std::string& cubin, std::string& log) {
+  const std::string name = L.name.empty() ? "ccb" : L.name;
+  std::vector<std::string> opts = {"--ptxas-options=-v"};
+  if (const char* f = std::getenv("CCB_MINB")) {
+    for (const auto& l : L.launches)
+      if (l.fn.rfind("ccb_mapreduce_", 0) == 0) opts.push_back("-DCCB_MINB_" + l.fn.substr(14) + "=" + f);
+    return nvrtc_compile_opts(L.source, name, opts, cubin, log);
+  }
+  CCB_TRY(nvrtc_compile_opts(L.source, name, opts, cubin, log));
+  std::vector<std::string> sp = spilling_kernels(log);
+  bool again = false;
+  for (const auto& fn : sp)
+    if (fn.rfind("ccb_mapreduce_", 0) == 0) {
+      opts.push_back("-DCCB_MINB_" + fn.substr(14) + "=1");
+      again = true;
+    }
+  if (!again) return CCB_OK;
+  return nvrtc_compile_opts(L.source, name, opts, cubin, log);
+}
+
 int need_device(Program* P) {
   if (!P) return fail(CCB_ERR_INVALID, "null program");
   if (P->device < 0) return fail(CCB_ERR_INVALID, "program was lowered without a device (ccb_program_lower)");
@@ -183,7 +229,7 @@ int ccb_program_create(const char* graph, int device, int lanes, ccb_program_t* 
     return code;
   };
   std::string cubin, log;
-  rc = nvrtc_compile(P->L.source, P->L.name.empty() ? "ccb" : P->L.name, cubin, log);
+  rc = compile_tuned(P->L, cubin, log);
   if (rc != CCB_OK) return cleanup(rc);
   CUresult r = d.cuModuleLoadData(&P->mod, cubin.data());
   if (r != CUDA_SUCCESS) return cleanup(cu_fail(r, "cuModuleLoadData"));

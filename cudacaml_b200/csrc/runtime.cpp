@@ -93,6 +93,11 @@ int current_device() { return g_current < 0 ? 0 : g_current; }
 static int ensure_current() { return ensure_context(current_device()); }
 
 int nvrtc_compile(const std::string& source, const std::string& name, std::string& cubin, std::string& log) {
+  return nvrtc_compile_opts(source, name, {}, cubin, log);
+}
+
+int nvrtc_compile_opts(const std::string& source, const std::string& name, const std::vector<std::string>& extra,
+                       std::string& cubin, std::string& log) {
   const Nvrtc& r = nvrtc();
   if (!r.ok) return fail(CCB_ERR_COMPILE, "NVRTC unavailable: " + r.why);
   nvrtcProgram prog;
@@ -100,8 +105,9 @@ int nvrtc_compile(const std::string& source, const std::string& name, std::strin
   const char* hdr_name[] = {"ccb_skel.cuh"};
   nvrtcResult rc = r.nvrtcCreateProgram(&prog, source.c_str(), (name + ".cu").c_str(), 1, hdr_src, hdr_name);
   if (rc != NVRTC_SUCCESS) return fail(CCB_ERR_COMPILE, std::string("nvrtcCreateProgram: ") + r.nvrtcGetErrorString(rc));
-  const char* opts[] = {"--gpu-architecture=sm_100a", "-std=c++17", "-lineinfo", "--fmad=true"};
-  rc = r.nvrtcCompileProgram(prog, 4, opts);
+  std::vector<const char*> opts = {"--gpu-architecture=sm_100a", "-std=c++17", "-lineinfo", "--fmad=true"};
+  for (auto& e : extra) opts.push_back(e.c_str());
+  rc = r.nvrtcCompileProgram(prog, (int)opts.size(), opts.data());
   size_t lsz = 0;
   r.nvrtcGetProgramLogSize(prog, &lsz);
   log.assign(lsz, '\0');

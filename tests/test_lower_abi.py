@@ -54,7 +54,7 @@ def test_examples_compile_for_sm100a(prog):
 
 def test_config_graphs_compile():
     for g in (X.call_greeks(1 << 20, F32), X.call_greeks(1 << 20, F64), X.reduce_scan_flat(1 << 20, F32),
-              X.reduce_scan_flat(1 << 20, I32), X.rows(64, 4096), X.rows(100, 16), X.scatter(1000, 7),
+              X.reduce_scan_flat(1 << 20, I32), X.reduce_scan_flat(1 << 20, F64), X.rows(64, 4096), X.rows(100, 16), X.scatter(1000, 7),
               X.gather(1000, 100), X.saxpy(1000, 2.0, F64)):
         assert nvrtc_ok(B.lower_info(g)["source"], g.name) > 0
 
@@ -79,7 +79,7 @@ def test_structure():
     a = D.param("a", F64, (4, 1 << 14))
     b = D.param("b", F64, (1 << 14, 4))
     assert k(Graph("mm", [("c", D.matmul(a, b))])) == 1
-    assert "ccb_mapreduce_0" in B.lower_info(Graph("mm", [("c", D.matmul(a, b))]))["source"]
+    assert "ccb_mapreduce_0_mm" in B.lower_info(Graph("mm", [("c", D.matmul(a, b))]))["source"]
 
 
 def test_plan_mentions_params_and_outputs():
