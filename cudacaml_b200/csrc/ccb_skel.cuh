@@ -420,6 +420,241 @@ __device__ __forceinline__ void scan_flat(const typename F::P& p) {
   if (threadIdx.x == 0 && tile == gridDim.x - 1) atomicExch(p.tile_counter, 0u);
 }
 
+// ---------------------------------------------------------------- staged flat scan (TMA)
+// Persistent single-pass scan of a 4-byte source buffer. Each CTA keeps three
+// 32 KiB tiles in flight in shared memory: one arriving by a 1-D bulk async
+// copy (cp.async.bulk, the TMA engine; never multicast), one whose aggregate
+// it publishes, and one it finishes. Publishing tile k's aggregate before
+// walking back for tile k-1 gives every predecessor a full iteration to
+// publish, so the walk rarely waits; the walk itself overlaps the next bulk
+// load. Tiles are claimed dynamically in order (forward progress as in
+// scan_flat). The tile aggregate folds each thread's strided chunks, i.e. it
+// assumes a commutative combiner, as the reference's device reduction does;
+// the scanned values themselves are combined in order.
+// F provides T (4 bytes), identity(), combine(a,b), src(p), dst(p); P provides
+// n, tile_counter, done_counter, status, epoch, err.
+constexpr unsigned ERR_TMA = 8u;
+constexpr unsigned MBAR_SPIN_LIMIT = 1u << 22;
+
+__device__ __forceinline__ unsigned smem_u32(const void* ptr) { return (unsigned)__cvta_generic_to_shared(ptr); }
+__device__ __forceinline__ void mbar_init(u64* bar, unsigned count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_fence_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+__device__ __forceinline__ void mbar_expect_tx(u64* bar, unsigned bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, unsigned bytes, u64* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ bool mbar_try_wait(u64* bar, unsigned parity) {
+  unsigned ok;
+  asm volatile(
+      "{\n .reg .pred q;\n mbarrier.try_wait.parity.shared::cta.b64 q, [%1], %2;\n selp.u32 %0, 1, 0, q;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait for a bulk copy; on timeout raise ERR_TMA and keep waiting, again
+// bounded, so the copy in flight lands before the CTA moves on.
+__device__ __forceinline__ void mbar_wait(u64* bar, unsigned parity, unsigned* err) {
+  for (unsigned it = 0; it < MBAR_SPIN_LIMIT; ++it)
+    if (mbar_try_wait(bar, parity)) return;
+  if (threadIdx.x == 0) raise_error(err, ERR_TMA);
+  for (unsigned it = 0; it < MBAR_SPIN_LIMIT; ++it)
+    if (mbar_try_wait(bar, parity)) return;
+}
+
+template <class F>
+__device__ __forceinline__ void publish_aggregate(const typename F::P& p, unsigned tile, typename F::T agg) {
+  const u64 ep = (u64)p.epoch << 34;
+  st_relaxed_u64(&p.status[tile], ep | (tile == 0 ? (2ull << 32) : (1ull << 32)) | to_bits32(agg));
+}
+
+// Walk back from `tile` (whose aggregate is published) to the nearest
+// inclusive prefix; publish tile's own inclusive prefix; return the exclusive
+// prefix. Warp-wide.
+template <class F>
+__device__ __forceinline__ typename F::T walk_back(const typename F::P& p, unsigned tile, typename F::T agg, int lane) {
+  typedef typename F::T T;
+  T prefix = F::identity();
+  if (tile == 0) return prefix;
+  const u64 ep = (u64)p.epoch << 34;
+  const u64 sentinel = ep | (2ull << 32) | to_bits32(F::identity());
+  long long pred = (long long)tile - 1;
+  unsigned spins = 0;
+  while (true) {
+    u64 s[LB_WINDOWS];
+#pragma unroll
+    for (int j = 0; j < LB_WINDOWS; ++j) {
+      const long long idx = pred - lane - 32 * j;
+      s[j] = idx >= 0 ? ld_relaxed_u64(&p.status[idx]) : sentinel;
+    }
+    bool done = false;
+#pragma unroll
+    for (int j = 0; j < LB_WINDOWS; ++j) {
+      if (done) break;
+      // this window must be fully published before it can be folded
+      while (!__all_sync(FULL, (s[j] >> 34) == (u64)p.epoch && ((s[j] >> 32) & 3u) != 0)) {
+        if (++spins > LOOKBACK_SPIN_LIMIT) {
+          if (lane == 0) raise_error(p.err, ERR_LOOKBACK);
+          return F::identity();
+        }
+        __nanosleep(16);
+        const long long idx = pred - lane - 32 * j;
+        if (idx >= 0) s[j] = ld_relaxed_u64(&p.status[idx]);
+      }
+      done = fold_window<F>(from_bits32<T>((unsigned)s[j]), ((s[j] >> 32) & 3u) == 2u, prefix, lane);
+    }
+    if (done) break;
+    pred -= 32 * LB_WINDOWS;
+  }
+  if (lane == 0) st_relaxed_u64(&p.status[tile], ep | (2ull << 32) | to_bits32(F::combine(prefix, agg)));
+  return prefix;
+}
+
+template <class F>
+__device__ __forceinline__ void scan_flat_staged(const typename F::P& p) {
+  typedef typename F::T T;
+  static_assert(sizeof(T) == 4, "staged scan is for 4-byte element types");
+  constexpr int BLOCK = 256, NBUF = 3, STRIPS = 8, STRIP = BLOCK * 4, TILE = STRIP * STRIPS;
+  constexpr int NW = BLOCK / 32;
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  T* buf = reinterpret_cast<T*>(smem_raw);
+  u64* bars = reinterpret_cast<u64*>(smem_raw + (size_t)NBUF * TILE * sizeof(T));
+  __shared__ int s_tile[NBUF];
+  __shared__ int s_tma[NBUF];
+  __shared__ T s_warp[NW + 1];
+  __shared__ T s_agg;
+  __shared__ T s_prefix;
+  const long long n = p.n;
+  const long long ntiles = (n + TILE - 1) / TILE;
+  const T* src = F::src(p);
+  T* dst = F::dst(p);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const bool src_aligned = aligned16(src);
+  const bool dst_aligned = aligned16(dst);
+  unsigned parity[NBUF] = {0u, 0u, 0u};
+
+  // thread 0: claim the next tile into buffer b and start its bulk load
+  auto claim = [&](int b) {
+    const unsigned t = atomicAdd(p.tile_counter, 1u);
+    const bool ok = (long long)t < ntiles;
+    s_tile[b] = ok ? (int)t : -1;
+    s_tma[b] = 0;
+    if (ok) {
+      const long long base = (long long)t * TILE;
+      if (src_aligned && base + TILE <= n) {
+        s_tma[b] = 1;
+        fence_proxy_async_smem();
+        mbar_expect_tx(&bars[b], TILE * (unsigned)sizeof(T));
+        bulk_load(buf + (size_t)b * TILE, src + base, TILE * (unsigned)sizeof(T), &bars[b]);
+      }
+    }
+  };
+
+  if (tid == 0) {
+    for (int b = 0; b < NBUF; ++b) mbar_init(&bars[b], 1);
+    mbar_fence_init();
+    claim(0);
+    claim(1);
+  }
+  __syncthreads();
+
+  T agg_prev = F::identity();
+  for (int k = 0;; ++k) {
+    const int bc = k % NBUF;            // tile k: publish its aggregate
+    const int bp = (k + NBUF - 1) % NBUF;  // tile k-1: finish it
+    const int tc = s_tile[bc];
+    const int tp = k > 0 ? s_tile[bp] : -1;
+    if (tc < 0 && tp < 0) break;
+    T agg_cur = F::identity();
+    if (tc >= 0) {
+      const long long base = (long long)tc * TILE;
+      T* b = buf + (size_t)bc * TILE;
+      if (s_tma[bc]) {
+        mbar_wait(&bars[bc], parity[bc], p.err);
+        parity[bc] ^= 1u;
+      } else {
+        for (int e = tid; e < TILE; e += BLOCK) b[e] = (base + e < n) ? src[base + e] : F::identity();
+        __syncthreads();
+      }
+      // tile aggregate: each thread folds its strided 16-byte chunks
+      T a = F::identity();
+#pragma unroll
+      for (int sI = 0; sI < STRIPS; ++sI) {
+        const V4<T> v = *reinterpret_cast<const V4<T>*>(b + (sI * BLOCK + tid) * 4);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) a = F::combine(a, v.v[q]);
+      }
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) a = F::combine(a, __shfl_down_sync(FULL, a, o));
+      if (lane == 0) s_warp[warp] = a;
+      __syncthreads();
+      if (warp == 0) {
+        T v = lane < NW ? s_warp[lane] : F::identity();
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) v = F::combine(v, __shfl_down_sync(FULL, v, o));
+        if (lane == 0) {
+          s_agg = v;
+          publish_aggregate<F>(p, (unsigned)tc, v);
+        }
+      }
+      __syncthreads();
+      agg_cur = s_agg;
+    }
+    if (tp >= 0) {
+      if (warp == 0) {
+        const T pre = walk_back<F>(p, (unsigned)tp, agg_prev, lane);
+        if (lane == 0) s_prefix = pre;
+      }
+      __syncthreads();
+      T carry = s_prefix;
+      const long long base = (long long)tp * TILE;
+      const T* b = buf + (size_t)bp * TILE;
+#pragma unroll 1
+      for (int sI = 0; sI < STRIPS; ++sI) {
+        const int e0 = (sI * BLOCK + tid) * 4;
+        V4<T> v = *reinterpret_cast<const V4<T>*>(b + e0);
+#pragma unroll
+        for (int q = 1; q < 4; ++q) v.v[q] = F::combine(v.v[q - 1], v.v[q]);
+        T total;
+        const T excl = block_scan_excl<F, BLOCK>(v.v[3], &total, s_warp);
+        const T pre = F::combine(carry, excl);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) v.v[q] = F::combine(pre, v.v[q]);
+        const long long g = base + e0;
+        if (dst_aligned && g + 4 <= n) {
+          st4(dst + g, v);
+        } else {
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            if (g + q < n) dst[g + q] = v.v[q];
+        }
+        carry = F::combine(carry, total);
+        __syncthreads();  // s_warp is reused by the next strip
+      }
+    }
+    // buffer bp is free (or was never used): claim tile k+2 into it
+    if (tid == 0) claim((k + 2) % NBUF);
+    __syncthreads();
+    agg_prev = agg_cur;
+  }
+  // the last CTA out rearms the counters for the next launch
+  if (tid == 0) {
+    __threadfence();
+    if (atomicAdd(p.done_counter, 1u) == gridDim.x - 1) {
+      *p.tile_counter = 0u;
+      *p.done_counter = 0u;
+      __threadfence();
+    }
+  }
+}
+
 // ---------------------------------------------------------------- rows
 // Row kernels over [rows; n] (last axis). F provides T, identity(),
 // combine(a,b), load(p,i), load4(p,i,T*), vec_ok(p) and, for reductions,

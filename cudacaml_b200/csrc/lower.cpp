@@ -1544,9 +1544,79 @@ class Lowerer {
     (void)T;
   }
 
+  // The staged (TMA) flat scan: a 4-byte scan whose source is a buffer read
+  // straight at the element index.
+  bool staged_scan_source(const Group& gr, int t, int& src_buf) const {
+    const GTensor& x = g.ts[t];
+    if (gr.kind != G_SCAN_FLAT || dt_size(x.dt) != 4) return false;
+    const KN& k = gr.ctx.n[gr.val];
+    if (k.op != K_LOAD || k.a != gr.ctx.index_node) return false;
+    src_buf = k.buf;
+    return true;
+  }
+
+  void emit_scan_staged(int gi, int srcb) {
+    Group& gr = groups[gi];
+    const int t = gr.root;
+    const GTensor& x = g.ts[t];
+    const char* T = dt_ctype(x.dt);
+    const std::string F = "F" + std::to_string(gi);
+    const std::string fn = "ccb_scanstaged_" + std::to_string(gi) + kname_suffix();
+    node_buf[t] = add_buf("t" + std::to_string(x.uid), dt_size(x.dt), x.numel, BR_NODE, t, false);
+    constexpr int64_t TILE = 8192;
+    const int64_t ntiles = std::max<int64_t>(1, (gr.domain + TILE - 1) / TILE);
+    const std::string pre = "g" + std::to_string(gi);
+    std::vector<Field> fields;
+    fields.push_back(in_field(srcb));
+    fields.push_back(out_field(t));
+    fields.push_back(buf_field("unsigned* err", out->err_buf));
+    fields.push_back(i64_field("n", gr.domain));
+    fields.push_back(buf_field("unsigned* tile_counter", add_buf(pre + "_tiles", 4, 1, BR_SCRATCH, -1, true)));
+    fields.push_back(buf_field("unsigned* done_counter", add_buf(pre + "_done", 4, 1, BR_SCRATCH, -1, true)));
+    fields.push_back(buf_field("unsigned long long* status", add_buf(pre + "_status", 8, ntiles, BR_SCRATCH, -1, true)));
+    Field ep;
+    ep.decl = "unsigned long long epoch";
+    ep.slot.kind = SL_EPOCH;
+    fields.push_back(ep);
+    src << "// staged flat scan " << gi << " over " << gr.domain << " elements (" << ntiles << " tiles of " << TILE << ")\n";
+    src << "struct " << F << " {\n";
+    emit_struct(fields);
+    src << "  typedef " << T << " T;\n";
+    {
+      std::ostringstream tmp;
+      KCtx c;
+      int iv = init_knode(c, t);
+      Emitter e(c, tmp);
+      std::string v = e.val(iv);
+      src << "  static __device__ __forceinline__ T identity() {\n" << tmp.str() << "    return " << v << ";\n  }\n";
+    }
+    src << "  static __device__ __forceinline__ T combine(T a, T b) {\n";
+    if (is_plain_add(t))
+      src << "    return " << bin_text(x.dt, B_ADD, "a", "b") << "; }\n";
+    else
+      src << combine_body(t, "    ");
+    src << "  static __device__ __forceinline__ const T* src(const P& p) { return p.b" << srcb << "; }\n";
+    src << "  static __device__ __forceinline__ T* dst(const P& p) { return p.o" << t << "; }\n";
+    src << "};\n";
+    src << "extern \"C\" __global__ void __launch_bounds__(256) " << fn << "(const " << F << "::P p) { ccb::scan_flat_staged<" << F
+        << ">(p); }\n\n";
+    LaunchSpec& l = add_launch(fn, fields);
+    l.mode = GM_PERSISTENT;
+    l.work = ntiles;
+    l.per_block = 1;
+    l.smem = (int)(3 * TILE * 4 + 64);
+  }
+
   void emit_scan(int gi) {
     Group& gr = groups[gi];
     const int t = gr.root;
+    {
+      int srcb = -1;
+      if (staged_scan_source(gr, t, srcb)) {
+        emit_scan_staged(gi, srcb);
+        return;
+      }
+    }
     const GTensor& x = g.ts[t];
     const char* T = dt_ctype(x.dt);
     const std::string F = "F" + std::to_string(gi);

@@ -79,6 +79,7 @@ struct LaunchSpec {
   int64_t per_block = 1;       // persistent: items one block iteration covers
   int64_t max_grid = 1 << 30;  // persistent: cap (scratch is sized for it)
   int block = 256;
+  int smem = 0;  // dynamic shared memory bytes
   std::vector<Slot> slots;
 };
 

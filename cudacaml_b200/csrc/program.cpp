@@ -43,6 +43,7 @@ int lane_check(Program& P, int lane) {
   if (e & 1u) m += " gather index out of bounds;";
   if (e & 2u) m += " scatter_add index out of bounds;";
   if (e & 4u) m += " scan look-back wait gave up (bounded spin exhausted);";
+  if (e & 8u) m += " bulk-copy (TMA) wait gave up (bounded spin exhausted);";
   *P.lanes[lane].host_err = 0;
   return fail(CCB_ERR_DEVICE_CHECK, m);
 }
@@ -119,7 +120,8 @@ int issue(Program& P, int lane, const void* const* h_in, void* const* h_out, con
       blk[s] = sl.kind == SL_BUF ? (uint64_t)ptr[sl.buf] : sl.kind == SL_I64 ? (uint64_t)sl.val : ln.epoch;
     }
     void* args[] = {blk.data()};
-    CCB_CU(d.cuLaunchKernel(P.fns[op.launch], P.gx[op.launch], P.gy[op.launch], 1, l.block, 1, 1, 0, stream, args, nullptr));
+    CCB_CU(d.cuLaunchKernel(P.fns[op.launch], P.gx[op.launch], P.gy[op.launch], 1, l.block, 1, 1, (unsigned)l.smem, stream,
+                            args, nullptr));
   }
   for (auto& c : copies) {
     const int64_t n = buf_bytes(P.L.bufs[c.second]);
@@ -243,9 +245,13 @@ int ccb_program_create(const char* graph, int device, int lanes, ccb_program_t* 
     if (r != CUDA_SUCCESS) return cleanup(cu_fail(r, "cuModuleGetFunction"));
     P->fns.push_back(f);
     int64_t gx = l.gx, gy = l.gy;
+    if (l.smem > 48 * 1024) {
+      r = d.cuFuncSetAttribute(f, CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES, l.smem);
+      if (r != CUDA_SUCCESS) return cleanup(cu_fail(r, "cuFuncSetAttribute(max dynamic shared memory)"));
+    }
     if (l.mode == GM_PERSISTENT) {
       int occ = 1;
-      d.cuOccupancyMaxActiveBlocksPerMultiprocessor(&occ, f, l.block, 0);
+      d.cuOccupancyMaxActiveBlocksPerMultiprocessor(&occ, f, l.block, (size_t)l.smem);
       const int64_t cap = std::min<int64_t>(l.max_grid, (int64_t)std::max(1, sms) * std::max(1, occ));
       const int64_t want = (l.work + l.per_block - 1) / std::max<int64_t>(1, l.per_block);
       gx = std::max<int64_t>(1, std::min(want, cap));

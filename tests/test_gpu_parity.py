@@ -323,3 +323,27 @@ def test_s19_multi_same_device_and_counter_split():
     pm = M.mean_scalar([dict(o)["price"] for o in per])
     t.release()
     assert abs(pm - p1) <= 1e-9 * (1 + abs(p1))
+
+
+@pytest.mark.parametrize("n", [1, 4, 8191, 8192, 8193, 3 * 8192 + 5, 1 << 16, (1 << 20) + 7])
+def test_flat_scan_tile_edges_i32_exact(n):
+    # the staged scan's 8192-element tiles: ragged last tiles, one-tile and
+    # multi-tile cases, bit-exact for I32 (wrapping add)
+    x = (X.philox_word0(9, n) & 1023).astype(np.int32)
+    g = X.scan_flat(n, I32)
+    got = dict(cuda.run(cuda.compile(g), [("x", Value.of_array(I32, (n,), x))]))["p"].data
+    assert np.array_equal(got, np.cumsum(x, dtype=np.int64).astype(np.int32))
+    diff(g, [("x", Value.of_array(I32, (n,), x))], tol=0.0)
+
+
+def test_flat_scan_max_and_repeat_runs():
+    # a non-add combiner through the staged path, and repeated launches of one
+    # program (epoch-tagged status words, counters re-armed by the kernel)
+    n = 100_003
+    x = X.philox_normal(12, n)
+    v = D.param("x", F32, (n,))
+    g = Graph("m", [("p", D.scan(D.max, D.const(F32, -3e38), v))])
+    c = cuda.compile(g)
+    for _ in range(3):
+        got = dict(cuda.run(c, [("x", Value.of_array(F32, (n,), x))]))["p"].data
+        assert np.array_equal(got, np.maximum.accumulate(x))
