@@ -523,13 +523,14 @@ __device__ __forceinline__ void scan_flat_staged(const typename F::P& p) {
   static_assert(sizeof(T) == 4, "staged scan is for 4-byte element types");
   constexpr int BLOCK = 256, NBUF = 3, STRIPS = 8, STRIP = BLOCK * 4, TILE = STRIP * STRIPS;
   constexpr int NW = BLOCK / 32;
+  static_assert(STRIPS * NW == 64, "the chunk-total scan folds 2 entries per lane");
   extern __shared__ __align__(128) unsigned char smem_raw[];
   T* buf = reinterpret_cast<T*>(smem_raw);
   u64* bars = reinterpret_cast<u64*>(smem_raw + (size_t)NBUF * TILE * sizeof(T));
   __shared__ int s_tile[NBUF];
   __shared__ int s_tma[NBUF];
-  __shared__ T s_warp[NW + 1];
-  __shared__ T s_agg;
+  __shared__ T s_ws[STRIPS * NW];   // warp totals per strip, (strip, warp) order
+  __shared__ T s_off[STRIPS * NW];  // their exclusive prefixes within the tile
   __shared__ T s_prefix;
   const long long n = p.n;
   const long long ntiles = (n + TILE - 1) / TILE;
@@ -565,14 +566,20 @@ __device__ __forceinline__ void scan_flat_staged(const typename F::P& p) {
   }
   __syncthreads();
 
+  // Thread tid owns chunk (strip s, tid): elements [s*STRIP + 4*tid, +4) of
+  // the tile, so chunk order (s, tid) is element order.
   T agg_prev = F::identity();
+  T off_prev[STRIPS];
+#pragma unroll
+  for (int sI = 0; sI < STRIPS; ++sI) off_prev[sI] = F::identity();
   for (int k = 0;; ++k) {
-    const int bc = k % NBUF;            // tile k: publish its aggregate
-    const int bp = (k + NBUF - 1) % NBUF;  // tile k-1: finish it
+    const int bc = k % NBUF;               // tile k: scan offsets + aggregate
+    const int bp = (k + NBUF - 1) % NBUF;  // tile k-1: prefix + store
     const int tc = s_tile[bc];
     const int tp = k > 0 ? s_tile[bp] : -1;
     if (tc < 0 && tp < 0) break;
     T agg_cur = F::identity();
+    T off_cur[STRIPS];
     if (tc >= 0) {
       const long long base = (long long)tc * TILE;
       T* b = buf + (size_t)bc * TILE;
@@ -583,29 +590,32 @@ __device__ __forceinline__ void scan_flat_staged(const typename F::P& p) {
         for (int e = tid; e < TILE; e += BLOCK) b[e] = (base + e < n) ? src[base + e] : F::identity();
         __syncthreads();
       }
-      // tile aggregate: each thread folds its strided 16-byte chunks
-      T a = F::identity();
+      T excl_w[STRIPS];
 #pragma unroll
       for (int sI = 0; sI < STRIPS; ++sI) {
-        const V4<T> v = *reinterpret_cast<const V4<T>*>(b + (sI * BLOCK + tid) * 4);
-#pragma unroll
-        for (int q = 0; q < 4; ++q) a = F::combine(a, v.v[q]);
+        const V4<T> v = *reinterpret_cast<const V4<T>*>(b + sI * STRIP + 4 * tid);
+        const T tot = F::combine(F::combine(F::combine(v.v[0], v.v[1]), v.v[2]), v.v[3]);
+        const T incl = warp_scan_incl<F>(tot, lane);
+        T ex = __shfl_up_sync(FULL, incl, 1);
+        excl_w[sI] = lane == 0 ? F::identity() : ex;
+        if (lane == 31) s_ws[sI * NW + warp] = incl;
       }
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) a = F::combine(a, __shfl_down_sync(FULL, a, o));
-      if (lane == 0) s_warp[warp] = a;
       __syncthreads();
       if (warp == 0) {
-        T v = lane < NW ? s_warp[lane] : F::identity();
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) v = F::combine(v, __shfl_down_sync(FULL, v, o));
-        if (lane == 0) {
-          s_agg = v;
-          publish_aggregate<F>(p, (unsigned)tc, v);
-        }
+        // 64 warp totals in (strip, warp) order, two per lane
+        const T w0 = s_ws[2 * lane], w1 = s_ws[2 * lane + 1];
+        const T pair = F::combine(w0, w1);
+        const T incl = warp_scan_incl<F>(pair, lane);
+        T ex = __shfl_up_sync(FULL, incl, 1);
+        if (lane == 0) ex = F::identity();
+        s_off[2 * lane] = ex;
+        s_off[2 * lane + 1] = F::combine(ex, w0);
+        if (lane == 31) publish_aggregate<F>(p, (unsigned)tc, incl);
+        agg_cur = __shfl_sync(FULL, incl, 31);
       }
       __syncthreads();
-      agg_cur = s_agg;
+#pragma unroll
+      for (int sI = 0; sI < STRIPS; ++sI) off_cur[sI] = F::combine(s_off[sI * NW + warp], excl_w[sI]);
     }
     if (tp >= 0) {
       if (warp == 0) {
@@ -613,20 +623,17 @@ __device__ __forceinline__ void scan_flat_staged(const typename F::P& p) {
         if (lane == 0) s_prefix = pre;
       }
       __syncthreads();
-      T carry = s_prefix;
+      const T carry = s_prefix;
       const long long base = (long long)tp * TILE;
       const T* b = buf + (size_t)bp * TILE;
-#pragma unroll 1
+#pragma unroll
       for (int sI = 0; sI < STRIPS; ++sI) {
-        const int e0 = (sI * BLOCK + tid) * 4;
+        const int e0 = sI * STRIP + 4 * tid;
         V4<T> v = *reinterpret_cast<const V4<T>*>(b + e0);
+        const T pre = F::combine(carry, off_prev[sI]);
+        v.v[0] = F::combine(pre, v.v[0]);
 #pragma unroll
         for (int q = 1; q < 4; ++q) v.v[q] = F::combine(v.v[q - 1], v.v[q]);
-        T total;
-        const T excl = block_scan_excl<F, BLOCK>(v.v[3], &total, s_warp);
-        const T pre = F::combine(carry, excl);
-#pragma unroll
-        for (int q = 0; q < 4; ++q) v.v[q] = F::combine(pre, v.v[q]);
         const long long g = base + e0;
         if (dst_aligned && g + 4 <= n) {
           st4(dst + g, v);
@@ -635,14 +642,15 @@ __device__ __forceinline__ void scan_flat_staged(const typename F::P& p) {
           for (int q = 0; q < 4; ++q)
             if (g + q < n) dst[g + q] = v.v[q];
         }
-        carry = F::combine(carry, total);
-        __syncthreads();  // s_warp is reused by the next strip
       }
     }
     // buffer bp is free (or was never used): claim tile k+2 into it
+    __syncthreads();
     if (tid == 0) claim((k + 2) % NBUF);
     __syncthreads();
     agg_prev = agg_cur;
+#pragma unroll
+    for (int sI = 0; sI < STRIPS; ++sI) off_prev[sI] = off_cur[sI];
   }
   // the last CTA out rearms the counters for the next launch
   if (tid == 0) {

@@ -238,16 +238,21 @@ class CudaResident:
             xty_b = R.Buffer(nb * 8)
             stream = self.regress.lane_stream(0)
             try:
-                cuda.run_device_ptrs(self.paths, [seed_b.ptr], [s_buf.ptr], stream)
+                def bind(c, **ptrs):  # device pointers in the program's param order
+                    return [ptrs[name] for name, _, _ in c.params]
+
+                cuda.run_device_ptrs(self.paths, bind(self.paths, seed=seed_b.ptr), [s_buf.ptr], stream)
                 # initial cash flow: intrinsic value at maturity (last column), on the device
-                cuda.run_device_ptrs(self.final, [s_buf.ptr], [cf_a.ptr], stream)
+                cuda.run_device_ptrs(self.final, bind(self.final, S=s_buf.ptr), [cf_a.ptr], stream)
                 cuda.check_device(self.paths, stream)
                 xtx = np.empty(nb * nb)
                 xty = np.empty(nb)
                 cur, nxt = cf_a, cf_b
                 for step in range(ns - 2, -1, -1):
                     R.check(R.lib().ccb_memcpy_h2d(t_b.ptr, np.array([step], np.int32).ctypes.data, 4, stream))
-                    cuda.run_device_ptrs(self.regress, [s_buf.ptr, cur.ptr, t_b.ptr], [xtx_b.ptr, xty_b.ptr], stream)
+                    outs = {"xtx": xtx_b.ptr, "xty": xty_b.ptr}
+                    cuda.run_device_ptrs(self.regress, bind(self.regress, S=s_buf.ptr, cf=cur.ptr, t=t_b.ptr),
+                                         [outs[name] for name, _, _ in self.regress.outputs], stream)
                     R.check(R.lib().ccb_memcpy_d2h(xtx.ctypes.data, xtx_b.ptr, xtx.nbytes, stream))
                     R.check(R.lib().ccb_memcpy_d2h(xty.ctypes.data, xty_b.ptr, xty.nbytes, stream))
                     cuda.check_device(self.regress, stream)
@@ -255,7 +260,8 @@ class CudaResident:
                         trace.append((step, xtx.copy(), xty.copy()))
                     beta = np.array(_beta(xtx, xty, nb), np.float64)
                     R.check(R.lib().ccb_memcpy_h2d(beta_b.ptr, beta.ctypes.data, beta.nbytes, stream))
-                    cuda.run_device_ptrs(self.update, [s_buf.ptr, cur.ptr, t_b.ptr, beta_b.ptr], [nxt.ptr], stream)
+                    cuda.run_device_ptrs(self.update, bind(self.update, S=s_buf.ptr, cf=cur.ptr, t=t_b.ptr, beta=beta_b.ptr),
+                                         [nxt.ptr], stream)
                     cur, nxt = nxt, cur
                 cfh = np.empty(n)
                 R.check(R.lib().ccb_memcpy_d2h(cfh.ctypes.data, cur.ptr, cfh.nbytes, stream))

@@ -347,3 +347,37 @@ def test_flat_scan_max_and_repeat_runs():
     for _ in range(3):
         got = dict(cuda.run(c, [("x", Value.of_array(F32, (n,), x))]))["p"].data
         assert np.array_equal(got, np.maximum.accumulate(x))
+
+
+@pytest.mark.parametrize("basis", ["scaled3", "poly4"])
+def test_lsm_drivers_match_interp(basis):
+    # the generic driver over the CUDA backend, the resident CUDA driver and
+    # the generic driver over the oracle: same normal equations every date,
+    # same price (examples/lsm.ml:251-420)
+    from cudacaml_b200 import lsm as L
+    m = X.MARKET if basis == "scaled3" else L.BASELINE_MARKET
+    n, ns = 4096, 16
+    ti, tc, tr = [], [], []
+    pi = L.Make(interp, n, ns, m, basis).price(11, trace=ti)
+    pc = L.Make(cuda, n, ns, m, basis).price(11, trace=tc)
+    res = L.CudaResident(n, ns, m, basis)
+    pr = res.price(11, trace=tr)
+    res.release()
+    for (si, ai, bi), (sc, ac, bc), (sr, ar, br) in zip(ti, tc, tr):
+        assert si == sc == sr
+        for e, g in ((ai, ac), (bi, bc), (ai, ar), (bi, br)):
+            assert np.all(np.abs(g - e) <= 1e-9 * (1 + np.abs(e))), (si, e, g)
+    assert abs(pc - pi) <= 1e-9 * (1 + abs(pi))
+    assert abs(pr - pi) <= 1e-9 * (1 + abs(pi))
+
+
+def test_s17_lsm_vs_binomial():
+    # S17: the resident driver against the binomial price (band 0.15), on the
+    # reference market (3-term basis) and the BASELINE market (4-term basis)
+    from cudacaml_b200 import lsm as L
+    for m, basis in ((X.MARKET, "scaled3"), (L.BASELINE_MARKET, "poly4")):
+        res = L.CudaResident(1 << 16, 50, m, basis)
+        px = res.price(11)
+        res.release()
+        assert abs(px - L.binomial_american_put(m)) <= 0.15, (basis, px)
+        assert px >= L.european_put(m) - 0.05
