@@ -198,6 +198,153 @@ def secondary_hbm(dev, stream_h, flush, pk):
     return res
 
 
+def secondary_configs(dev, flush, pk, quick=False):
+    """The other BASELINE configurations, each device-timed (median of 5 after
+    2 warm-ups, L2 flushed before each): rows (65536 x 4096 F32 reduce_rows max
+    and scan_rows add), scatter_add of 2^27 Zipf(1.1) updates into 2^20 bins,
+    gather of 2^27 from a 2^24 table, saxpy+sum at 2^20 (F32, F64), the
+    Longstaff-Schwartz price (2^22 paths x 64 dates, 4-term basis, F64) and the
+    MLP training step (8192 x 4096 -> 8192 -> 1024, F32). Inputs are generated
+    on the device by the reference's own Rng graphs (Zipf indices by a host
+    inverse-CDF table over device-generated uniforms)."""
+    import numpy as np
+    from cudacaml_b200 import backend_cuda as B
+    from cudacaml_b200 import dsl as D
+    from cudacaml_b200 import examples as X
+    from cudacaml_b200 import lsm as L
+    from cudacaml_b200 import rng as Rng
+    from cudacaml_b200 import runtime as R
+    from cudacaml_b200.ir import F32, F64, I32, Graph, Value
+
+    res = {}
+    seed_buf = R.Buffer(4)
+
+    def gen(graph, nbytes, seed):
+        c = B.compile_on(dev, graph)
+        out = R.Buffer(nbytes)
+        seed_buf.upload(np.array([seed], np.int32))
+        B.run_device_ptrs(c, [seed_buf.ptr], [out.ptr], None)
+        B.check_device(c, None)
+        B.release(c)
+        return out
+
+    def normal_f32(shape, seed, scale=1.0):
+        z = D.map(lambda v: D.cast(F32, D.mul(v, D.const(F64, scale))), Rng.normal(F64, D.scalar("seed", I32), shape))
+        return gen(Graph("gen", [("x", z)]), 4 * int(np.prod(shape)), seed)
+
+    def time_prog(c, ins, outs, reps=5):
+        s = c.lane_stream(0)
+        e0, e1 = R.Event(), R.Event()
+        ts = []
+        for k in range(2 + reps):
+            flush(s)
+            e0.record(s)
+            B.run_device_ptrs(c, [b.ptr for b in ins], [b.ptr for b in outs], s)
+            e1.record(s)
+            e1.synchronize()
+            if k >= 2:
+                ts.append(e0.elapsed_ms(e1) * 1e-3)
+        B.check_device(c, s)
+        return statistics.median(ts)
+
+    def hbm(t, alg):
+        return {"ms": t * 1e3, "gbs": alg / t / 1e9, "frac_of_measured_hbm": alg / t / 1e9 / pk["hbm_gbs"], "alg_bytes": alg}
+
+    # rows
+    rows, n = 65536, 4096
+    x = normal_f32((rows, n), 3)
+    for name, g, ob, alg in (("reduce_rows_max_65536x4096", Graph("rmax", [("m", D.reduce_rows(D.max, D.const(F32, -3e38), D.param("x", F32, (rows, n))))]), 4 * rows, 4 * rows * n + 4 * rows),
+                             ("scan_rows_add_65536x4096", Graph("rscan", [("p", D.scan_rows(D.add, D.const(F32, 0.0), D.param("x", F32, (rows, n))))]), 4 * rows * n, 8 * rows * n)):
+        c = B.compile_on(dev, g)
+        o = R.Buffer(ob)
+        res[name] = hbm(time_prog(c, [x], [o]), alg)
+        o.free()
+        B.release(c)
+    x.free()
+
+    # scatter (Zipf) and gather
+    m = 1 << 27
+    bins = 1 << 20
+    u = gen(Graph("u", [("u", Rng.uniform(F64, D.scalar("seed", I32), (m,)))]), 8 * m, 4)
+    uh = np.empty(m, np.float64)
+    u.download(uh)
+    u.free()
+    w = 1.0 / np.power(np.arange(1, bins + 1, dtype=np.float64), 1.1)
+    cdf = np.cumsum(w)
+    cdf /= cdf[-1]
+    idx = np.minimum(np.searchsorted(cdf, uh, side="left"), bins - 1).astype(np.int32)
+    del uh
+    ib = R.Buffer(4 * m)
+    ib.upload(idx)
+    vb = gen(Graph("v", [("v", Rng.uniform(F32, D.scalar("seed", I32), (m,)))]), 4 * m, 3)
+    c = B.compile_on(dev, X.scatter(m, bins))
+    o = R.Buffer(4 * bins)
+    r = hbm(time_prog(c, [ib, vb], [o]), 8 * m)
+    r["updates_per_s"] = m / (r["ms"] * 1e-3)
+    r["hot_bin_share"] = float(np.mean(idx == 0))
+    res["scatter_add_zipf_2p27_into_2p20"] = r
+    o.free()
+    B.release(c)
+    tbl = 1 << 24
+    gi = gen(Graph("gi", [("i", D.map(lambda w_: D.bit_and(w_, D.const(I32, tbl - 1)), Rng.u32(D.scalar("seed", I32), (m,))))]), 4 * m, 4)
+    tb = normal_f32((tbl,), 3)
+    c = B.compile_on(dev, X.gather(m, tbl))
+    o = R.Buffer(4 * m)
+    res["gather_2p27_from_2p24"] = hbm(time_prog(c, [gi, tb], [o]), 12 * m)
+    for b in (o, gi, tb, ib, vb):
+        b.free()
+    B.release(c)
+
+    # saxpy + sum
+    for dt, esz in ((F32, 4), (F64, 8)):
+        k = 1 << 20
+        xs = gen(Graph("x", [("x", D.map(lambda v: D.cast(dt, D.sub(D.mul(D.const(F64, 2.0), v), D.const(F64, 1.0))),
+                                          Rng.uniform(F64, D.scalar("seed", I32), (k,))))]), esz * k, 1)
+        ys = gen(Graph("y", [("y", D.map(lambda v: D.cast(dt, D.sub(D.mul(D.const(F64, 2.0), v), D.const(F64, 1.0))),
+                                          Rng.uniform(F64, D.scalar("seed", I32), (k,))))]), esz * k, 2)
+        c = B.compile_on(dev, X.saxpy(k, 2.0, dt))
+        rb, sb = R.Buffer(esz * k), R.Buffer(esz)
+        t = time_prog(c, [xs, ys], [rb, sb], reps=20)
+        r = hbm(t, 3 * esz * k)
+        r["note"] = "12.6/25.2 MB: launch-latency bound at this size"
+        res[f"saxpy_sum_2p20_{dt.value}"] = r
+        for b in (xs, ys, rb, sb):
+            b.free()
+        B.release(c)
+
+    # Longstaff-Schwartz, BASELINE configuration
+    if not quick:
+        lp = L.CudaResident(1 << 22, 64, L.BASELINE_MARKET, "poly4", device=dev)
+        lp.price(7)
+        t0 = time.perf_counter()
+        px = lp.price(7)
+        t = time.perf_counter() - t0
+        lp.release()
+        res["lsm_2p22x64_poly4_f64"] = {"ms": t * 1e3, "price": px, "binomial": L.binomial_american_put(L.BASELINE_MARKET),
+                                         "note": "wall time of one full price (paths graph + 63 regress/host-solve/update dates), device-resident"}
+
+    # MLP training step
+    if not quick:
+        bsz, din, hid, dout = 8192, 4096, 8192, 1024
+        xb = normal_f32((bsz, din), 5)
+        w1 = normal_f32((din, hid), 6, 1.0 / math.sqrt(din))
+        w2 = normal_f32((hid, dout), 7, 1.0 / math.sqrt(hid))
+        tt = normal_f32((bsz, dout), 8)
+        c = B.compile_on(dev, X.mlp_step(bsz, din, hid, dout))
+        outs = [R.Buffer(4 * int(np.prod(shape)) if shape else 4) for _, _, shape in c.outputs]
+        named = {"X": xb, "W1": w1, "W2": w2, "T": tt}
+        t = time_prog(c, [named[nm] for nm, _, _ in c.params], outs, reps=3)
+        fl = X.mlp_flops(bsz, din, hid, dout)
+        res["mlp_step_8192x4096x8192x1024_f32"] = {"ms": t * 1e3, "tflops": fl / t / 1e12, "flops": fl,
+                                                    "launches": c.num_launches(),
+                                                    "note": "matmuls on CUDA cores (FP32 FMA), not yet tensor cores"}
+        for b in outs + [xb, w1, w2, tt]:
+            b.free()
+        B.release(c)
+    seed_buf.free()
+    return res
+
+
 def measure_greeks(args, dtype, rank, world, local, dist, comm, flush):
     """Device-timed and end-to-end paths/s of the Greeks graph in `dtype`."""
     import numpy as np
@@ -352,6 +499,10 @@ def run_ours(args):
     secondary = None
     if rank == 0 and world == 1 and not args.no_secondary:
         secondary = secondary_hbm(local, None, flush, pk)
+        try:
+            secondary.update(secondary_configs(local, flush, pk))
+        except Exception as e:  # keep the headline line; report what failed
+            secondary["configs_error"] = f"{type(e).__name__}: {e}"
         secondary["bs_greeks_f32_2p28"] = {
             "value": f32["value"], "unit": "paths/s", "e2e": f32["e2e"], "ms_per_step": f32["ms_per_step"],
             "result": f32["outs"],

@@ -351,3 +351,37 @@ def gather(n: int, table: int) -> Graph:
     idx = D.param("idx", I32, (n,))
     t = D.param("table", F32, (table,))
     return Graph("gather", [("g", D.gather(idx, t))])
+
+
+# ---------------------------------------------------------------------------
+# Two-layer MLP training step (BASELINE configuration)
+# ---------------------------------------------------------------------------
+def tanh_like(z):
+    """tanh through exp: 1 - 2 / (exp(2z) + 1), saturating cleanly at +-1."""
+    d = z.dtype
+    return D.sub(D.const(d, 1.0), D.div(D.const(d, 2.0), D.add(D.exp(D.mul(D.const(d, 2.0), z)), D.const(d, 1.0))))
+
+
+def mlp_loss(batch: int, din: int, hidden: int, dout: int, dtype: Dtype = F32) -> Graph:
+    """loss = sum((tanh_like(X W1) W2 - T)^2): matmul -> map -> matmul ->
+    squared-error reduce."""
+    x = D.param("X", dtype, (batch, din))
+    w1 = D.param("W1", dtype, (din, hidden))
+    w2 = D.param("W2", dtype, (hidden, dout))
+    t = D.param("T", dtype, (batch, dout))
+    a1 = D.map(tanh_like, D.matmul(x, w1))
+    y = D.matmul(a1, w2)
+    d = D.map2(D.sub, y, t)
+    loss = D.reduce(D.add, D.const(dtype, 0.0), D.map(lambda e: D.mul(e, e), d))
+    return Graph("mlp", [("loss", loss)])
+
+
+def mlp_step(batch: int, din: int, hidden: int, dout: int, dtype: Dtype = F32) -> Graph:
+    """The loss and its gradients wrt W1 and W2 (Grad.grad)."""
+    return Grad.grad(mlp_loss(batch, din, hidden, dout, dtype), "loss", ["W1", "W2"])
+
+
+def mlp_flops(batch: int, din: int, hidden: int, dout: int) -> float:
+    """Forward X.W1 and A1.W2, backward dA1 = dY.W2^T, dW2 = A1^T.dY and
+    dW1 = X^T.dZ1: 2*B*Din*H * 2 + 2*B*H*Dout * 3."""
+    return 2.0 * batch * din * hidden * 2 + 2.0 * batch * hidden * dout * 3
