@@ -813,6 +813,40 @@ __device__ __forceinline__ void scatter_add(const typename F::P& p) {
   }
 }
 
+// Privatised scatter_add: the first PRIV bins accumulate in shared memory
+// (fast shared atomics; skewed index distributions such as Zipf put most of
+// their mass there), the rest go straight to global atomics, and each block
+// flushes its non-zero private bins with one global atomic per bin at the end.
+// Persistent grid; dynamic shared memory of PRIV * sizeof(T) bytes.
+template <class F, int PRIV>
+__device__ __forceinline__ void scatter_add_priv(const typename F::P& p) {
+  typedef typename F::T T;
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  T* sh = reinterpret_cast<T*>(smem_raw);
+  const long long n = p.n, m = p.m;
+  const int priv = (int)(m < PRIV ? m : PRIV);
+  for (int b = threadIdx.x; b < priv; b += blockDim.x) sh[b] = T(0);
+  __syncthreads();
+  const long long nth = (long long)gridDim.x * blockDim.x;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += nth) {
+    const int j = F::idx(p, i);
+    const T v = F::val(p, i);
+    if ((unsigned)j >= (unsigned long long)m) {
+      raise_error(p.err, ERR_SCATTER_OOB);
+      continue;
+    }
+    if (j < priv)
+      atomicAdd(&sh[j], v);
+    else
+      atomicAdd(&p.out[j], v);
+  }
+  __syncthreads();
+  for (int b = threadIdx.x; b < priv; b += blockDim.x) {
+    const T v = sh[b];
+    if (v != T(0)) atomicAdd(&p.out[b], v);
+  }
+}
+
 // ---------------------------------------------------------------- matmul (CUDA cores)
 // C[M,N] = A[M,K] . B[K,N], row-major, each output accumulated in ascending k
 // (the reference's contract, lib/ir/tensor.ml:35-40). 64x64 output tile per

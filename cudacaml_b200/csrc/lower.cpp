@@ -1746,12 +1746,15 @@ class Lowerer {
       src << "    return " << v << ";\n  }\n";
     }
     src << "};\n";
-    src << "extern \"C\" __global__ void __launch_bounds__(256) " << fn << "(const " << F << "::P p) { ccb::scatter_add<" << F
-        << ">(p); }\n\n";
+    // 64 KiB of private bins per block (16384 4-byte or 8192 8-byte bins)
+    const int priv = 65536 / dt_size(x.dt);
+    src << "extern \"C\" __global__ void __launch_bounds__(256) " << fn << "(const " << F << "::P p) { ccb::scatter_add_priv<" << F
+        << ", " << priv << ">(p); }\n\n";
     LaunchSpec& l = add_launch(fn, fields);
     l.mode = GM_PERSISTENT;
     l.work = gr.domain;
-    l.per_block = 256 * 4;
+    l.per_block = 256 * 16;
+    l.smem = (int)(std::min<int64_t>(x.numel, priv) * dt_size(x.dt));
   }
 
   void emit_matmul(int gi) {
