@@ -44,8 +44,9 @@ def peaks():
     if os.path.exists(p):
         with open(p) as f:
             d = json.load(f)
-        return {"hbm_gbs": d["hbm_gbs"], "sm_max_mhz": d.get("sm_max_mhz", 1965.0), "src": "measured"}
-    return {"hbm_gbs": 6650.0, "sm_max_mhz": 1965.0, "src": "fallback"}
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d.get("bf16_tflops", 1590.0), "sm_max_mhz": d.get("sm_max_mhz", 1965.0),
+                "src": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "sm_max_mhz": 1965.0, "src": "fallback"}
 
 
 class ClockSampler:
@@ -330,17 +331,26 @@ def secondary_configs(dev, flush, pk, quick=False):
         w1 = normal_f32((din, hid), 6, 1.0 / math.sqrt(din))
         w2 = normal_f32((hid, dout), 7, 1.0 / math.sqrt(hid))
         tt = normal_f32((bsz, dout), 8)
-        c = B.compile_on(dev, X.mlp_step(bsz, din, hid, dout))
-        outs = [R.Buffer(4 * int(np.prod(shape)) if shape else 4) for _, _, shape in c.outputs]
         named = {"X": xb, "W1": w1, "W2": w2, "T": tt}
-        t = time_prog(c, [named[nm] for nm, _, _ in c.params], outs, reps=3)
         fl = X.mlp_flops(bsz, din, hid, dout)
-        res["mlp_step_8192x4096x8192x1024_f32"] = {"ms": t * 1e3, "tflops": fl / t / 1e12, "flops": fl,
-                                                    "launches": c.num_launches(),
-                                                    "note": "matmuls on CUDA cores (FP32 FMA), not yet tensor cores"}
-        for b in outs + [xb, w1, w2, tt]:
+        tf32_peak = pk["bf16_tflops"] / 2.0
+        for prec, reps in (("tf32", 10), ("f32", 3)):
+            c = B.compile_on(dev, X.mlp_step(bsz, din, hid, dout), matmul=prec)
+            outs = [R.Buffer(4 * int(np.prod(shape)) if shape else 4) for _, _, shape in c.outputs]
+            t = time_prog(c, [named[nm] for nm, _, _ in c.params], outs, reps=reps)
+            line = {"ms": t * 1e3, "tflops": fl / t / 1e12, "flops": fl, "launches": c.num_launches()}
+            if prec == "tf32":
+                line["frac_of_tf32_peak"] = fl / t / 1e12 / tf32_peak
+                line["note"] = ("matmuls on tcgen05 tensor cores (kind::tf32, TMEM accumulators, TMA operands); "
+                                "TF32 peak taken as half the measured dense bf16 %.0f TFLOP/s" % pk["bf16_tflops"])
+            else:
+                line["note"] = "F32 precision mode: matmuls on CUDA cores (FP32 FMA)"
+            res[f"mlp_step_8192x4096x8192x1024_{prec}"] = line
+            for b in outs:
+                b.free()
+            B.release(c)
+        for b in (xb, w1, w2, tt):
             b.free()
-        B.release(c)
     seed_buf.free()
     return res
 
@@ -554,17 +564,41 @@ def run_profile_case(args):
     from cudacaml_b200 import examples as X
     from cudacaml_b200 import runtime as R
     from cudacaml_b200.ir import F32, F64
+    from cudacaml_b200 import dsl as D
+    from cudacaml_b200.ir import I32, Graph, Value
     R.set_device(0)
     n = args.size
     if args.profile in ("greeks64", "greeks32"):
         dt = F64 if args.profile == "greeks64" else F32
         c = B.compile(X.call_greeks(n, dt))
         ins = X.bs_inputs(dt, seed=SEED)
-    else:
+    elif args.profile in ("reduce", "scan"):
         g = {"reduce": X.reduce_flat(n, F32), "scan": X.scan_flat(n, F32)}[args.profile]
         c = B.compile(g)
-        from cudacaml_b200.ir import Value
         ins = [("x", Value.of_array(F32, (n,), np.full(n, 0.5, np.float32)))]
+    elif args.profile in ("rows_reduce", "rows_scan"):
+        rows = n // 4096
+        x = D.param("x", F32, (rows, 4096))
+        op = (D.reduce_rows(D.max, D.const(F32, -3e38), x) if args.profile == "rows_reduce"
+              else D.scan_rows(D.add, D.const(F32, 0.0), x))
+        c = B.compile(Graph("rows", [("r", op)]))
+        ins = [("x", Value.of_array(F32, (rows, 4096), np.full(rows * 4096, 0.5, np.float32)))]
+    elif args.profile == "scatter":
+        bins = 1 << 20
+        c = B.compile(X.scatter(n, bins))
+        ins = [("idx", Value.of_array(I32, (n,), X.zipf_indices(4, n, bins))),
+               ("v", Value.of_array(F32, (n,), np.full(n, 0.5, np.float32)))]
+    elif args.profile == "gather":
+        tbl = 1 << 24
+        c = B.compile(X.gather(n, tbl))
+        ins = [("idx", Value.of_array(I32, (n,), (X.philox_word0(4, n) & (tbl - 1)).astype(np.int32))),
+               ("table", Value.of_array(F32, (tbl,), np.full(tbl, 0.5, np.float32)))]
+    else:  # mlp at a reduced size
+        b = n
+        c = B.compile(X.mlp_step(b, b // 2, b, b // 8), matmul="tf32" if args.profile == "mlp_tf32" else "f32")
+        rng = np.random.default_rng(0)
+        ins = [(nm, Value.of_array(F32, shape, rng.standard_normal(int(np.prod(shape))).astype(np.float32) * 0.05))
+               for nm, _, shape in c.params]
     for _ in range(3):
         out = B.run(c, ins)
     print(json.dumps({k: float(v.data[0]) for k, v in out if v.numel == 1}))
@@ -578,7 +612,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-secondary", action="store_true")
-    ap.add_argument("--profile", default=None, choices=["greeks64", "greeks32", "reduce", "scan"],
+    ap.add_argument("--profile", default=None,
+                    choices=["greeks64", "greeks32", "reduce", "scan", "rows_reduce", "rows_scan", "scatter", "gather", "mlp",
+                             "mlp_tf32"],
                     help="run a small fixed case (3 launches) for an ncu capture, no timing")
     ap.add_argument("--size", type=int, default=1 << 24, help="paths/elements of the --profile case")
     args = ap.parse_args()

@@ -21,6 +21,21 @@ from .wire import to_wire
 
 name = "cuda"
 
+# Precision of F32 matmul nodes for graphs compiled without an explicit
+# choice: "f32" (F32 arithmetic, as the reference) or "tf32" (tcgen05 tensor
+# cores, TF32 operands, F32 accumulation). Like torch's allow_tf32 switch.
+matmul_precision = "f32"
+
+
+def set_matmul_precision(p: str) -> None:
+    global matmul_precision
+    to_wire(Graph("probe", []), p)  # validates the name
+    matmul_precision = p
+
+
+def _wire(graph: Graph, matmul) -> bytes:
+    return to_wire(graph, matmul or matmul_precision).encode()
+
 _CODE_DT = {0: Dtype.F32, 1: Dtype.F64, 2: Dtype.I32, 3: Dtype.I64}
 
 
@@ -43,7 +58,7 @@ def _io_specs(h, count_fn, get_fn):
 class Compiled:
     """A program compiled for one device, with ``streams`` executors."""
 
-    def __init__(self, graph: Graph, device: int, streams: int):
+    def __init__(self, graph: Graph, device: int, streams: int, matmul=None):
         if streams < 1:
             raise ValueError("Backend_cuda.compile_on: streams must be >= 1")
         self.graph = graph
@@ -51,7 +66,7 @@ class Compiled:
         self.streams = streams
         self.next = 0
         h = ctypes.c_void_p()
-        R.check(R.lib().ccb_program_create(to_wire(graph).encode(), device, streams, ctypes.byref(h)))
+        R.check(R.lib().ccb_program_create(_wire(graph, matmul), device, streams, ctypes.byref(h)))
         self.h = h.value
         self.params = _io_specs(self.h, "ccb_program_num_params", "ccb_program_param")
         self.outputs = _io_specs(self.h, "ccb_program_num_outputs", "ccb_program_output")
@@ -114,10 +129,10 @@ def _ptr_array(ptrs):
     return a
 
 
-def source(graph: Graph) -> str:
+def source(graph: Graph, matmul=None) -> str:
     """The generated CUDA C++ for a graph, without compiling it."""
     h = ctypes.c_void_p()
-    R.check(R.lib().ccb_program_lower(to_wire(graph).encode(), ctypes.byref(h)))
+    R.check(R.lib().ccb_program_lower(_wire(graph, matmul), ctypes.byref(h)))
     try:
         s = ctypes.c_char_p()
         R.check(R.lib().ccb_program_source(h.value, ctypes.byref(s)))
@@ -126,11 +141,11 @@ def source(graph: Graph) -> str:
         R.lib().ccb_program_destroy(h.value)
 
 
-def lower_info(graph: Graph) -> dict:
+def lower_info(graph: Graph, matmul=None) -> dict:
     """Kernel count, launches per run and the host plan, without a device."""
     L = R.lib()
     h = ctypes.c_void_p()
-    R.check(L.ccb_program_lower(to_wire(graph).encode(), ctypes.byref(h)))
+    R.check(L.ccb_program_lower(_wire(graph, matmul), ctypes.byref(h)))
     try:
         k = ctypes.c_int()
         n = ctypes.c_int()
@@ -145,16 +160,16 @@ def lower_info(graph: Graph) -> dict:
         L.ccb_program_destroy(h.value)
 
 
-def compile_on(device: int, graph: Graph, streams: int = 1) -> Compiled:
-    return Compiled(graph, device, streams)
+def compile_on(device: int, graph: Graph, streams: int = 1, matmul=None) -> Compiled:
+    return Compiled(graph, device, streams, matmul)
 
 
-def compile_with(streams: int, graph: Graph) -> Compiled:
-    return Compiled(graph, 0, streams)
+def compile_with(streams: int, graph: Graph, matmul=None) -> Compiled:
+    return Compiled(graph, 0, streams, matmul)
 
 
-def compile(graph: Graph) -> Compiled:  # noqa: A001 - Backend.S.compile
-    return Compiled(graph, 0, 1)
+def compile(graph: Graph, matmul=None) -> Compiled:  # noqa: A001 - Backend.S.compile
+    return Compiled(graph, 0, 1, matmul)
 
 
 def device_of(c: Compiled) -> int:

@@ -903,4 +903,239 @@ __device__ __forceinline__ void matmul_tiled(const typename F::P& p) {
     }
 }
 
+// ------------------------------------------------------------------------
+// F32 matmul on the tcgen05 tensor cores (kind::tf32), persistent.
+//
+// One CTA per SM owns 128x256 output tiles in turn. Warp 0 (one thread) is
+// the TMA producer: per 32-wide k-step it loads the A tile (128 x 32) and
+// the B tile (256 x 32) into a 4-deep ring of 48 KiB stages, 128-byte
+// swizzled. Warp 1 (one thread) issues tcgen05.mma (M=128, N=256, K=8, four
+// per stage) into one of two TMEM accumulators of 256 fp32 columns, and
+// releases each stage with tcgen05.commit. Warps 2-5 drain the finished
+// accumulator (tcgen05.ld, 32 columns at a time, one TMEM lane quadrant per
+// warp) into global memory while the next tile accumulates in the other
+// buffer. Loads are plain TMA (no cluster multicast).
+//
+// Operands arrive as views of materialised row-major buffers: A is K-major
+// (A[r][k] at r*K+k) or MN-major (at k*M+r); B is MN-major (B[k][c] at
+// k*N+c) or K-major (at c*K+k). Out-of-range tile rows and k-steps read as
+// zero (TMA fill), so any M, N, K >= 1 is exact in shape; stores are masked.
+//
+// Numerics: TF32 operands (10 explicit mantissa bits), FP32 accumulation.
+// Bound used by the tests: |C - C_exact| <= (2^-9 + K*2^-23) * sum_k |A||B|.
+//
+// F provides P (first fields: TmaDesc ta, tb; then C, err, M, N, K) and the
+// constants A_MN, B_MN.
+struct alignas(64) TmaDesc {
+  unsigned long long w[16];
+};
+
+namespace tc {
+constexpr int BM = 128, BN = 256, BK = 32, STAGES = 4, THREADS = 192;
+constexpr unsigned A_BYTES = BM * BK * 4, B_BYTES = BN * BK * 4, STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr unsigned SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+constexpr unsigned TMEM_COLS = 2 * BN;
+constexpr int GROUP_M = 16;  // tile raster: 16 M-tiles per band for L2 reuse
+constexpr unsigned ERR_TC_WAIT = 16u;
+
+__device__ __forceinline__ void wait(u64* bar, unsigned parity, unsigned* err) {
+  for (unsigned it = 0; it < MBAR_SPIN_LIMIT; ++it)
+    if (mbar_try_wait(bar, parity)) return;
+  raise_error(err, ERR_TC_WAIT);
+  for (unsigned it = 0; it < MBAR_SPIN_LIMIT; ++it)
+    if (mbar_try_wait(bar, parity)) return;
+}
+__device__ __forceinline__ void arrive(u64* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void tma_load_2d(unsigned dst, const TmaDesc* map, int x, int y, u64* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+      "l"((unsigned long long)map), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// Shared-memory matrix descriptor, SWIZZLE_128B, version 1 (sm_100).
+__device__ __forceinline__ u64 sdesc(unsigned saddr, unsigned lbo, unsigned sbo) {
+  return (u64)((saddr >> 4) & 0x3FFFu) | ((u64)((lbo >> 4) & 0x3FFFu) << 16) | ((u64)((sbo >> 4) & 0x3FFFu) << 32) |
+         (1ull << 46) | (2ull << 61);
+}
+__device__ __forceinline__ void mma(unsigned d, u64 a, u64 b, unsigned idesc, unsigned accumulate) {
+  const unsigned z = 0;
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n}\n" ::"r"(d),
+      "l"(a), "l"(b), "r"(idesc), "r"(accumulate), "r"(z), "r"(z), "r"(z), "r"(z));
+}
+__device__ __forceinline__ void commit(u64* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void ld32(unsigned taddr, float* v) {
+  unsigned r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void tile_of(long long t, int tiles_m, int tiles_n, int& tm, int& tn) {
+  const long long band = (long long)GROUP_M * tiles_n;
+  const int first = (int)(t / band) * GROUP_M;
+  const int rows = min(tiles_m - first, GROUP_M);
+  const int r = (int)(t % band);
+  tm = first + r % rows;
+  tn = r / rows;
+}
+}  // namespace tc
+
+template <class F>
+__device__ __forceinline__ void matmul_tc(const typename F::P& p) {
+  using namespace tc;
+  extern __shared__ __align__(1024) unsigned char ccb_tc_smem[];
+  const unsigned raw = smem_u32(ccb_tc_smem);
+  const unsigned pad = (1024u - (raw & 1023u)) & 1023u;
+  unsigned char* base = ccb_tc_smem + pad;
+  const unsigned sbase = raw + pad;
+  u64* full = (u64*)(base + STAGES * STAGE_BYTES);
+  u64* empty = full + STAGES;
+  u64* accf = empty + STAGES;
+  u64* acce = accf + 2;
+  unsigned* tslot = (unsigned*)(acce + 2);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long long M = p.M, N = p.N, K = p.K;
+  const int tiles_m = (int)((M + BM - 1) / BM), tiles_n = (int)((N + BN - 1) / BN);
+  const long long ntiles = (long long)tiles_m * tiles_n;
+  const int KT = (int)((K + BK - 1) / BK);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&accf[b], 1);
+      mbar_init(&acce[b], 4);
+    }
+    mbar_fence_init();
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tslot)), "r"(TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const unsigned tmem = *tslot;
+
+  if (warp == 0) {
+    if (lane == 0) {  // TMA producer
+      unsigned stage = 0, phase = 0;
+      for (long long t = blockIdx.x; t < ntiles; t += gridDim.x) {
+        int tm, tn;
+        tile_of(t, tiles_m, tiles_n, tm, tn);
+        const int m0 = tm * BM, n0 = tn * BN;
+        for (int ks = 0; ks < KT; ++ks) {
+          wait(&empty[stage], phase ^ 1u, p.err);
+          const unsigned sa = sbase + stage * STAGE_BYTES, sb = sa + A_BYTES;
+          mbar_expect_tx(&full[stage], STAGE_BYTES);
+          const int k0 = ks * BK;
+          if (F::A_MN) {
+#pragma unroll
+            for (int g = 0; g < BM / 32; ++g) tma_load_2d(sa + g * 4096u, &p.ta, m0 + 32 * g, k0, &full[stage]);
+          } else {
+            tma_load_2d(sa, &p.ta, k0, m0, &full[stage]);
+          }
+          if (F::B_MN) {
+#pragma unroll
+            for (int g = 0; g < BN / 32; ++g) tma_load_2d(sb + g * 4096u, &p.tb, n0 + 32 * g, k0, &full[stage]);
+          } else {
+            tma_load_2d(sb, &p.tb, k0, n0, &full[stage]);
+          }
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {  // MMA issuer
+      const unsigned idesc = (1u << 4) | (2u << 7) | (2u << 10) | ((F::A_MN ? 1u : 0u) << 15) | ((F::B_MN ? 1u : 0u) << 16) |
+                             ((unsigned)(BN >> 3) << 17) | ((unsigned)(BM >> 4) << 24);
+      unsigned stage = 0, phase = 0;
+      int it = 0;
+      for (long long t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
+        const unsigned ab = it & 1, aph = (it >> 1) & 1;
+        wait(&acce[ab], aph ^ 1u, p.err);
+        fence_after();
+        const unsigned d = tmem + ab * BN;
+        for (int ks = 0; ks < KT; ++ks) {
+          wait(&full[stage], phase, p.err);
+          fence_after();
+          const unsigned sa = sbase + stage * STAGE_BYTES, sb = sa + A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < BK / 8; ++kk) {
+            const u64 a = F::A_MN ? sdesc(sa + kk * 1024u, 4096u, 1024u) : sdesc(sa + kk * 32u, 16u, 1024u);
+            const u64 b = F::B_MN ? sdesc(sb + kk * 1024u, 4096u, 1024u) : sdesc(sb + kk * 32u, 16u, 1024u);
+            mma(d, a, b, idesc, (ks | kk) != 0 ? 1u : 0u);
+          }
+          commit(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        commit(&accf[ab]);
+      }
+    }
+  } else {  // epilogue: warps 2..5, TMEM lane quadrant warp % 4
+    const int q = warp & 3;
+    const bool vec = ((((unsigned long long)p.C) & 15ull) == 0) && (N % 4 == 0);
+    int it = 0;
+    for (long long t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
+      int tm, tn;
+      tile_of(t, tiles_m, tiles_n, tm, tn);
+      const long long row = (long long)tm * BM + q * 32 + lane;
+      const long long n0 = (long long)tn * BN;
+      const unsigned ab = it & 1, aph = (it >> 1) & 1;
+      wait(&accf[ab], aph, p.err);
+      __syncwarp();  // tcgen05.ld is warp-collective: reconverge after the polls
+      fence_after();
+      for (int c = 0; c < BN && n0 + c < N; c += 32) {
+        float v[32];
+        __syncwarp();
+        ld32(tmem + ((unsigned)(q * 32) << 16) + ab * BN + c, v);
+        if (row < M) {
+          float* dst = p.C + row * N + n0 + c;
+          if (vec && n0 + c + 32 <= N) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 4) *(float4*)(dst + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+          } else {
+            for (int i = 0; i < 32 && n0 + c + i < N; ++i) dst[i] = v[i];
+          }
+        }
+      }
+      fence_before();
+      __syncwarp();
+      if (lane == 0) arrive(&acce[ab]);
+    }
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+  __syncwarp();
+  if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+}
+
 }  // namespace ccb

@@ -77,6 +77,7 @@ const Driver& driver() {
     S(cuOccupancyMaxActiveBlocksPerMultiprocessor, "cuOccupancyMaxActiveBlocksPerMultiprocessor")
     S(cuGetErrorString, "cuGetErrorString")
     S(cuPointerGetAttribute, "cuPointerGetAttribute")
+    S(cuTensorMapEncodeTiled, "cuTensorMapEncodeTiled")
 #undef S
     d.ok = ok;
   });

@@ -54,6 +54,7 @@ struct Driver {
   CCB_DRV(cuOccupancyMaxActiveBlocksPerMultiprocessor)
   CCB_DRV(cuGetErrorString)
   CCB_DRV(cuPointerGetAttribute)
+  CCB_DRV(cuTensorMapEncodeTiled)
 #undef CCB_DRV
 };
 

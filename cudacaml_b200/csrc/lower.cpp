@@ -109,6 +109,13 @@ int parse_graph(const char* text, GGraph& g) {
         header = true;
       } else if (tag == "name") {
         ls >> g.name;
+      } else if (tag == "opt") {
+        std::string key, val;
+        ls >> key >> val;
+        if (key != "matmul") bad("wire: unknown option " + key);
+        if (val == "f32") g.matmul = MM_F32;
+        else if (val == "tf32") g.matmul = MM_TF32;
+        else bad("wire: matmul precision must be f32 or tf32, got " + val);
       } else if (tag == "e") {
         int64_t id;
         std::string dts, kind;
@@ -715,7 +722,7 @@ struct Emitter {
 // ===================================================================== lowering
 namespace {
 
-enum GKind { G_MAPRED, G_SCAN_FLAT, G_SCAN_ROWS, G_RED_ROWS, G_SCATTER, G_MATMUL };
+enum GKind { G_MAPRED, G_SCAN_FLAT, G_SCAN_ROWS, G_RED_ROWS, G_SCATTER, G_MATMUL, G_MATMUL_TC };
 
 struct Red {
   int t = -1;           // output tensor
@@ -762,6 +769,166 @@ class Lowerer {
     return x.kind == T_MATMUL && g.ts[x.dep0].shape.size() == 2 && g.ts[x.dep0].shape[1] <= kSmallK;
   }
 
+  // ------------------------------------------------------------ tensor-core operands
+  // An F32 product with enough work runs on the tcgen05 tensor cores. Its
+  // operands must then be plain views of buffers: each operand is traced
+  // through reshapes and index-affine gathers (Dsl.transpose is one,
+  // lib/ir/dsl.ml:167-182) to the tensor it reads, which is materialised,
+  // and the trace must end in row-major or transposed order.
+  struct TcInfo {
+    bool on = false;
+    int va = -1, vb = -1;       // tensors read for A and B
+    bool a_mn = false, b_mn = false;  // A stored [K][M]; B stored [K][N]
+  };
+  std::vector<TcInfo> tc;
+
+  // a*r + b*c + k over r in [0,R), c in [0,C).
+  struct Aff {
+    bool ok = false;
+    int64_t a = 0, b = 0, k = 0;
+  };
+  static void aff_range(const Aff& f, int64_t R, int64_t C, int64_t& lo, int64_t& hi) {
+    const int64_t ea = f.a * (R - 1), eb = f.b * (C - 1);
+    lo = f.k + std::min<int64_t>(0, ea) + std::min<int64_t>(0, eb);
+    hi = f.k + std::max<int64_t>(0, ea) + std::max<int64_t>(0, eb);
+  }
+  static bool int_dt(Dt d) { return d == DT_I32 || d == DT_I64; }
+
+  // The value of integer element function `e` (Arg 0 and Index bound to
+  // `arg`) as an affine form, exact over the whole (r, c) domain, or !ok.
+  Aff aff_expr(int e, const Aff& arg, int64_t R, int64_t C, std::unordered_map<int, Aff>& memo) const {
+    auto it = memo.find(e);
+    if (it != memo.end()) return it->second;
+    const GExpr& x = g.ex[e];
+    Aff r;
+    switch (x.kind) {
+      case E_CONST:
+        if (int_dt(x.dt)) {
+          r.ok = true;
+          r.k = x.i;
+        }
+        break;
+      case E_ARG:
+        if (x.i == 0) r = arg;
+        break;
+      case E_INDEX: r = arg; break;
+      case E_CAST:
+        if (int_dt(x.dt) && int_dt(g.ex[x.a].dt)) r = aff_expr(x.a, arg, R, C, memo);
+        break;
+      case E_BINOP: {
+        if (!int_dt(x.dt)) break;
+        const Aff u = aff_expr(x.a, arg, R, C, memo), v = aff_expr(x.b, arg, R, C, memo);
+        if (!u.ok || !v.ok) break;
+        const bool uc = u.a == 0 && u.b == 0, vc = v.a == 0 && v.b == 0;
+        if (x.op == B_ADD) {
+          r = {true, u.a + v.a, u.b + v.b, u.k + v.k};
+        } else if (x.op == B_SUB) {
+          r = {true, u.a - v.a, u.b - v.b, u.k - v.k};
+        } else if (x.op == B_MUL && (uc || vc)) {
+          r = uc ? Aff{true, v.a * u.k, v.b * u.k, v.k * u.k} : Aff{true, u.a * v.k, u.b * v.k, u.k * v.k};
+        } else if (x.op == B_DIV && vc && v.k > 0) {
+          // non-negative numerator: truncation is floor; one coordinate must
+          // pass through whole and the rest stay inside [0, d)
+          const int64_t d = v.k;
+          int64_t lo, hi;
+          aff_range(u, R, C, lo, hi);
+          if (lo < 0) break;
+          const Aff ra{true, u.a, 0, u.k}, rb{true, 0, u.b, u.k};
+          int64_t l2, h2;
+          if (u.a % d == 0 && u.b % d == 0 && u.k >= 0 && u.k < d) {
+            r = {true, u.a / d, u.b / d, 0};
+          } else if (u.a % d == 0 && (aff_range(rb, R, C, l2, h2), l2 >= 0 && h2 < d)) {
+            r = {true, u.a / d, 0, 0};
+          } else if (u.b % d == 0 && (aff_range(ra, R, C, l2, h2), l2 >= 0 && h2 < d)) {
+            r = {true, 0, u.b / d, 0};
+          }
+        }
+        break;
+      }
+      default: break;
+    }
+    if (r.ok) {  // the element arithmetic must not wrap anywhere on the domain
+      int64_t lo, hi;
+      aff_range(r, R, C, lo, hi);
+      const int64_t lim = x.dt == DT_I32 ? (int64_t(1) << 31) : (int64_t(1) << 62);
+      if (lo < -lim || hi >= lim) r.ok = false;
+    }
+    memo[e] = r;
+    return r;
+  }
+
+  // Trace operand tensor d (element (r, c) of an R x C operand at flat index
+  // C*r + c) through reshapes and affine gathers. Returns the tensor reached
+  // and, in f, the flat index of (r, c) in it.
+  int peel(int d, int64_t R, int64_t C, Aff& f) const {
+    f = Aff{true, C, 1, 0};
+    for (int guard = 0; guard < 32; ++guard) {
+      const GTensor& x = g.ts[d];
+      if (mat[d]) return d;
+      if (x.kind == T_RESHAPE) {
+        d = x.dep0;
+        continue;
+      }
+      if (x.kind != T_GATHER) return d;
+      const GTensor& ix = g.ts[x.dep0];
+      Aff nf;
+      if (ix.kind == T_IOTA) {
+        nf = f;
+      } else if (ix.kind == T_MAP && g.ts[ix.dep0].kind == T_IOTA && g.ts[ix.dep0].numel == ix.numel) {
+        std::unordered_map<int, Aff> memo;
+        nf = aff_expr(ix.body, f, R, C, memo);
+      }
+      if (!nf.ok) return d;
+      int64_t lo, hi;
+      aff_range(nf, R, C, lo, hi);
+      if (lo < 0 || hi >= g.ts[x.dep1].numel) return d;
+      f = nf;
+      d = x.dep1;
+    }
+    return d;
+  }
+
+  // Work below this (M*N*K) stays on the exact CUDA-core tile kernel.
+  static constexpr int64_t kTcMinWork = int64_t(1) << 21;
+
+  void plan_tensor_core() {
+    const int T = (int)g.ts.size();
+    tc.assign(T, TcInfo());
+    if (g.matmul != MM_TF32) return;
+    for (int t = 0; t < T; ++t) {
+      const GTensor& x = g.ts[t];
+      if (x.kind != T_MATMUL || x.dt != DT_F32 || small_k(t)) continue;
+      const GTensor &A = g.ts[x.dep0], &Bt = g.ts[x.dep1];
+      if (A.dt != DT_F32 || Bt.dt != DT_F32) continue;
+      const int64_t M = x.shape[0], N = x.shape[1], K = A.shape[1];
+      if (M * N <= 32 && K >= 2048) continue;  // split-K reduction pass
+      if (K < 32 || M * N * K < kTcMinWork || M >= (int64_t(1) << 31) || N >= (int64_t(1) << 31) ||
+          K >= (int64_t(1) << 31))
+        continue;
+      TcInfo ti;
+      Aff fa, fb;
+      ti.va = peel(x.dep0, M, K, fa);
+      ti.vb = peel(x.dep1, K, N, fb);
+      auto is = [](const Aff& f, int64_t a, int64_t b) { return f.ok && f.a == a && f.b == b && f.k == 0; };
+      if (g.ts[ti.va].numel != M * K || g.ts[ti.va].dt != DT_F32 || !(is(fa, K, 1) || is(fa, 1, M))) {
+        ti.va = x.dep0;
+        fa = Aff{true, K, 1, 0};
+      }
+      if (g.ts[ti.vb].numel != K * N || g.ts[ti.vb].dt != DT_F32 || !(is(fb, N, 1) || is(fb, 1, K))) {
+        ti.vb = x.dep1;
+        fb = Aff{true, N, 1, 0};
+      }
+      ti.a_mn = !is(fa, K, 1);
+      ti.b_mn = is(fb, N, 1);
+      // TMA: every row pitch a multiple of 16 bytes
+      if ((ti.a_mn ? M : K) % 4 != 0 || (ti.b_mn ? N : K) % 4 != 0) continue;
+      ti.on = true;
+      tc[t] = ti;
+      mat[ti.va] = 1;
+      mat[ti.vb] = 1;
+    }
+  }
+
   void analyse() {
     const int T = (int)g.ts.size();
     uses.assign(T, 0);
@@ -780,6 +947,7 @@ class Lowerer {
       mat[t] = x.kind == T_PARAM || barrier || is_out[t];
       if (mat[t] && x.dt == DT_BOOL) bad("Value.create: Bool tensors are not storable (node n" + std::to_string(x.uid) + ")");
     }
+    plan_tensor_core();
   }
 
   // ------------------------------------------------------------ element builder
@@ -1211,6 +1379,12 @@ class Lowerer {
         }
         case T_MATMUL: {
           const int64_t M = x.shape[0], N = x.shape[1], K = g.ts[x.dep0].shape[1];
+          if (tc[t].on) {
+            const int gi = new_group(G_MATMUL_TC, M * N);
+            groups[gi].root = t;
+            group_of[t] = gi;
+            break;
+          }
           if (small_k(t)) {  // an output: an element-wise store
             if (cur >= 0 && try_join(cur, t)) break;
             cur = new_group(G_MAPRED, x.numel == 1 ? 1 : x.numel);
@@ -1802,6 +1976,62 @@ class Lowerer {
     l.gy = std::max<int64_t>(1, (M + 63) / 64);
   }
 
+  // F32 product on the tensor cores (ccb::matmul_tc): operands by TMA from
+  // the buffers the operand views resolve to.
+  void emit_matmul_tc(int gi) {
+    Group& gr = groups[gi];
+    const int t = gr.root;
+    const GTensor& x = g.ts[t];
+    const TcInfo& ti = tc[t];
+    const std::string F = "F" + std::to_string(gi);
+    const std::string fn = "ccb_matmultc_" + std::to_string(gi) + kname_suffix();
+    const int64_t M = x.shape[0], N = x.shape[1], K = g.ts[x.dep0].shape[1];
+    node_buf[t] = add_buf("t" + std::to_string(x.uid), 4, x.numel, BR_NODE, t, false);
+    if (node_buf[ti.va] < 0 || node_buf[ti.vb] < 0) bad("lower: internal: tensor-core operand without a buffer");
+    std::vector<Field> fields;
+    Field fa, fb;
+    fa.decl = "ccb::TmaDesc ta";
+    fa.slot.kind = SL_TMAP;
+    fa.slot.buf = node_buf[ti.va];
+    fa.slot.tbox[0] = 32;
+    if (ti.a_mn) {  // A^T stored [K][M]: 32 x 32 boxes, four per 128-row tile
+      fa.slot.tdim[0] = M, fa.slot.tdim[1] = K, fa.slot.tstride = M * 4, fa.slot.tbox[1] = 32;
+    } else {  // A stored [M][K]: one 32 x 128 box
+      fa.slot.tdim[0] = K, fa.slot.tdim[1] = M, fa.slot.tstride = K * 4, fa.slot.tbox[1] = 128;
+    }
+    fb.decl = "ccb::TmaDesc tb";
+    fb.slot.kind = SL_TMAP;
+    fb.slot.buf = node_buf[ti.vb];
+    fb.slot.tbox[0] = 32;
+    if (ti.b_mn) {  // B stored [K][N]: 32 x 32 boxes, eight per 256-column tile
+      fb.slot.tdim[0] = N, fb.slot.tdim[1] = K, fb.slot.tstride = N * 4, fb.slot.tbox[1] = 32;
+    } else {  // B^T stored [N][K]: one 32 x 256 box
+      fb.slot.tdim[0] = K, fb.slot.tdim[1] = N, fb.slot.tstride = K * 4, fb.slot.tbox[1] = 256;
+    }
+    fields.push_back(fa);  // tensor maps first: 64-byte aligned in the block
+    fields.push_back(fb);
+    fields.push_back(buf_field("float* __restrict__ C", node_buf[t]));
+    fields.push_back(buf_field("unsigned* err", out->err_buf));
+    fields.push_back(i64_field("M", M));
+    fields.push_back(i64_field("N", N));
+    fields.push_back(i64_field("K", K));
+    src << "// matmul " << gi << " on tensor cores (tf32): [" << M << "x" << K << "] . [" << K << "x" << N << "], A "
+        << (ti.a_mn ? "MN" : "K") << "-major from n" << g.ts[ti.va].uid << ", B " << (ti.b_mn ? "MN" : "K")
+        << "-major from n" << g.ts[ti.vb].uid << "\n";
+    src << "struct " << F << " {\n";
+    emit_struct(fields);
+    src << "  static constexpr bool A_MN = " << (ti.a_mn ? "true" : "false") << ", B_MN = " << (ti.b_mn ? "true" : "false")
+        << ";\n};\n";
+    src << "extern \"C\" __global__ void __launch_bounds__(192, 1) " << fn << "(const __grid_constant__ " << F
+        << "::P p) { ccb::matmul_tc<" << F << ">(p); }\n\n";
+    LaunchSpec& l = add_launch(fn, fields);
+    l.mode = GM_PERSISTENT;
+    l.work = ((M + 127) / 128) * ((N + 255) / 256);
+    l.per_block = 1;
+    l.block = 192;
+    l.smem = 4 * (128 * 32 * 4 + 256 * 32 * 4) + 1024 + 256;
+  }
+
   void generate(Lowered& o) {
     out = &o;
     o.name = g.name;
@@ -1833,6 +2063,7 @@ class Lowerer {
         case G_RED_ROWS: emit_red_rows(gi); break;
         case G_SCATTER: emit_scatter(gi); break;
         case G_MATMUL: emit_matmul(gi); break;
+        case G_MATMUL_TC: emit_matmul_tc(gi); break;
       }
     }
     for (auto& op : g.outputs) {

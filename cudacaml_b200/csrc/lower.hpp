@@ -42,8 +42,11 @@ struct GTensor {
   int64_t numel = 1;
 };
 
+enum MatmulMode { MM_F32 = 0, MM_TF32 = 1 };
+
 struct GGraph {
   std::string name;
+  int matmul = MM_F32;  // wire "opt matmul": precision of F32 products
   std::vector<GExpr> ex;
   std::vector<GTensor> ts;
   std::vector<std::pair<std::string, int>> outputs;
@@ -63,11 +66,18 @@ struct BufSpec {
   bool zero = false;  // zero-filled once at allocation
 };
 
-enum SlotKind { SL_BUF = 0, SL_I64 = 1, SL_EPOCH = 2 };
+// SL_TMAP: a 128-byte TMA tensor map (16 words, 64-byte aligned in the
+// parameter block) over buffer `buf`, 2-D fp32, 128-byte swizzle: inner
+// extent tdim[0], outer tdim[1], outer stride tstride bytes, box tbox[0] x
+// tbox[1]. The executor encodes it against the buffer the run binds.
+enum SlotKind { SL_BUF = 0, SL_I64 = 1, SL_EPOCH = 2, SL_TMAP = 3 };
 struct Slot {
   int kind = SL_BUF;
   int buf = -1;
   int64_t val = 0;
+  int64_t tdim[2] = {0, 0};
+  int64_t tstride = 0;
+  int tbox[2] = {0, 0};
 };
 
 enum GridMode { GM_FIXED = 0, GM_PERSISTENT = 1 };

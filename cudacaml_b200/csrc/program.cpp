@@ -24,6 +24,8 @@ struct Lane {
   std::vector<CUdeviceptr> bufs;
   unsigned* host_err = nullptr;  // pinned slot the error word is copied to
   uint64_t epoch = 0;
+  // Encoded tensor maps, keyed by (launch, slot), with the base they encode.
+  std::unordered_map<int64_t, std::pair<CUdeviceptr, CUtensorMap>> tmaps;
 };
 
 struct Program {
@@ -44,6 +46,7 @@ int lane_check(Program& P, int lane) {
   if (e & 2u) m += " scatter_add index out of bounds;";
   if (e & 4u) m += " scan look-back wait gave up (bounded spin exhausted);";
   if (e & 8u) m += " bulk-copy (TMA) wait gave up (bounded spin exhausted);";
+  if (e & 16u) m += " tensor-core pipeline wait gave up (bounded spin exhausted);";
   *P.lanes[lane].host_err = 0;
   return fail(CCB_ERR_DEVICE_CHECK, m);
 }
@@ -68,6 +71,32 @@ int destroy(Program* P) {
     if (P->mod) d.cuModuleUnload(P->mod);
   }
   delete P;
+  return CCB_OK;
+}
+
+// The TMA tensor map of slot `sl` over the buffer at `base`, encoded once per
+// (lane, launch, slot, base). A base that is not 16-byte aligned cannot be
+// described to the copy engine and is rejected.
+int tensor_map(Lane& ln, int64_t key, const Slot& sl, CUdeviceptr base, const CUtensorMap*& out) {
+  auto it = ln.tmaps.find(key);
+  if (it != ln.tmaps.end() && it->second.first == base) {
+    out = &it->second.second;
+    return CCB_OK;
+  }
+  if (base & 15)
+    return fail(CCB_ERR_INVALID, "tensor-core matmul operand at a device address that is not 16-byte aligned");
+  CUtensorMap m;
+  const cuuint64_t dims[2] = {(cuuint64_t)sl.tdim[0], (cuuint64_t)sl.tdim[1]};
+  const cuuint64_t strides[1] = {(cuuint64_t)sl.tstride};
+  const cuuint32_t box[2] = {(cuuint32_t)sl.tbox[0], (cuuint32_t)sl.tbox[1]};
+  const cuuint32_t estr[2] = {1, 1};
+  CCB_CU(driver().cuTensorMapEncodeTiled(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void*)base, dims, strides, box, estr,
+                                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE));
+  auto& slot = ln.tmaps[key];
+  slot.first = base;
+  slot.second = m;
+  out = &slot.second;
   return CCB_OK;
 }
 
@@ -114,11 +143,19 @@ int issue(Program& P, int lane, const void* const* h_in, void* const* h_out, con
       continue;
     }
     const LaunchSpec& l = P.L.launches[op.launch];
-    blk.assign(l.slots.size(), 0);
+    blk.clear();
     for (size_t s = 0; s < l.slots.size(); ++s) {
       const Slot& sl = l.slots[s];
-      blk[s] = sl.kind == SL_BUF ? (uint64_t)ptr[sl.buf] : sl.kind == SL_I64 ? (uint64_t)sl.val : ln.epoch;
+      if (sl.kind == SL_TMAP) {
+        const CUtensorMap* m = nullptr;
+        CCB_TRY(tensor_map(ln, op.launch * 64 + (int64_t)s, sl, ptr[sl.buf], m));
+        const uint64_t* w = reinterpret_cast<const uint64_t*>(m);
+        blk.insert(blk.end(), w, w + 16);
+        continue;
+      }
+      blk.push_back(sl.kind == SL_BUF ? (uint64_t)ptr[sl.buf] : sl.kind == SL_I64 ? (uint64_t)sl.val : ln.epoch);
     }
+    blk.resize((blk.size() + 7) & ~(size_t)7, 0);  // a block with tensor maps is padded to 64 bytes
     void* args[] = {blk.data()};
     CCB_CU(d.cuLaunchKernel(P.fns[op.launch], P.gx[op.launch], P.gy[op.launch], 1, l.block, 1, 1, (unsigned)l.smem, stream,
                             args, nullptr));

@@ -8,6 +8,7 @@ every expression node is written once, before its users, under its own id.
 
     ccbgraph 1
     name <graph name>
+    opt matmul <f32|tf32>                optional; F32 product precision (default f32)
     e <eid> <dtype> const <value>        f32/f64 value = IEEE-754 double bits (hex)
     e <eid> <dtype> arg <i>
     e <eid> i32 index
@@ -41,8 +42,18 @@ def _const_text(e: Expr) -> str:
     return str(int(e.value))
 
 
-def to_wire(g: Graph) -> str:
+MATMUL_PRECISIONS = ("f32", "tf32")
+
+
+def to_wire(g: Graph, matmul: str = "f32") -> str:
+    """``matmul`` selects how F32 products are computed: "f32" keeps F32
+    arithmetic (the reference's), "tf32" runs them on the tensor cores with
+    TF32 operands and F32 accumulation (error bound in ccb_skel.cuh)."""
+    if matmul not in MATMUL_PRECISIONS:
+        raise ValueError(f"matmul precision must be one of {MATMUL_PRECISIONS}, got {matmul!r}")
     lines = ["ccbgraph 1", f"name {_check_name(g.name)}"]
+    if matmul != "f32":
+        lines.append(f"opt matmul {matmul}")
     written = set()
 
     def emit_expr(root: Expr):

@@ -1,0 +1,102 @@
+"""F32 products on the tcgen05 tensor cores (graphs compiled with
+matmul="tf32"), through libccb.so.
+
+The reference computes F32 products with F32 FMAs in ascending k
+(lib/lower/lower.ml:806-958; the interpreter's sequential fold,
+lib/backend_interp/cudacaml_backend_interp.ml:407-433). The tensor-core path
+reads TF32 operands (10 explicit mantissa bits) and accumulates in F32, so
+it is held to the componentwise bound stated with the kernel:
+
+    |C - C_exact| <= (2^-9 + K * 2^-23) * sum_k |A[r,k]| |B[k,c]|
+
+with C_exact the F64 product of the same F32 inputs. Shapes cover whole and
+partial 128 x 256 output tiles, a partial 32-wide k-step, all four operand
+orders (row-major and transposed views), and more tiles than SMs, so the
+persistent CTAs reuse both TMEM accumulators.
+"""
+import numpy as np
+import pytest
+
+from cudacaml_b200 import backend_cuda as cuda
+from cudacaml_b200 import differential as Diff
+from cudacaml_b200 import dsl as D
+from cudacaml_b200 import examples as X
+from cudacaml_b200.ir import F32, Graph, Value
+from oracle import interp
+
+pytestmark = pytest.mark.gpu
+
+
+def tf32_bound(c, a, b):
+    exact = a.astype(np.float64) @ b.astype(np.float64)
+    mag = np.abs(a.astype(np.float64)) @ np.abs(b.astype(np.float64))
+    lim = (2.0 ** -9 + a.shape[1] * 2.0 ** -23) * mag + 1e-30
+    return np.abs(c.astype(np.float64) - exact) / lim
+
+
+SHAPES = [(128, 64, 256), (300, 200, 260), (2048, 256, 4096), (4096, 64, 4096)]
+
+
+@pytest.mark.parametrize("m,k,n", SHAPES, ids=lambda v: str(v))
+@pytest.mark.parametrize("ta,tb", [(False, False), (True, False), (False, True), (True, True)],
+                         ids=["AB", "AtB", "ABt", "AtBt"])
+def test_tf32_product_within_bound(m, k, n, ta, tb):
+    rng = np.random.default_rng(m * 7 + k * 13 + n + 2 * ta + tb)
+    a = rng.standard_normal((m, k)).astype(np.float32)
+    b = rng.standard_normal((k, n)).astype(np.float32)
+    pa = D.param("a", F32, (k, m) if ta else (m, k))
+    pb = D.param("b", F32, (n, k) if tb else (k, n))
+    g = Graph("tc", [("c", D.matmul(D.transpose(pa) if ta else pa, D.transpose(pb) if tb else pb))])
+    c = cuda.compile(g, matmul="tf32")
+    try:
+        assert "launch ccb_matmultc_" in c.plan()
+        ins = [("a", Value.of_array(F32, pa.shape, np.ascontiguousarray(a.T if ta else a))),
+               ("b", Value.of_array(F32, pb.shape, np.ascontiguousarray(b.T if tb else b)))]
+        out = dict(cuda.run(c, ins))["c"].data.reshape(m, n)
+        ratio = tf32_bound(out, a, b)
+        worst = np.unravel_index(int(np.argmax(ratio)), ratio.shape)
+        assert ratio.max() <= 1.0, f"error/bound {ratio.max():.3g} at {worst}"
+        # the same graph twice in a row gives the same bits (no stale accumulator)
+        again = dict(cuda.run(c, ins))["c"].data.reshape(m, n)
+        assert np.array_equal(out, again)
+    finally:
+        cuda.release(c)
+
+
+def test_tf32_exact_on_small_integers():
+    # integers below 2^10 are exact in TF32 and every partial sum is exact in F32
+    m, k, n = 256, 96, 512
+    a = (np.arange(m * k) % 13 - 6).astype(np.float32).reshape(m, k)
+    b = (np.arange(k * n) % 11 - 5).astype(np.float32).reshape(k, n)
+    g = Graph("ti", [("c", D.matmul(D.param("a", F32, (m, k)), D.param("b", F32, (k, n))))])
+    c = cuda.compile(g, matmul="tf32")
+    out = dict(cuda.run(c, [("a", Value.of_array(F32, (m, k), a)), ("b", Value.of_array(F32, (k, n), b))]))["c"]
+    assert np.array_equal(out.data.reshape(m, n), (a.astype(np.float64) @ b.astype(np.float64)).astype(np.float32))
+    cuda.release(c)
+
+
+class _Tf32:
+    """The CUDA backend with TF32 products, as a Differential candidate."""
+    name = "cuda-tf32"
+
+    @staticmethod
+    def compile(g):
+        return cuda.compile(g, matmul="tf32")
+
+    @staticmethod
+    def run(c, inputs):
+        return cuda.run(c, inputs)
+
+
+def test_mlp_step_tf32_vs_interp():
+    # the benchmark's MLP step at 1/32 of its size: loss and both weight
+    # gradients within 1e-2 of the F32 interpreter (Differential band)
+    bsz, din, hid, dout = 256, 128, 256, 32
+    g = X.mlp_step(bsz, din, hid, dout)
+    rng = np.random.default_rng(3)
+    scale = {"X": 1.0, "W1": din ** -0.5, "W2": hid ** -0.5, "T": 1.0}
+    shapes = {"X": (bsz, din), "W1": (din, hid), "W2": (hid, dout), "T": (bsz, dout)}
+    ins = [(nm, Value.of_array(F32, shapes[nm], (rng.standard_normal(shapes[nm]) * scale[nm]).astype(np.float32)))
+           for nm in ("X", "W1", "W2", "T")]
+    err = Diff.check(interp, _Tf32, g, ins, tolerance=1e-2)
+    assert err is None, err

@@ -114,3 +114,51 @@ def test_no_device_is_reported_not_crashed():
         pytest.skip("a device is present")
     with pytest.raises(R.CcbError):
         B.compile(X.saxpy(8, 2.0))
+
+
+# ---------------------------------------------------------------- tensor-core products
+def _tc_lines(info):
+    return [ln for ln in info["source"].splitlines() if ln.startswith("// matmul") and "tensor cores" in ln]
+
+
+def test_matmul_precision_option_and_default():
+    g = X.mlp_step(512, 256, 512, 128)
+    assert "matmultc" not in B.lower_info(g)["plan"]  # F32 arithmetic unless asked
+    info = B.lower_info(g, matmul="tf32")
+    assert info["plan"].count("launch ccb_matmultc_") == 5
+    assert info["launches"] == 8  # 5 products + A1, dY(+loss), dZ1 element passes
+    with pytest.raises(ValueError):
+        B.lower_info(g, matmul="bf16")
+    assert nvrtc_ok(info["source"], "mlp_tf32") > 0
+
+
+def test_tensor_core_operand_views():
+    a = D.param("a", F32, (256, 512))   # used transposed: A^T is [512 x 256], stored [K][M]
+    b = D.param("b", F32, (256, 384))   # B [K][N] row-major
+    w = D.param("w", F32, (256, 384))   # used transposed as B: stored [N][K]
+    g = Graph("v", [("c", D.matmul(D.transpose(a), b)), ("d", D.matmul(b, D.transpose(w)))])
+    lines = _tc_lines(B.lower_info(g, matmul="tf32"))
+    assert len(lines) == 2
+    assert f"A MN-major from n{a.uid}" in lines[0] and f"B MN-major from n{b.uid}" in lines[0]
+    assert f"A K-major from n{b.uid}" in lines[1] and f"B K-major from n{w.uid}" in lines[1]
+
+
+def test_tensor_core_operand_expression_is_materialised():
+    a = D.param("a", F32, (256, 256))
+    b = D.param("b", F32, (256, 256))
+    e = D.map(lambda v: D.exp(v), a)
+    g = Graph("m", [("c", D.matmul(D.transpose(e), b))])
+    info = B.lower_info(g, matmul="tf32")
+    # exp(a) is written once by an element pass, then read transposed by TMA
+    assert info["plan"].count("launch ccb_mapreduce_") == 1
+    assert len(_tc_lines(info)) == 1 and "A MN-major" in _tc_lines(info)[0]
+
+
+def test_tensor_core_eligibility():
+    def mm(dt, m, k, n):
+        return Graph("e", [("c", D.matmul(D.param("a", dt, (m, k)), D.param("b", dt, (k, n))))])
+    assert _tc_lines(B.lower_info(mm(F32, 256, 256, 256), matmul="tf32"))
+    assert not _tc_lines(B.lower_info(mm(F64, 256, 256, 256), matmul="tf32"))   # no f64 kind
+    assert not _tc_lines(B.lower_info(mm(F32, 16, 16, 16), matmul="tf32"))      # tiny: exact kernel
+    assert not _tc_lines(B.lower_info(mm(F32, 256, 255, 256), matmul="tf32"))   # 1020-byte rows: no TMA
+    assert not _tc_lines(B.lower_info(mm(F32, 4, 4096, 4), matmul="tf32"))      # split-K reduction
