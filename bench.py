@@ -593,6 +593,12 @@ def run_profile_case(args):
         c = B.compile(X.gather(n, tbl))
         ins = [("idx", Value.of_array(I32, (n,), (X.philox_word0(4, n) & (tbl - 1)).astype(np.int32))),
                ("table", Value.of_array(F32, (tbl,), np.full(tbl, 0.5, np.float32)))]
+    elif args.profile == "mm_tf32":  # one square tensor-core product
+        a = D.param("a", F32, (n, n))
+        bm = D.param("b", F32, (n, n))
+        c = B.compile(Graph("mm", [("c", D.matmul(a, bm))]), matmul="tf32")
+        rng = np.random.default_rng(0)
+        ins = [(nm, Value.of_array(F32, (n, n), rng.standard_normal(n * n).astype(np.float32))) for nm in ("a", "b")]
     else:  # mlp at a reduced size
         b = n
         c = B.compile(X.mlp_step(b, b // 2, b, b // 8), matmul="tf32" if args.profile == "mlp_tf32" else "f32")
@@ -614,7 +620,7 @@ def main():
     ap.add_argument("--no-secondary", action="store_true")
     ap.add_argument("--profile", default=None,
                     choices=["greeks64", "greeks32", "reduce", "scan", "rows_reduce", "rows_scan", "scatter", "gather", "mlp",
-                             "mlp_tf32"],
+                             "mlp_tf32", "mm_tf32"],
                     help="run a small fixed case (3 launches) for an ncu capture, no timing")
     ap.add_argument("--size", type=int, default=1 << 24, help="paths/elements of the --profile case")
     args = ap.parse_args()

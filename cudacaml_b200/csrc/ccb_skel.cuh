@@ -918,7 +918,8 @@ __device__ __forceinline__ void matmul_tiled(const typename F::P& p) {
 //
 // Operands arrive as views of materialised row-major buffers: A is K-major
 // (A[r][k] at r*K+k) or MN-major (at k*M+r); B is MN-major (B[k][c] at
-// k*N+c) or K-major (at c*K+k). Out-of-range tile rows and k-steps read as
+// k*N+c) or K-major (at c*K+k). K-major tiles are loaded with the 128-byte
+// swizzle, MN-major tiles with the 128-byte swizzle of 32-byte atoms. Out-of-range tile rows and k-steps read as
 // zero (TMA fill), so any M, N, K >= 1 is exact in shape; stores are masked.
 //
 // Numerics: TF32 operands (10 explicit mantissa bits), FP32 accumulation.
@@ -957,10 +958,23 @@ __device__ __forceinline__ void tma_load_2d(unsigned dst, const TmaDesc* map, in
 __device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
-// Shared-memory matrix descriptor, SWIZZLE_128B, version 1 (sm_100).
-__device__ __forceinline__ u64 sdesc(unsigned saddr, unsigned lbo, unsigned sbo) {
+// Shared-memory matrix descriptor, version 1 (sm_100). Layout 2 is the
+// 128-byte swizzle with 16-byte atoms (K-major operands); layout 1 the
+// 128-byte swizzle with 32-byte atoms, the only one UMMA accepts for
+// MN-major 32-bit operands.
+constexpr unsigned LAYOUT_SW128 = 2u, LAYOUT_SW128_BASE32B = 1u;
+__device__ __forceinline__ u64 sdesc(unsigned saddr, unsigned lbo, unsigned sbo, unsigned layout) {
   return (u64)((saddr >> 4) & 0x3FFFu) | ((u64)((lbo >> 4) & 0x3FFFu) << 16) | ((u64)((sbo >> 4) & 0x3FFFu) << 32) |
-         (1ull << 46) | (2ull << 61);
+         (1ull << 46) | ((u64)layout << 61);
+}
+// K-major tile: 128-byte rows, 8-row groups 1024 bytes apart; k-step kk
+// (8 tf32 = 32 bytes) starts kk*32 bytes into the swizzle atom.
+__device__ __forceinline__ u64 desc_k(unsigned tile, int kk) { return sdesc(tile + kk * 32u, 16u, 1024u, LAYOUT_SW128); }
+// MN-major tile: 32-element (128-byte) rows along MN, one row per k; 4-row
+// atoms 512 bytes apart (SBO) and 32-element MN blocks 4096 bytes apart (LBO);
+// k-step kk covers rows 8kk..8kk+7.
+__device__ __forceinline__ u64 desc_mn(unsigned tile, int kk) {
+  return sdesc(tile + kk * 1024u, 4096u, 512u, LAYOUT_SW128_BASE32B);
 }
 __device__ __forceinline__ void mma(unsigned d, u64 a, u64 b, unsigned idesc, unsigned accumulate) {
   const unsigned z = 0;
@@ -1086,8 +1100,8 @@ __device__ __forceinline__ void matmul_tc(const typename F::P& p) {
           const unsigned sa = sbase + stage * STAGE_BYTES, sb = sa + A_BYTES;
 #pragma unroll
           for (int kk = 0; kk < BK / 8; ++kk) {
-            const u64 a = F::A_MN ? sdesc(sa + kk * 1024u, 4096u, 1024u) : sdesc(sa + kk * 32u, 16u, 1024u);
-            const u64 b = F::B_MN ? sdesc(sb + kk * 1024u, 4096u, 1024u) : sdesc(sb + kk * 32u, 16u, 1024u);
+            const u64 a = F::A_MN ? desc_mn(sa, kk) : desc_k(sa, kk);
+            const u64 b = F::B_MN ? desc_mn(sb, kk) : desc_k(sb, kk);
             mma(d, a, b, idesc, (ks | kk) != 0 ? 1u : 0u);
           }
           commit(&empty[stage]);

@@ -1996,6 +1996,7 @@ class Lowerer {
     fa.slot.tbox[0] = 32;
     if (ti.a_mn) {  // A^T stored [K][M]: 32 x 32 boxes, four per 128-row tile
       fa.slot.tdim[0] = M, fa.slot.tdim[1] = K, fa.slot.tstride = M * 4, fa.slot.tbox[1] = 32;
+      fa.slot.tswizzle = (int)CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
     } else {  // A stored [M][K]: one 32 x 128 box
       fa.slot.tdim[0] = K, fa.slot.tdim[1] = M, fa.slot.tstride = K * 4, fa.slot.tbox[1] = 128;
     }
@@ -2005,6 +2006,7 @@ class Lowerer {
     fb.slot.tbox[0] = 32;
     if (ti.b_mn) {  // B stored [K][N]: 32 x 32 boxes, eight per 256-column tile
       fb.slot.tdim[0] = N, fb.slot.tdim[1] = K, fb.slot.tstride = N * 4, fb.slot.tbox[1] = 32;
+      fb.slot.tswizzle = (int)CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
     } else {  // B^T stored [N][K]: one 32 x 256 box
       fb.slot.tdim[0] = K, fb.slot.tdim[1] = N, fb.slot.tstride = K * 4, fb.slot.tbox[1] = 256;
     }

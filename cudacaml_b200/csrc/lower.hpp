@@ -67,7 +67,7 @@ struct BufSpec {
 };
 
 // SL_TMAP: a 128-byte TMA tensor map (16 words, 64-byte aligned in the
-// parameter block) over buffer `buf`, 2-D fp32, 128-byte swizzle: inner
+// parameter block) over buffer `buf`, 2-D fp32, swizzle `tswizzle`: inner
 // extent tdim[0], outer tdim[1], outer stride tstride bytes, box tbox[0] x
 // tbox[1]. The executor encodes it against the buffer the run binds.
 enum SlotKind { SL_BUF = 0, SL_I64 = 1, SL_EPOCH = 2, SL_TMAP = 3 };
@@ -78,6 +78,7 @@ struct Slot {
   int64_t tdim[2] = {0, 0};
   int64_t tstride = 0;
   int tbox[2] = {0, 0};
+  int tswizzle = 3;  // CUtensorMapSwizzle: 3 = 128B, 4 = 128B with 32-byte atoms
 };
 
 enum GridMode { GM_FIXED = 0, GM_PERSISTENT = 1 };

@@ -91,7 +91,7 @@ int tensor_map(Lane& ln, int64_t key, const Slot& sl, CUdeviceptr base, const CU
   const cuuint32_t box[2] = {(cuuint32_t)sl.tbox[0], (cuuint32_t)sl.tbox[1]};
   const cuuint32_t estr[2] = {1, 1};
   CCB_CU(driver().cuTensorMapEncodeTiled(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void*)base, dims, strides, box, estr,
-                                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                         CU_TENSOR_MAP_INTERLEAVE_NONE, (CUtensorMapSwizzle)sl.tswizzle,
                                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE));
   auto& slot = ln.tmaps[key];
   slot.first = base;

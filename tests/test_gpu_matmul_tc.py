@@ -18,7 +18,6 @@ import numpy as np
 import pytest
 
 from cudacaml_b200 import backend_cuda as cuda
-from cudacaml_b200 import differential as Diff
 from cudacaml_b200 import dsl as D
 from cudacaml_b200 import examples as X
 from cudacaml_b200.ir import F32, Graph, Value
@@ -75,22 +74,12 @@ def test_tf32_exact_on_small_integers():
     cuda.release(c)
 
 
-class _Tf32:
-    """The CUDA backend with TF32 products, as a Differential candidate."""
-    name = "cuda-tf32"
-
-    @staticmethod
-    def compile(g):
-        return cuda.compile(g, matmul="tf32")
-
-    @staticmethod
-    def run(c, inputs):
-        return cuda.run(c, inputs)
-
-
 def test_mlp_step_tf32_vs_interp():
-    # the benchmark's MLP step at 1/32 of its size: loss and both weight
-    # gradients within 1e-2 of the F32 interpreter (Differential band)
+    """The benchmark's MLP step at 1/32 of its size against the F32
+    interpreter. Gradient entries are sums of 256 signed products, so near-zero
+    entries carry the absolute TF32 error of their large terms: the check is
+    normwise, max|g - e| <= 1e-2 * max|e| per output (the elementwise bound is
+    tested on the products above)."""
     bsz, din, hid, dout = 256, 128, 256, 32
     g = X.mlp_step(bsz, din, hid, dout)
     rng = np.random.default_rng(3)
@@ -98,5 +87,13 @@ def test_mlp_step_tf32_vs_interp():
     shapes = {"X": (bsz, din), "W1": (din, hid), "W2": (hid, dout), "T": (bsz, dout)}
     ins = [(nm, Value.of_array(F32, shapes[nm], (rng.standard_normal(shapes[nm]) * scale[nm]).astype(np.float32)))
            for nm in ("X", "W1", "W2", "T")]
-    err = Diff.check(interp, _Tf32, g, ins, tolerance=1e-2)
-    assert err is None, err
+    expected = dict(interp.run(interp.compile(g), ins))
+    c = cuda.compile(g, matmul="tf32")
+    assert c.plan().count("launch ccb_matmultc_") == 5
+    got = dict(cuda.run(c, ins))
+    cuda.release(c)
+    for name, e in expected.items():
+        ev = e.data.astype(np.float64)
+        gv = got[name].data.astype(np.float64)
+        rel = np.max(np.abs(gv - ev)) / np.max(np.abs(ev))
+        assert rel <= 1e-2, f"{name}: normwise error {rel:.3g}"
