@@ -328,6 +328,13 @@ struct KCtx {
     return index_node;
   }
   int bin(Dt dt, int op, int a, int b) {
+    if (dt == DT_I32 && (op == B_ADD || op == B_SUB || op == B_MUL || op == B_DIV)) {
+      const int r = affine_bin(op, a, b);
+      if (r >= 0) return r;
+    }
+    return raw_bin(dt, op, a, b);
+  }
+  int raw_bin(Dt dt, int op, int a, int b) {
     KN k;
     k.op = K_BIN;
     k.dt = dt;
@@ -335,6 +342,125 @@ struct KCtx {
     k.a = a;
     k.b = b;
     return mk(k);
+  }
+
+  // ---- exact affine forms of I32 values
+  // An I32 value built from additions, subtractions and constant multiples
+  // is kept as sum(c_j * atom_j) + k over "atoms" (nodes of any other kind),
+  // in ascending atom order, so every spelling of the same index arithmetic
+  // ((4i+1)/4, i + 2^22 - 2^22, ...) lands on one node. Coefficients wrap
+  // modulo 2^32 exactly as the I32 arithmetic they replace. A division by a
+  // positive constant is resolved only when value ranges prove it exact:
+  // the numerator is non-negative (truncation = floor) and its part that is
+  // not a multiple of the divisor stays inside [0, d).
+  struct Aff {
+    std::vector<std::pair<int, int64_t>> t;  // (atom node, coefficient)
+    int64_t k = 0;
+  };
+  std::unordered_map<int, Aff> aff;  // sum nodes built by affine_build -> form
+
+  static int64_t w32(int64_t v) { return (int64_t)(int32_t)(uint32_t)(uint64_t)v; }
+  Aff aff_of(int id) const {
+    Aff f;
+    if (n[id].op == K_CONST) {
+      f.k = n[id].iv;
+      return f;
+    }
+    auto it = aff.find(id);
+    if (it != aff.end()) return it->second;
+    f.t.push_back({id, 1});
+    return f;
+  }
+  static Aff aff_add(const Aff& a, const Aff& b, int64_t sb) {
+    Aff r;
+    size_t i = 0, j = 0;
+    while (i < a.t.size() || j < b.t.size()) {
+      int id;
+      int64_t c;
+      if (j >= b.t.size() || (i < a.t.size() && a.t[i].first < b.t[j].first)) {
+        id = a.t[i].first, c = a.t[i].second, ++i;
+      } else if (i >= a.t.size() || b.t[j].first < a.t[i].first) {
+        id = b.t[j].first, c = w32(sb * b.t[j].second), ++j;
+      } else {
+        id = a.t[i].first, c = w32(a.t[i].second + sb * b.t[j].second), ++i, ++j;
+      }
+      if (c != 0) r.t.push_back({id, c});
+    }
+    r.k = w32(a.k + sb * b.k);
+    return r;
+  }
+  static Aff aff_scale(const Aff& a, int64_t c) {
+    Aff r;
+    c = w32(c);
+    if (c == 0) return r;
+    for (auto& tm : a.t) {
+      const int64_t v = w32(tm.second * c);
+      if (v) r.t.push_back({tm.first, v});
+    }
+    r.k = w32(a.k * c);
+    return r;
+  }
+  // The exact (unwrapped) range of the form's value, when every atom is ranged.
+  bool aff_range(const Aff& f, int64_t& lo, int64_t& hi) const {
+    lo = hi = f.k;
+    for (auto& tm : f.t) {
+      const KN& x = n[tm.first];
+      if (!x.ranged) return false;
+      const int64_t c = tm.second, e1 = c * x.lo, e2 = c * x.hi;
+      lo += std::min(e1, e2);
+      hi += std::max(e1, e2);
+      if (lo < -(int64_t(1) << 40) || hi > (int64_t(1) << 40)) return false;
+    }
+    return true;
+  }
+  int affine_build(const Aff& f) {
+    if (f.t.empty()) return cint(DT_I32, f.k);
+    if (f.t.size() == 1 && f.t[0].second == 1 && f.k == 0) return f.t[0].first;
+    int acc = -1;
+    for (auto& tm : f.t) {
+      const int64_t c = tm.second;
+      if (c == -1 && acc >= 0) {
+        acc = raw_bin(DT_I32, B_SUB, acc, tm.first);
+        continue;
+      }
+      const int term = c == 1 ? tm.first : raw_bin(DT_I32, B_MUL, tm.first, cint(DT_I32, c));
+      acc = acc < 0 ? term : raw_bin(DT_I32, B_ADD, acc, term);
+    }
+    if (f.k > 0 || f.k == INT32_MIN) acc = raw_bin(DT_I32, B_ADD, acc, cint(DT_I32, f.k));
+    else if (f.k < 0) acc = raw_bin(DT_I32, B_SUB, acc, cint(DT_I32, -f.k));
+    if (n[acc].op != K_CONST) aff[acc] = f;
+    return acc;
+  }
+  int affine_bin(int op, int a, int b) {
+    const Aff fa = aff_of(a), fb = aff_of(b);
+    const bool ca = fa.t.empty(), cb = fb.t.empty();
+    if (ca && cb) return -1;  // constant folding
+    switch (op) {
+      case B_ADD: return affine_build(aff_add(fa, fb, 1));
+      case B_SUB: return affine_build(aff_add(fa, fb, -1));
+      case B_MUL:
+        if (ca) return affine_build(aff_scale(fb, fa.k));
+        if (cb) return affine_build(aff_scale(fa, fb.k));
+        return -1;
+      case B_DIV: {
+        if (!cb || fb.k <= 0) return -1;
+        const int64_t d = fb.k;
+        int64_t lo, hi;
+        if (!aff_range(fa, lo, hi) || lo < 0 || hi > INT32_MAX) return -1;
+        Aff y, rest;
+        for (auto& tm : fa.t) {
+          if (tm.second % d == 0) y.t.push_back({tm.first, tm.second / d});
+          else rest.t.push_back(tm);
+        }
+        const int64_t q = fa.k >= 0 ? fa.k / d : -((-fa.k + d - 1) / d);
+        rest.k = fa.k - q * d;  // in [0, d)
+        int64_t rlo, rhi;
+        if (!aff_range(rest, rlo, rhi) || rlo < 0 || rhi >= d) return -1;
+        y.k = q;
+        return affine_build(y);
+      }
+      default: return -1;
+    }
   }
   int un(Dt dt, int op, int a) {
     KN k;
@@ -368,6 +494,45 @@ struct KCtx {
       k.dt = dt;
       k.iv = wrap(dt, v);
       return;
+    }
+    auto is_k = [&](int id) { return id >= 0 && n[id].op == K_CONST && !is_float(n[id].dt); };
+    auto to_bool = [&](bool v) {
+      k = KN();
+      k.op = K_CONST;
+      k.dt = DT_BOOL;
+      k.iv = v ? 1 : 0;
+    };
+    if (k.op == K_CMP && is_k(k.a) && is_k(k.b)) {
+      const int64_t x = n[k.a].iv, y = n[k.b].iv;
+      const int c = k.sub;
+      to_bool(c == C_EQ ? x == y : c == C_NE ? x != y : c == C_LT ? x < y : c == C_LE ? x <= y : c == C_GT ? x > y : x >= y);
+      return;
+    }
+    if (k.op == K_NOT && is_k(k.a)) {
+      to_bool(n[k.a].iv == 0);
+      return;
+    }
+    if (k.op == K_LOGIC && is_k(k.a) && is_k(k.b)) {
+      const bool x = n[k.a].iv != 0, y = n[k.b].iv != 0;
+      to_bool(k.sub == 0 ? (x && y) : (x || y));
+      return;
+    }
+    if (k.op == K_SELECT && (is_k(k.a) || k.b == k.c)) {
+      const int pick = k.b == k.c ? k.b : (n[k.a].iv != 0 ? k.b : k.c);
+      k = n[pick];
+      return;
+    }
+    // one spelling for commuted operands: a+b = b+a and a*b = b*a exactly,
+    // in IEEE arithmetic as in wrapping integers
+    if (k.op == K_BIN && k.a > k.b &&
+        (k.sub == B_ADD || k.sub == B_MUL || (is_int(k.dt) && (k.sub == B_AND || k.sub == B_OR || k.sub == B_XOR))))
+      std::swap(k.a, k.b);
+    if (k.op == K_BIN && k.sub == B_MUL && is_float(k.dt)) {  // x * 1.0 == x exactly, NaN and -0 included
+      auto one = [&](int id) { return n[id].op == K_CONST && n[id].f == 1.0; };
+      if (one(k.a) || one(k.b)) {
+        k = n[one(k.a) ? k.b : k.a];
+        return;
+      }
     }
     if (k.op != K_BIN || !is_int(k.dt)) return;
     if (n[k.a].op == K_CONST && n[k.b].op == K_CONST) {
@@ -656,10 +821,14 @@ struct Emitter {
       out = lit(t);
       return true;
     }
-    if (k.op == K_BIN && k.sub == B_AND && k.dt == DT_I64 && c.n[k.b].op == K_CONST && c.n[k.b].iv == 0xFFFFFFFFLL &&
-        c.n[k.a].op == K_CAST && c.n[c.n[k.a].a].dt == DT_I32) {
-      out = val(c.n[k.a].a);
-      return true;
+    if (k.op == K_BIN && k.sub == B_AND && k.dt == DT_I64) {  // either operand order (AND is commutative)
+      for (int s = 0; s < 2; ++s) {
+        const int m = s ? k.a : k.b, v = s ? k.b : k.a;
+        if (c.n[m].op == K_CONST && c.n[m].iv == 0xFFFFFFFFLL && c.n[v].op == K_CAST && c.n[c.n[v].a].dt == DT_I32) {
+          out = val(c.n[v].a);
+          return true;
+        }
+      }
     }
     return false;
   }
@@ -1585,6 +1754,15 @@ class Lowerer {
     for (int b : direct) src << " && ccb::aligned16(p.b" << b << ")";
     for (auto& s : gr.stores) src << " && ccb::aligned16(p.o" << s.first << ")";
     src << ";\n  }\n";
+    // Reductions of one value with one combiner from one identity (the two
+    // halves of a symmetric X^T X, say) are accumulated once.
+    std::vector<int> alias(R, -1);
+    for (int r = 0; r < R; ++r)
+      for (int q = 0; q < r && alias[r] < 0; ++q) {
+        const Red &a = gr.reds[q], &b = gr.reds[r];
+        auto comb = [&](const Red& x) { return (x.comb_t < 0 || is_plain_add(x.comb_t)) ? -1 : x.comb_t; };
+        if (alias[q] < 0 && a.var == b.var && a.init == b.init && a.dt == b.dt && comb(a) == comb(b)) alias[r] = q;
+      }
     // elem
     src << "  static __device__ __forceinline__ void elem(const P& p, int i, acc_t* acc) {\n";
     {
@@ -1594,6 +1772,7 @@ class Lowerer {
         src << "    p.o" << s.first << "[i] = " << v << ";\n";
       }
       for (int r = 0; r < R; ++r) {
+        if (alias[r] >= 0) continue;
         std::string v = e.val(gr.reds[r].var);
         src << "    acc[" << r << "] = combine(" << r << ", acc[" << r << "], " << v << ");\n";
       }
@@ -1614,6 +1793,7 @@ class Lowerer {
         src << "    S" << s.first << ".v[" << j << "] = " << v << ";\n";
       }
       for (int r = 0; r < R; ++r) {
+        if (alias[r] >= 0) continue;
         std::string v = e.val(gr.reds[r].var);
         src << "    acc[" << r << "] = combine(" << r << ", acc[" << r << "], " << v << ");\n";
       }
@@ -1628,11 +1808,12 @@ class Lowerer {
       for (int r = 0; r < R; ++r) {
         const Red& rd = gr.reds[r];
         std::string fv = "f" + std::to_string(r);
+        const std::string rv = "res[" + std::to_string(alias[r] >= 0 ? alias[r] : r) + "]";
         if (rd.inv >= 0) {
           std::string iv = e.val(rd.inv);
-          src << "    const acc_t " << fv << " = " << bin_text(acc, B_MUL, iv, "res[" + std::to_string(r) + "]") << ";\n";
+          src << "    const acc_t " << fv << " = " << bin_text(acc, B_MUL, iv, rv) << ";\n";
         } else {
-          src << "    const acc_t " << fv << " = res[" << r << "];\n";
+          src << "    const acc_t " << fv << " = " << rv << ";\n";
         }
         e.redval.push_back(fv);
         src << "    p.o" << rd.t << "[" << rd.elem << "] = " << fv << ";\n";
