@@ -349,6 +349,29 @@ def test_flat_scan_max_and_repeat_runs():
         assert np.array_equal(got, np.maximum.accumulate(x))
 
 
+@pytest.mark.parametrize("n", [1 << 20, (1 << 20) + 32, 3 * 296 * 8192 + 96, (1 << 24) + 4096])
+def test_flat_scan_large_i32_exact(n):
+    # larger flat scans: a partial last tile, a few hundred tiles, thousands of
+    # tiles; bit-exact I32, three launches of one program (epoch-tagged
+    # statuses, re-armed counters)
+    x = (X.philox_word0(13, n) & 1023).astype(np.int32)
+    c = cuda.compile(X.scan_flat(n, I32))
+    want = np.cumsum(x, dtype=np.int64).astype(np.int32)
+    for _ in range(3):
+        got = dict(cuda.run(c, [("x", Value.of_array(I32, (n,), x))]))["p"].data
+        assert np.array_equal(got, want)
+
+
+def test_flat_scan_large_max_f32():
+    # a non-add combiner with a non-zero identity over many tiles
+    n = (1 << 21) + 4064
+    x = X.philox_normal(14, n)
+    v = D.param("x", F32, (n,))
+    c = cuda.compile(Graph("m", [("p", D.scan(D.max, D.const(F32, -3e38), v))]))
+    got = dict(cuda.run(c, [("x", Value.of_array(F32, (n,), x))]))["p"].data
+    assert np.array_equal(got, np.maximum.accumulate(x))
+
+
 @pytest.mark.parametrize("basis", ["scaled3", "poly4"])
 def test_lsm_drivers_match_interp(basis):
     # the generic driver over the CUDA backend, the resident CUDA driver and
