@@ -455,6 +455,85 @@ def measure_greeks(args, dtype, rank, world, local, dist, comm, flush):
             "launches": n_launch}
 
 
+def measure_mlp_dp(rank, world, local, dist, comm, flush, pk):
+    """The MLP training step data-parallel over `world` GPUs (BASELINE
+    configs: global batch 8192 split by rows, gradients combined by NCCL
+    all-reduce): per rank the tf32 step on 8192/world rows, then one grouped
+    NCCL all-reduce (sum) of loss, dW1 and dW2 on the same stream. Device time
+    per step, max over ranks; inputs device-generated, rank-specific rows."""
+    import math
+    import numpy as np
+    import torch
+    from cudacaml_b200 import backend_cuda as B
+    from cudacaml_b200 import dsl as D
+    from cudacaml_b200 import examples as X
+    from cudacaml_b200 import rng as Rng
+    from cudacaml_b200 import runtime as R
+    from cudacaml_b200.ir import F32, F64, I32, Graph, numel
+
+    L = R.lib()
+    bsz, din, hid, dout = 8192, 4096, 8192, 1024
+    per = bsz // world
+    seed_buf = R.Buffer(4)
+
+    def normal_f32(shape, seed, scale=1.0):
+        z = D.map(lambda v: D.cast(F32, D.mul(v, D.const(F64, scale))), Rng.normal(F64, D.scalar("seed", I32), shape))
+        c = B.compile_on(local, Graph("gen", [("x", z)]))
+        out = R.Buffer(4 * int(np.prod(shape)))
+        seed_buf.upload(np.array([seed], np.int32))
+        B.run_device_ptrs(c, [seed_buf.ptr], [out.ptr], None)
+        B.check_device(c, None)
+        B.release(c)
+        return out
+
+    # Set-up first; every rank agrees it succeeded before any NCCL call, so a
+    # failing rank cannot leave the others waiting inside a collective.
+    err = None
+    try:
+        named = {"X": normal_f32((per, din), 5 + 1000 * rank), "W1": normal_f32((din, hid), 6, 1.0 / math.sqrt(din)),
+                 "W2": normal_f32((hid, dout), 7, 1.0 / math.sqrt(hid)), "T": normal_f32((per, dout), 8 + 1000 * rank)}
+        c = B.compile_on(local, X.mlp_step(per, din, hid, dout), matmul="tf32")
+        outs = [R.Buffer(4 * numel(shape) if shape else 4) for _, _, shape in c.outputs]
+    except Exception as e:  # noqa: BLE001
+        err = f"{type(e).__name__}: {e}"
+    ok = torch.tensor([0.0 if err else 1.0], device=f"cuda:{local}")
+    dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+    if float(ok[0]) < 1.0:
+        return {"error": err or "set-up failed on another rank"}
+    ins = [named[nm].ptr for nm, _, _ in c.params]
+    s = c.lane_stream(0)
+    ar_bytes = sum(4 * numel(shape) for _, _, shape in c.outputs)
+
+    e0, e1, e2 = R.Event(), R.Event(), R.Event()
+    t_step, t_comp = [], []
+    for k in range(3 + 10):
+        flush(s)
+        e0.record(s)
+        B.run_device_ptrs(c, ins, [b.ptr for b in outs], s)
+        e1.record(s)
+        R.check(L.ccb_group_start())
+        for buf, (_, dt, shape) in zip(outs, c.outputs):
+            R.check(L.ccb_allreduce(comm, buf.ptr, buf.ptr, numel(shape), R.DT_CODE[dt.value], 0, s))
+        R.check(L.ccb_group_end())
+        e2.record(s)
+        e2.synchronize()
+        if k >= 3:
+            t_step.append(e0.elapsed_ms(e2))
+            t_comp.append(e0.elapsed_ms(e1))
+    B.check_device(c, s)
+    ts = torch.tensor([float(np.median(t_step)), float(np.median(t_comp))], device=f"cuda:{local}")
+    dist.all_reduce(ts, op=dist.ReduceOp.MAX)
+    ms, ms_comp = float(ts[0]), float(ts[1])
+    for b in outs + list(named.values()) + [seed_buf]:
+        b.free()
+    B.release(c)
+    fl = X.mlp_flops(bsz, din, hid, dout)
+    return {"ms": ms, "tflops": fl / ms / 1e9, "compute_ms": ms_comp, "allreduce_ms": ms - ms_comp,
+            "allreduce_bytes_per_rank": ar_bytes, "rows_per_gpu": per,
+            "note": "global batch 8192 split by rows; per rank the tf32 step then a grouped NCCL all-reduce (sum) of "
+                    "loss, dW1, dW2 on the same stream; device time, max over ranks, median of 10 after 3 warm-ups"}
+
+
 def run_ours(args):
     from cudacaml_b200 import examples as X
     from cudacaml_b200 import runtime as R
@@ -507,6 +586,13 @@ def run_ours(args):
     if world == 1 and not args.no_secondary:
         f32 = measure_greeks(args, F32, rank, world, local, dist, comm, flush)
     secondary = None
+    if world > 1 and not args.no_secondary:
+        try:
+            mlp = measure_mlp_dp(rank, world, local, dist, comm, flush, pk)
+        except Exception as e:  # noqa: BLE001 - reported, not fatal to the headline
+            mlp = {"error": f"{type(e).__name__}: {e}"}
+        if rank == 0:
+            secondary = {f"mlp_step_8192x4096x8192x1024_tf32_dp{world}": mlp}
     if rank == 0 and world == 1 and not args.no_secondary:
         secondary = secondary_hbm(local, None, flush, pk)
         try:

@@ -7,7 +7,7 @@ copy), issues all devices before waiting on any, and returns one output list
 per device. ``concat`` and ``mean_scalar`` combine on the host as the
 reference does.
 
-Two additions, both opt-in:
+Additions, all opt-in:
 
 * ``counter_key="seed"`` splits a Monte-Carlo graph by *counter range* with the
   same seed (device d draws Philox counters [d*n/D, (d+1)*n/D)), so D devices
@@ -16,6 +16,13 @@ Two additions, both opt-in:
   add a scalar ``__ctr_base`` parameter to every Rng counter.
 * ``allreduce_mean(names, inputs)`` recombines scalar outputs with one NCCL
   all-reduce over NVLink instead of a host loop.
+* ``allreduce_sum(names, inputs)`` sums whole outputs across the devices on
+  the devices (one NCCL all-reduce per output, grouped): a loss and the weight
+  gradients of a batch split by rows, as in the MLP training step.
+* ``split=[names]`` limits slicing to the named inputs (the reference slices
+  every input whose leading dimension is n, which also cuts a weight matrix
+  whose first dimension happens to equal the batch size); ``matmul=`` is the
+  F32 product precision each device program is compiled with.
 """
 from __future__ import annotations
 
@@ -89,7 +96,7 @@ def mean_scalar(values) -> float:
 
 
 class Multi:
-    def __init__(self, devices, n: int, build, counter_key: str | None = None):
+    def __init__(self, devices, n: int, build, counter_key: str | None = None, split=None, matmul=None):
         devices = list(devices)
         d = len(devices)
         if d == 0:
@@ -100,19 +107,27 @@ class Multi:
         self.n = n
         self.per = n // d
         self.counter_key = counter_key
+        self.split = None if split is None else set(split)
         self.released = False
         self.slots = []
         for ordinal in devices:
             g = build(self.per)
             if counter_key is not None:
                 g = offset_counters(g, counter_key)
-            self.slots.append(B.compile_on(ordinal, g))
+            self.slots.append(B.compile_on(ordinal, g, matmul=matmul))
         self._comms = None
+
+    def _splits(self, name, v) -> bool:
+        if self.split is not None:
+            if name in self.split and (not len(v.shape) or v.shape[0] != self.n):
+                raise ValueError(f"Multi.run: input {name} has shape {list(v.shape)}, leading dimension {self.n} expected")
+            return name in self.split
+        return bool(len(v.shape)) and v.shape[0] == self.n
 
     def _inputs_for(self, i: int, inputs):
         out = []
         for name, v in inputs:
-            if len(v.shape) and v.shape[0] == self.n:
+            if self._splits(name, v):
                 rest = v.shape[1:]
                 stride = numel(rest)
                 data = v.data[i * self.per * stride:(i + 1) * self.per * stride]
@@ -137,8 +152,26 @@ class Multi:
         """Run every device resident, all-reduce the named scalar outputs with
         NCCL (sum) across devices, and return {name: sum / d}. Needs distinct
         device ordinals (NCCL puts one rank on each GPU)."""
+        d = len(self.devices)
+        sums = self.allreduce_sum(names, inputs)
+        for name, v in sums.items():
+            if v.numel != 1:
+                raise ValueError(f"Multi.allreduce_mean: output {name} is not a scalar")
+        return {name: float(v.data[0]) / d for name, v in sums.items()}
+
+    def allreduce_sum(self, names, inputs):
+        """Run every device resident, all-reduce the named outputs with NCCL
+        (sum) across the devices, on the devices, and return {name: Value}
+        (the sum, read back from the first device). Needs distinct device
+        ordinals (NCCL puts one rank on each GPU)."""
+        if self.released:
+            raise RuntimeError("Multi.run: this Multi.t has been released")
         if len(set(self.devices)) != len(self.devices):
-            raise ValueError("Multi.allreduce_mean: NCCL needs distinct devices; use mean_scalar for repeats")
+            raise ValueError("Multi.allreduce: NCCL needs distinct devices; use mean_scalar for repeats")
+        out_names = [n for n, _, _ in self.slots[0].outputs]
+        for name in names:
+            if name not in out_names:
+                raise ValueError(f"Multi.allreduce: no output named {name}")
         L = R.lib()
         d = len(self.devices)
         if self._comms is None:
@@ -178,7 +211,7 @@ class Multi:
             host = np.empty(numel(shape), dtype=dt.np)
             with R.with_device(self.slots[0].device):
                 outs_dev[0][j].download(host)
-            result[name] = float(host[0]) / d
+            result[name] = Value(dt, tuple(shape), host)
         for c, (ib, ob) in zip(self.slots, keep):
             with R.with_device(c.device):
                 for b in ib + ob:

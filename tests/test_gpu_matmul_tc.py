@@ -97,3 +97,25 @@ def test_mlp_step_tf32_vs_interp():
         gv = got[name].data.astype(np.float64)
         rel = np.max(np.abs(gv - ev)) / np.max(np.abs(ev))
         assert rel <= 1e-2, f"{name}: normwise error {rel:.3g}"
+
+
+def test_mlp_multi_allreduce_sum_one_device():
+    # Multi with an explicit row split (X and T, not W2 whose first dimension
+    # equals the batch) and an NCCL all-reduce of loss and gradients; on one
+    # device the sum is the single-device result itself
+    from cudacaml_b200 import multi as M
+    bsz, din, hid, dout = 256, 128, 256, 256
+    rng = np.random.default_rng(5)
+    shapes = {"X": (bsz, din), "W1": (din, hid), "W2": (hid, dout), "T": (bsz, dout)}
+    ins = [(nm, Value.of_array(F32, shapes[nm], rng.standard_normal(shapes[nm]).astype(np.float32) * 0.1))
+           for nm in ("X", "W1", "W2", "T")]
+    c = cuda.compile(X.mlp_step(bsz, din, hid, dout), matmul="tf32")
+    want = dict(cuda.run(c, ins))
+    cuda.release(c)
+    t = M.Multi([0], bsz, lambda k: X.mlp_step(k, din, hid, dout), split=["X", "T"], matmul="tf32")
+    got = t.allreduce_sum(["loss", "dloss/dW1", "dloss/dW2"], ins)
+    t.release()
+    for name, v in got.items():
+        assert np.array_equal(v.data, want[name].data), name
+    with pytest.raises(ValueError):
+        M.Multi([0], bsz, lambda k: X.mlp_step(k, din, hid, dout), split=["W1"]).run(ins)
