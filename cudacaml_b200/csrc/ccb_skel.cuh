@@ -663,6 +663,38 @@ __device__ __forceinline__ void scan_flat_staged(const typename F::P& p) {
   }
 }
 
+// ---------------------------------------------------------------- transpose
+// A materialised Dsl.transpose of a buffer: src [rows; cols] -> dst
+// [cols; rows], in 32 x 32 tiles staged through shared memory so that both
+// the reads (rows of src) and the writes (rows of dst) are coalesced.
+// Persistent grid over tiles. F provides T, src(p), dst(p); P provides
+// rows, cols.
+template <class F>
+__device__ __forceinline__ void transpose_tiles(const typename F::P& p) {
+  typedef typename F::T T;
+  __shared__ T tile[32][33];
+  const long long rows = p.rows, cols = p.cols;
+  const long long tr = (rows + 31) / 32, tcn = (cols + 31) / 32;
+  const T* src = F::src(p);
+  T* dst = F::dst(p);
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8 threads
+  for (long long t = blockIdx.x; t < tr * tcn; t += gridDim.x) {
+    const long long r0 = (t / tcn) * 32, c0 = (t % tcn) * 32;
+#pragma unroll
+    for (int k = ty; k < 32; k += 8) {
+      const long long r = r0 + k, c = c0 + tx;
+      if (r < rows && c < cols) tile[k][tx] = src[r * cols + c];
+    }
+    __syncthreads();
+#pragma unroll
+    for (int k = ty; k < 32; k += 8) {
+      const long long c = c0 + k, r = r0 + tx;
+      if (c < cols && r < rows) dst[c * rows + r] = tile[tx][k];
+    }
+    __syncthreads();
+  }
+}
+
 // ---------------------------------------------------------------- rows
 // Row kernels over [rows; n] (last axis). F provides T, identity(),
 // combine(a,b), load(p,i), load4(p,i,T*), vec_ok(p) and, for reductions,

@@ -74,6 +74,7 @@ const Driver& driver() {
     S(cuModuleGetFunction, "cuModuleGetFunction")
     S(cuLaunchKernel, "cuLaunchKernel")
     S(cuFuncSetAttribute, "cuFuncSetAttribute")
+    S(cuFuncGetAttribute, "cuFuncGetAttribute")
     S(cuOccupancyMaxActiveBlocksPerMultiprocessor, "cuOccupancyMaxActiveBlocksPerMultiprocessor")
     S(cuGetErrorString, "cuGetErrorString")
     S(cuPointerGetAttribute, "cuPointerGetAttribute")

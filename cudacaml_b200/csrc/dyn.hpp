@@ -51,6 +51,7 @@ struct Driver {
   CCB_DRV(cuModuleGetFunction)
   CCB_DRV(cuLaunchKernel)
   CCB_DRV(cuFuncSetAttribute)
+  CCB_DRV(cuFuncGetAttribute)
   CCB_DRV(cuOccupancyMaxActiveBlocksPerMultiprocessor)
   CCB_DRV(cuGetErrorString)
   CCB_DRV(cuPointerGetAttribute)

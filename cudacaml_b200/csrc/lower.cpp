@@ -891,7 +891,7 @@ struct Emitter {
 // ===================================================================== lowering
 namespace {
 
-enum GKind { G_MAPRED, G_SCAN_FLAT, G_SCAN_ROWS, G_RED_ROWS, G_SCATTER, G_MATMUL, G_MATMUL_TC };
+enum GKind { G_MAPRED, G_SCAN_FLAT, G_SCAN_ROWS, G_RED_ROWS, G_SCATTER, G_MATMUL, G_MATMUL_TC, G_TRANSPOSE };
 
 struct Red {
   int t = -1;           // output tensor
@@ -1055,6 +1055,27 @@ class Lowerer {
       d = x.dep1;
     }
     return d;
+  }
+
+  // A materialised gather that is exactly the transpose of a materialised
+  // 2-D buffer (the index is affine, (r, c) -> c*R + r over the [R; C]
+  // output): it gets a tiled transpose kernel instead of a strided gather.
+  bool transpose_of(int t, int& src) const {
+    const GTensor& x = g.ts[t];
+    if (x.kind != T_GATHER || x.shape.size() != 2 || (dt_size(x.dt) != 4 && dt_size(x.dt) != 8)) return false;
+    const int64_t R = x.shape[0], C = x.shape[1];
+    if (R < 1 || C < 1) return false;
+    const GTensor& ix = g.ts[x.dep0];
+    if (!(ix.kind == T_MAP && g.ts[ix.dep0].kind == T_IOTA && g.ts[ix.dep0].numel == ix.numel && ix.numel == x.numel))
+      return false;
+    std::unordered_map<int, Aff> memo;
+    const Aff f = aff_expr(ix.body, Aff{true, C, 1, 0}, R, C, memo);
+    if (!f.ok || f.a != 1 || f.b != R || f.k != 0) return false;
+    int d = x.dep1;
+    while (g.ts[d].kind == T_RESHAPE && !mat[d]) d = g.ts[d].dep0;
+    if (!mat[d] || g.ts[d].numel != R * C || g.ts[d].dt != x.dt) return false;
+    src = d;
+    return true;
   }
 
   // Work below this (M*N*K) stays on the exact CUDA-core tile kernel.
@@ -1510,6 +1531,14 @@ class Lowerer {
         case T_GATHER:
         case T_RESHAPE:
         case T_BROADCAST: {
+          int tsrc = -1;
+          if (x.kind == T_GATHER && x.numel >= 4096 && transpose_of(t, tsrc)) {
+            const int gi = new_group(G_TRANSPOSE, x.numel);
+            groups[gi].root = t;
+            groups[gi].val = tsrc;  // the tensor transposed
+            group_of[t] = gi;
+            break;
+          }
           if (cur >= 0 && try_join(cur, t)) break;
           cur = new_group(G_MAPRED, x.numel == 1 ? 1 : x.numel);
           if (!try_join(cur, t)) bad("lower: internal: cannot start a pass");
@@ -2215,6 +2244,35 @@ class Lowerer {
     l.smem = 4 * (128 * 32 * 4 + 256 * 32 * 4) + 1024 + 256;
   }
 
+  void emit_transpose(int gi) {
+    Group& gr = groups[gi];
+    const int t = gr.root, srcb = gr.val;
+    const GTensor& x = g.ts[t];
+    const char* T = dt_ctype(x.dt);
+    const std::string F = "F" + std::to_string(gi);
+    const std::string fn = "ccb_transpose_" + std::to_string(gi) + kname_suffix();
+    node_buf[t] = add_buf("t" + std::to_string(x.uid), dt_size(x.dt), x.numel, BR_NODE, t, false);
+    const int64_t R = x.shape[0], C = x.shape[1];  // output [R; C] = transpose of src [C; R]
+    std::vector<Field> fields;
+    fields.push_back(in_field(srcb));
+    fields.push_back(out_field(t));
+    fields.push_back(i64_field("rows", C));
+    fields.push_back(i64_field("cols", R));
+    src << "// transpose " << gi << ": n" << g.ts[srcb].uid << " [" << C << "x" << R << "] -> n" << x.uid << "\n";
+    src << "struct " << F << " {\n";
+    emit_struct(fields);
+    src << "  typedef " << T << " T;\n";
+    src << "  static __device__ __forceinline__ const T* src(const P& p) { return p.b" << srcb << "; }\n";
+    src << "  static __device__ __forceinline__ T* dst(const P& p) { return p.o" << t << "; }\n";
+    src << "};\n";
+    src << "extern \"C\" __global__ void __launch_bounds__(256) " << fn << "(const " << F << "::P p) { ccb::transpose_tiles<" << F
+        << ">(p); }\n\n";
+    LaunchSpec& l = add_launch(fn, fields);
+    l.mode = GM_PERSISTENT;
+    l.work = ((R + 31) / 32) * ((C + 31) / 32);
+    l.per_block = 1;
+  }
+
   void generate(Lowered& o) {
     out = &o;
     o.name = g.name;
@@ -2247,6 +2305,7 @@ class Lowerer {
         case G_SCATTER: emit_scatter(gi); break;
         case G_MATMUL: emit_matmul(gi); break;
         case G_MATMUL_TC: emit_matmul_tc(gi); break;
+        case G_TRANSPOSE: emit_transpose(gi); break;
       }
     }
     for (auto& op : g.outputs) {

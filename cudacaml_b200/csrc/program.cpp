@@ -4,6 +4,7 @@
 // Executor (lib/backend_cuda/executor.ml:72-244).
 #include <algorithm>
 #include <cstdlib>
+#include <cstdio>
 #include <cstring>
 #include <memory>
 #include <unordered_map>
@@ -38,9 +39,19 @@ struct Program {
   int num_launch_ops = 0;
 };
 
+// The device error word of a lane accumulates over runs (each run copies it
+// to the lane's pinned slot, nothing clears it) until a check reports it;
+// then it is cleared, so a chain of runs checked once reports any error
+// raised anywhere in the chain.
 int lane_check(Program& P, int lane) {
   const unsigned e = *P.lanes[lane].host_err;
   if (e == 0) return CCB_OK;
+  {
+    const Driver& d = driver();
+    Lane& ln = P.lanes[lane];
+    CCB_CU(d.cuMemsetD8Async(ln.bufs[P.L.err_buf], 0, 4, ln.stream));
+    CCB_CU(d.cuStreamSynchronize(ln.stream));
+  }
   std::string m = "device check failed:";
   if (e & 1u) m += " gather index out of bounds;";
   if (e & 2u) m += " scatter_add index out of bounds;";
@@ -171,56 +182,47 @@ int issue(Program& P, int lane, const void* const* h_in, void* const* h_out, con
     }
   }
   CCB_CU(d.cuMemcpyDtoHAsync(ln.host_err, ln.bufs[P.L.err_buf], 4, stream));
-  CCB_CU(d.cuMemsetD8Async(ln.bufs[P.L.err_buf], 0, 4, stream));
   CCB_CU(d.cuEventRecord(ln.done, stream));
   return CCB_OK;
 }
 
 Program* as_prog(ccb_program_t p) { return static_cast<Program*>(p); }
 
-// Kernels whose ptxas report (NVRTC log with -v) shows spill stores.
-std::vector<std::string> spilling_kernels(const std::string& log) {
-  std::vector<std::string> out;
-  size_t pos = 0;
-  const std::string tag = "Function properties for ";
-  while ((pos = log.find(tag, pos)) != std::string::npos) {
-    pos += tag.size();
-    const size_t eol = log.find('\n', pos);
-    const std::string fn = log.substr(pos, eol - pos);
-    const size_t next = log.find('\n', eol + 1);
-    const std::string props = log.substr(eol + 1, next - eol - 1);
-    const size_t sp = props.find(" bytes spill stores");
-    if (sp != std::string::npos) {
-      size_t b = props.rfind(',', sp);
-      b = (b == std::string::npos) ? 0 : b + 1;
-      if (std::atol(props.substr(b, sp - b).c_str()) > 0) out.push_back(fn);
-    }
-    pos = eol;
-  }
-  return out;
-}
-
-// Compile with the occupancy bounds the generator asked for; recompile
-// without the bound for any map-reduce pass that would spill. CCB_MINB=<n>
-// in the environment forces one bound for every pass (a tuning aid).
-int compile_tuned(const Lowered& L, std::string& cubin, std::string& log) {
+// Compile with the occupancy bound the generator asked for (8 resident
+// blocks of 256 threads: 32 registers), load, and recompile without the bound
+// any map-reduce pass whose loaded function uses local memory (spills or
+// register arrays that did not fit). The local size is read from the loaded
+// function, not from a compiler log. CCB_MINB=<n> in the environment forces
+// one bound for every pass (a tuning aid).
+int compile_tuned(const Lowered& L, CUmodule& mod, std::vector<std::string>& relaxed) {
+  const Driver& d = driver();
   const std::string name = L.name.empty() ? "ccb" : L.name;
-  std::vector<std::string> opts = {"--ptxas-options=-v"};
+  std::vector<std::string> opts;
+  std::string cubin, log;
   if (const char* f = std::getenv("CCB_MINB")) {
     for (const auto& l : L.launches)
       if (l.fn.rfind("ccb_mapreduce_", 0) == 0) opts.push_back("-DCCB_MINB_" + l.fn.substr(14) + "=" + f);
-    return nvrtc_compile_opts(L.source, name, opts, cubin, log);
+    CCB_TRY(nvrtc_compile_opts(L.source, name, opts, cubin, log));
+    CCB_CU(d.cuModuleLoadData(&mod, cubin.data()));
+    return CCB_OK;
   }
   CCB_TRY(nvrtc_compile_opts(L.source, name, opts, cubin, log));
-  std::vector<std::string> sp = spilling_kernels(log);
-  bool again = false;
-  for (const auto& fn : sp)
-    if (fn.rfind("ccb_mapreduce_", 0) == 0) {
-      opts.push_back("-DCCB_MINB_" + fn.substr(14) + "=1");
-      again = true;
-    }
-  if (!again) return CCB_OK;
-  return nvrtc_compile_opts(L.source, name, opts, cubin, log);
+  CCB_CU(d.cuModuleLoadData(&mod, cubin.data()));
+  for (const auto& l : L.launches) {
+    if (l.fn.rfind("ccb_mapreduce_", 0) != 0) continue;
+    CUfunction f;
+    CCB_CU(d.cuModuleGetFunction(&f, mod, l.fn.c_str()));
+    int local = 0;
+    CCB_CU(d.cuFuncGetAttribute(&local, CU_FUNC_ATTRIBUTE_LOCAL_SIZE_BYTES, f));
+    if (local > 0) relaxed.push_back(l.fn);
+  }
+  if (relaxed.empty()) return CCB_OK;
+  for (const auto& fn : relaxed) opts.push_back("-DCCB_MINB_" + fn.substr(14) + "=1");
+  d.cuModuleUnload(mod);
+  mod = nullptr;
+  CCB_TRY(nvrtc_compile_opts(L.source, name, opts, cubin, log));
+  CCB_CU(d.cuModuleLoadData(&mod, cubin.data()));
+  return CCB_OK;
 }
 
 int need_device(Program* P) {
@@ -267,11 +269,12 @@ int ccb_program_create(const char* graph, int device, int lanes, ccb_program_t* 
     destroy(P);
     return code;
   };
-  std::string cubin, log;
-  rc = compile_tuned(P->L, cubin, log);
+  std::vector<std::string> relaxed;
+  rc = compile_tuned(P->L, P->mod, relaxed);
   if (rc != CCB_OK) return cleanup(rc);
-  CUresult r = d.cuModuleLoadData(&P->mod, cubin.data());
-  if (r != CUDA_SUCCESS) return cleanup(cu_fail(r, "cuModuleLoadData"));
+  if (std::getenv("CCB_DEBUG_TUNE"))
+    for (const auto& fn : relaxed) fprintf(stderr, "ccb tune %s: bound relaxed (local memory at 8 blocks/SM)\n", fn.c_str());
+  CUresult r;
   int sms = 0;
   CUdevice dev;
   d.cuDeviceGet(&dev, device);
@@ -295,6 +298,11 @@ int ccb_program_create(const char* graph, int device, int lanes, ccb_program_t* 
       gy = 1;
     }
     if (gx > 0x7fffffff || gy > 65535) return cleanup(fail(CCB_ERR_UNSUPPORTED, "launch grid too large for " + l.fn));
+    if (std::getenv("CCB_DEBUG_TUNE")) {
+      int regs = 0;
+      d.cuFuncGetAttribute(&regs, CU_FUNC_ATTRIBUTE_NUM_REGS, f);
+      fprintf(stderr, "ccb grid %s: %lld x %lld, %d registers\n", l.fn.c_str(), (long long)gx, (long long)gy, regs);
+    }
     P->gx.push_back((unsigned)gx);
     P->gy.push_back((unsigned)gy);
   }

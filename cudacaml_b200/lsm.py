@@ -12,8 +12,10 @@ Three graphs are compiled once and then only run (lsm.ml:126-236):
 The basis is either the reference's strike-scaled ``[1, S/K, (S/K)^2]``
 (``basis="scaled3"``, lsm.ml:170-192) or ``[1, S, S^2, S^3]``
 (``basis="poly4"``, the BASELINE configuration). The small dense solve is a
-host Gaussian elimination with partial pivoting, as the reference's solve3
-(lsm.ml:69-104), generalised to n x n.
+Gaussian elimination with partial pivoting, as the reference's solve3
+(lsm.ml:69-104), generalised to n x n: on the host in the generic driver
+(``Make``), and as a one-launch graph (``solve_graph``) in the resident CUDA
+driver.
 """
 from __future__ import annotations
 
@@ -100,18 +102,23 @@ def paths_graph(n_paths: int, n_steps: int, m: Market = MARKET) -> Graph:
     return Graph("lsm_paths", [("S", s)])
 
 
-def _basis(n_paths, n_steps, strike, basis):
+def _basis(n_paths, n_steps, strike, basis, layout="paths"):
     """Column t of S, the in-the-money mask and the masked design matrix
-    (lsm.ml:170-192)."""
+    (lsm.ml:170-192). ``layout="paths"`` reads S as the reference stores it,
+    [n_paths; n_steps]; ``layout="dates"`` reads its transpose [n_steps;
+    n_paths], where date t is one contiguous row."""
     nb = _nb(basis)
-    grid = (n_paths, n_steps)
     gb = (n_paths, nb)
     kf = lambda v: D.const(F64, v)  # noqa: E731
     ki = lambda v: D.const(I32, v)  # noqa: E731
-    s = D.param("S", F64, grid)
     cf = D.param("cf", F64, (n_paths,))
     tb = D.broadcast((n_paths,), D.scalar("t", I32))
-    idx = D.map2(lambda p, tv: D.add(D.mul(p, ki(n_steps)), tv), D.iota((n_paths,)), tb)
+    if layout == "paths":
+        s = D.param("S", F64, (n_paths, n_steps))
+        idx = D.map2(lambda p, tv: D.add(D.mul(p, ki(n_steps)), tv), D.iota((n_paths,)), tb)
+    else:
+        s = D.param("S", F64, (n_steps, n_paths))
+        idx = D.map2(lambda p, tv: D.add(D.mul(tv, ki(n_paths)), p), D.iota((n_paths,)), tb)
     st = D.gather(idx, s)
     itm = D.map(lambda x: D.select(D.lt(x, kf(strike)), kf(1.0), kf(0.0)), st)
     row = D.map(lambda k: D.div(k, ki(nb)), D.iota(gb))
@@ -131,20 +138,20 @@ def _basis(n_paths, n_steps, strike, basis):
     return cf, st, itm, D.map2(D.mul, ph, itm3)
 
 
-def regress_graph(n_paths, n_steps, strike, disc, basis="scaled3") -> Graph:
+def regress_graph(n_paths, n_steps, strike, disc, basis="scaled3", layout="paths") -> Graph:
     """lsm.ml:201-212."""
-    cf, st, itm, xm = _basis(n_paths, n_steps, strike, basis)
+    cf, st, itm, xm = _basis(n_paths, n_steps, strike, basis, layout)
     kf = lambda v: D.const(F64, v)  # noqa: E731
     y = D.map2(lambda c, mk: D.mul(D.mul(kf(disc), c), mk), cf, itm)
     xt = D.transpose(xm)
     return Graph("lsm_regress", [("xtx", D.matmul(xt, xm)), ("xty", D.matmul(xt, D.reshape((n_paths, 1), y)))])
 
 
-def update_graph(n_paths, n_steps, strike, disc, basis="scaled3") -> Graph:
+def update_graph(n_paths, n_steps, strike, disc, basis="scaled3", layout="paths") -> Graph:
     """lsm.ml:219-234: exercise where intrinsic beats the fitted continuation;
     otherwise keep the realised cash flow, discounted."""
     nb = _nb(basis)
-    cf, st, itm, xm = _basis(n_paths, n_steps, strike, basis)
+    cf, st, itm, xm = _basis(n_paths, n_steps, strike, basis, layout)
     kf = lambda v: D.const(F64, v)  # noqa: E731
     beta = D.param("beta", F64, (nb, 1))
     cont = D.reshape((n_paths,), D.matmul(xm, beta))
@@ -157,6 +164,95 @@ def update_graph(n_paths, n_steps, strike, disc, basis="scaled3") -> Graph:
     keep = D.map2(lambda s, c: D.select(exercises(s, c), kf(0.0), kf(1.0)), st, cont)
     held = D.map2(lambda k, c: D.mul(k, D.mul(kf(disc), c)), keep, cf)
     return Graph("lsm_update", [("cf", D.map2(D.add, exv, held))])
+
+
+def solve_graph(nb: int) -> Graph:
+    """The normal-equation solve of ``_beta`` as a graph, so that the
+    resident driver keeps beta on the device: the ridge and the "fewer than nb
+    in-the-money paths" rule of lsm.ml:283-294, and the Gaussian elimination
+    with partial pivoting of ``solve`` (solve3, lsm.ml:69-104) in the same
+    operation order -- the pivot is the first row of largest magnitude, rows
+    are swapped by selects, a pivot not above 1e-300 or a non-finite result
+    gives zeros. Every value is a one-element F64 tensor; the graph lowers to
+    one single-element pass. Outputs b0 .. b{nb-1}, each [1]."""
+    xtx = D.param("xtx", F64, (nb * nb,))
+    xty = D.param("xty", F64, (nb,))
+    one = (1,)
+    kf = lambda v: D.const(F64, v)  # noqa: E731
+
+    def el(src, i):
+        return D.gather(D.full(I32, one, i), src)
+
+    def f2(op, x, y):
+        return D.map2(op, x, y)
+
+    # Flags are F64 0/1 tensors (a graph may not hold Bool tensors: every
+    # node of the reference interpreter is a storable value).
+    def pick(c, x, y):  # c ? x : y: a select each way, then a sum with +0
+        return f2(D.add, D.map2(lambda cc, v: D.select(D.gt(cc, kf(0.5)), v, kf(0.0)), c, x),
+                  D.map2(lambda cc, v: D.select(D.gt(cc, kf(0.5)), kf(0.0), v), c, y))
+
+    def absf(x):
+        return D.map(D.abs, x)
+
+    def flag2(cmp, x, y):
+        return D.map2(lambda u, v: D.select(cmp(u, v), kf(1.0), kf(0.0)), x, y)
+
+    def flag1(pred, x):
+        return D.map(lambda u: D.select(pred(u), kf(1.0), kf(0.0)), x)
+
+    def band(x, y):
+        return f2(D.mul, x, y)
+
+    def bor(x, y):
+        return f2(D.max, x, y)
+
+    def bnot(x):
+        return D.map(lambda u: D.sub(kf(1.0), u), x)
+
+    a = [[el(xtx, i * nb + j) for j in range(nb)] for i in range(nb)]
+    bv = [el(xty, i) for i in range(nb)]
+    few = flag1(lambda e: D.lt(e, kf(float(nb))), a[0][0])
+    a = [[D.map(lambda e: D.add(e, kf(1e-10)), a[i][j]) if i == j else a[i][j] for j in range(nb)] for i in range(nb)]
+    bad = few
+    for k in range(nb):
+        best = absf(a[k][k])
+        ind = {k: D.full(F64, one, 1.0)}
+        for i in range(k + 1, nb):
+            take = flag2(D.gt, absf(a[i][k]), best)
+            best = pick(take, absf(a[i][k]), best)
+            keep = bnot(take)
+            for m in list(ind):
+                ind[m] = band(ind[m], keep)
+            ind[i] = take
+        bad = bor(bad, flag1(lambda e: D.not_(D.gt(e, kf(1e-300))), best))
+        rowk = []
+        for j in range(nb):
+            v = a[k][j]
+            for i in range(k + 1, nb):
+                v = pick(ind[i], a[i][j], v)
+            rowk.append(v)
+        bk = bv[k]
+        for i in range(k + 1, nb):
+            bk = pick(ind[i], bv[i], bk)
+        for i in range(k + 1, nb):
+            a[i] = [pick(ind[i], a[k][j], a[i][j]) for j in range(nb)]
+            bv[i] = pick(ind[i], bv[k], bv[i])
+        a[k], bv[k] = rowk, bk
+        for i in range(k + 1, nb):
+            fct = f2(D.div, a[i][k], a[k][k])
+            for j in range(k, nb):
+                a[i][j] = f2(D.sub, a[i][j], f2(D.mul, fct, a[k][j]))
+            bv[i] = f2(D.sub, bv[i], f2(D.mul, fct, bv[k]))
+    x = [None] * nb
+    for i in range(nb - 1, -1, -1):
+        acc = bv[i]
+        for j in range(i + 1, nb):
+            acc = f2(D.sub, acc, f2(D.mul, a[i][j], x[j]))
+        x[i] = f2(D.div, acc, a[i][i])
+    for i in range(nb):
+        bad = bor(bad, flag1(lambda e: D.not_(D.eq(D.sub(e, e), kf(0.0))), x[i]))
+    return Graph("lsm_solve", [(f"b{i}", pick(bad, D.full(F64, one, 0.0), x[i])) for i in range(nb)])
 
 
 def _beta(xtx, xty, nb):
@@ -204,9 +300,12 @@ class Make:
 
 
 class CudaResident:
-    """The resident CUDA driver (lsm.ml:321-420): S and the running cash flow
-    never leave the device; per date only the normal equations (nb^2 + nb
-    doubles) come back and beta (nb doubles) goes out."""
+    """The resident CUDA driver (lsm.ml:321-420): S, the running cash flow,
+    the normal equations and beta never leave the device. The reference's
+    driver brings the normal equations to the host each date for its solve;
+    here the same solve runs as a graph (solve_graph) on the device, so the
+    host only launches. S is transposed once after generation so that each
+    date reads one contiguous row; the device buffers are allocated once."""
 
     def __init__(self, n_paths: int, n_steps: int, m: Market = MARKET, basis: str = "scaled3", device: int = 0):
         from . import backend_cuda as cuda
@@ -219,61 +318,81 @@ class CudaResident:
         self.strike = m.strike
         self.device = device
         self.paths = cuda.compile_on(device, paths_graph(n_paths, n_steps, m))
-        self.regress = cuda.compile_on(device, regress_graph(n_paths, n_steps, self.strike, self.disc, basis))
-        self.update = cuda.compile_on(device, update_graph(n_paths, n_steps, self.strike, self.disc, basis))
+        self.dates = cuda.compile_on(device, _dates_graph(n_paths, n_steps))
+        self.regress = cuda.compile_on(device, regress_graph(n_paths, n_steps, self.strike, self.disc, basis, "dates"))
+        self.update = cuda.compile_on(device, update_graph(n_paths, n_steps, self.strike, self.disc, basis, "dates"))
         self.final = cuda.compile_on(device, _final_graph(n_paths, n_steps, self.strike))
+        self.solve = cuda.compile_on(device, solve_graph(self.nb))
+        cfp = D.param("cf", F64, (n_paths,))
+        self.total = cuda.compile_on(device, Graph("lsm_total", [("s", D.reduce(D.add, D.const(F64, 0.0), cfp))]))
+        n, ns, nb = n_paths, n_steps, self.nb
+        with R.with_device(device):
+            self.bufs = {"S": R.Buffer(n * ns * 8), "ST": R.Buffer(n * ns * 8), "cf_a": R.Buffer(n * 8),
+                         "cf_b": R.Buffer(n * 8), "seed": R.Buffer(4), "t": R.Buffer(4 * ns), "beta": R.Buffer(nb * 8),
+                         "xtx": R.Buffer(nb * nb * 8), "xty": R.Buffer(nb * 8), "sum": R.Buffer(8)}
+            self.bufs["t"].upload(np.arange(ns, dtype=np.int32))  # date t lives at t + 4 t bytes
 
     def price(self, seed: int, trace=None) -> float:
+        """Generation, the transpose and all dates run back to back on one
+        stream: per date regress, the graph solve of the normal equations
+        (beta stays on the device) and update. The host only launches; with
+        `trace` the normal equations are also copied out each date (which
+        synchronises)."""
         cuda, R = self.cuda, self.R
         n, ns, nb = self.n_paths, self.n_steps, self.nb
-        with R.with_device(self.device):
-            s_buf = R.Buffer(n * ns * 8)
-            cf_a = R.Buffer(n * 8)
-            cf_b = R.Buffer(n * 8)
-            seed_b = R.Buffer(4)
-            seed_b.upload(np.array([seed], np.int32))
-            t_b = R.Buffer(4)
-            beta_b = R.Buffer(nb * 8)
-            xtx_b = R.Buffer(nb * nb * 8)
-            xty_b = R.Buffer(nb * 8)
-            stream = self.regress.lane_stream(0)
-            try:
-                def bind(c, **ptrs):  # device pointers in the program's param order
-                    return [ptrs[name] for name, _, _ in c.params]
+        b = self.bufs
+        stream = self.regress.lane_stream(0)
+        progs = (self.paths, self.dates, self.final, self.regress, self.solve, self.update)
 
-                cuda.run_device_ptrs(self.paths, bind(self.paths, seed=seed_b.ptr), [s_buf.ptr], stream)
-                # initial cash flow: intrinsic value at maturity (last column), on the device
-                cuda.run_device_ptrs(self.final, bind(self.final, S=s_buf.ptr), [cf_a.ptr], stream)
-                cuda.check_device(self.paths, stream)
-                xtx = np.empty(nb * nb)
-                xty = np.empty(nb)
-                cur, nxt = cf_a, cf_b
-                for step in range(ns - 2, -1, -1):
-                    R.check(R.lib().ccb_memcpy_h2d(t_b.ptr, np.array([step], np.int32).ctypes.data, 4, stream))
-                    outs = {"xtx": xtx_b.ptr, "xty": xty_b.ptr}
-                    cuda.run_device_ptrs(self.regress, bind(self.regress, S=s_buf.ptr, cf=cur.ptr, t=t_b.ptr),
-                                         [outs[name] for name, _, _ in self.regress.outputs], stream)
-                    R.check(R.lib().ccb_memcpy_d2h(xtx.ctypes.data, xtx_b.ptr, xtx.nbytes, stream))
-                    R.check(R.lib().ccb_memcpy_d2h(xty.ctypes.data, xty_b.ptr, xty.nbytes, stream))
+        def bind(c, **ptrs):  # device pointers in the program's param order
+            return [ptrs[name] for name, _, _ in c.params]
+
+        with R.with_device(self.device):
+            seed_h = np.array([seed], np.int32)
+            R.check(R.lib().ccb_memcpy_h2d(b["seed"].ptr, seed_h.ctypes.data, 4, stream))
+            cuda.run_device_ptrs(self.paths, bind(self.paths, seed=b["seed"].ptr), [b["S"].ptr], stream)
+            cuda.run_device_ptrs(self.dates, bind(self.dates, S=b["S"].ptr), [b["ST"].ptr], stream)
+            # initial cash flow: intrinsic value at maturity (last column), on the device
+            cuda.run_device_ptrs(self.final, bind(self.final, S=b["S"].ptr), [b["cf_a"].ptr], stream)
+            xtx = np.empty(nb * nb)
+            xty = np.empty(nb)
+            beta_outs = [b["beta"].ptr + 8 * j for j in range(nb)]
+            cur, nxt = b["cf_a"], b["cf_b"]
+            for step in range(ns - 2, -1, -1):
+                t_ptr = b["t"].ptr + 4 * step
+                outs = {"xtx": b["xtx"].ptr, "xty": b["xty"].ptr}
+                cuda.run_device_ptrs(self.regress, bind(self.regress, S=b["ST"].ptr, cf=cur.ptr, t=t_ptr),
+                                     [outs[name] for name, _, _ in self.regress.outputs], stream)
+                if trace is not None:
+                    R.check(R.lib().ccb_memcpy_d2h(xtx.ctypes.data, b["xtx"].ptr, xtx.nbytes, stream))
+                    R.check(R.lib().ccb_memcpy_d2h(xty.ctypes.data, b["xty"].ptr, xty.nbytes, stream))
                     cuda.check_device(self.regress, stream)
-                    if trace is not None:
-                        trace.append((step, xtx.copy(), xty.copy()))
-                    beta = np.array(_beta(xtx, xty, nb), np.float64)
-                    R.check(R.lib().ccb_memcpy_h2d(beta_b.ptr, beta.ctypes.data, beta.nbytes, stream))
-                    cuda.run_device_ptrs(self.update, bind(self.update, S=s_buf.ptr, cf=cur.ptr, t=t_b.ptr, beta=beta_b.ptr),
-                                         [nxt.ptr], stream)
-                    cur, nxt = nxt, cur
-                cfh = np.empty(n)
-                R.check(R.lib().ccb_memcpy_d2h(cfh.ctypes.data, cur.ptr, cfh.nbytes, stream))
-                cuda.check_device(self.update, stream)
-            finally:
-                for b in (s_buf, cf_a, cf_b, seed_b, t_b, beta_b, xtx_b, xty_b):
-                    b.free()
-        return self.disc * float(np.sum(cfh)) / n
+                    trace.append((step, xtx.copy(), xty.copy()))
+                cuda.run_device_ptrs(self.solve, bind(self.solve, xtx=b["xtx"].ptr, xty=b["xty"].ptr),
+                                     [beta_outs[int(name[1:])] for name, _, _ in self.solve.outputs], stream)
+                cuda.run_device_ptrs(self.update, bind(self.update, S=b["ST"].ptr, cf=cur.ptr, t=t_ptr, beta=b["beta"].ptr),
+                                     [nxt.ptr], stream)
+                cur, nxt = nxt, cur
+            # the mean of the discounted cash flows (lsm.ml:303-305): summed on the device
+            cuda.run_device_ptrs(self.total, [cur.ptr], [b["sum"].ptr], stream)
+            tot = np.empty(1)
+            R.check(R.lib().ccb_memcpy_d2h(tot.ctypes.data, b["sum"].ptr, 8, stream))
+            for c in progs + (self.total,):  # each program's error word, accumulated over all its runs
+                cuda.check_device(c, stream)
+        return self.disc * float(tot[0]) / n
 
     def release(self):
-        for c in (self.paths, self.regress, self.update, self.final):
+        with self.R.with_device(self.device):
+            for buf in self.bufs.values():
+                buf.free()
+        self.bufs = {}
+        for c in (self.paths, self.dates, self.regress, self.update, self.final, self.solve, self.total):
             self.cuda.release(c)
+
+
+def _dates_graph(n_paths, n_steps) -> Graph:
+    """S [n_paths; n_steps] -> its transpose [n_steps; n_paths] (Dsl.transpose)."""
+    return Graph("lsm_dates", [("ST", D.transpose(D.param("S", F64, (n_paths, n_steps))))])
 
 
 def _final_graph(n_paths, n_steps, strike) -> Graph:

@@ -146,7 +146,10 @@ int ccb_program_run(ccb_program_t prog, const void* const* inputs, void* const* 
  * lib/backend_cuda/executor.ml:181-244): kernels read `inputs[i]` and write
  * `outputs[j]` (caller-owned device pointers of the exact byte size) directly.
  * Issued on `stream` (NULL: the lane's own stream); it does not synchronise.
- * ccb_program_check then synchronises that stream and reads the error word. */
+ * ccb_program_check then synchronises that stream and reads the error word.
+ * A lane's error word accumulates over runs until a wait or check reports it
+ * (and clears it), so a chain of device runs checked once reports an error
+ * raised anywhere in the chain. */
 int ccb_program_run_device(ccb_program_t prog, int lane, const void* const* inputs,
                            void* const* outputs, ccb_stream_t stream);
 int ccb_program_check(ccb_program_t prog, int lane, ccb_stream_t stream);

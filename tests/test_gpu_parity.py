@@ -137,6 +137,20 @@ def test_matmul_transposed_operands_and_skinny():
     diff(g, [("a", va), ("b", vb)], tol=1e-9)
 
 
+@pytest.mark.parametrize("dt,m,n", [(F32, 300, 500), (F64, 1000, 37), (I32, 64, 4096 + 3)])
+def test_materialised_transpose_tiles(dt, m, n):
+    # a materialised Dsl.transpose of a buffer takes the tiled transpose
+    # kernel: partial tiles on both axes, bit-exact for every dtype
+    a = D.param("a", dt, (m, n))
+    g = Graph("tr", [("t", D.transpose(a)), ("s", D.reduce(D.add, D.const(dt, 0), D.transpose(a)))])
+    c = cuda.compile(g)
+    assert "launch ccb_transpose_" in c.plan()
+    x = (np.arange(m * n) % 1000 - 500).astype(dt.np).reshape(m, n)
+    got = dict(cuda.run(c, [("a", Value.of_array(dt, (m, n), x))]))
+    assert np.array_equal(got["t"].data.reshape(n, m), x.T)
+    diff(g, [("a", Value.of_array(dt, (m, n), x))], tol=1e-3 if dt is F32 else 0.0)
+
+
 def test_s12_scatter():
     n = 100_000
     idx = Value.of_array(I32, (n,), (np.arange(n) % 7).astype(np.int32))

@@ -228,3 +228,27 @@ def test_programs_registry_runs():
     for p in X.PROGRAMS:
         o = run(p.graph(), p.inputs())
         assert o, p.name
+
+
+def test_lsm_solve_graph_matches_host_solve():
+    # the resident driver's graph solve against the host solve it restates,
+    # on the oracle: regular, pivoting, too few paths, singular
+    from cudacaml_b200 import lsm as L
+    from cudacaml_b200.ir import F64, Value
+    g = L.solve_graph(4)
+    rng = np.random.default_rng(1)
+    for case in range(5):
+        x = rng.standard_normal((100, 4)) * (1, 30, 900, 27000)
+        y = rng.standard_normal(100)
+        xtx, xty = x.T @ x, x.T @ y
+        if case == 1:
+            xtx[[0, 1]] = xtx[[1, 0]]
+        if case == 2:
+            xtx[0, 0] = 2.0
+        if case == 3:
+            xtx = np.zeros((4, 4))
+            xtx[0, 0] = 50.0
+        want = L._beta(list(xtx.ravel()), list(xty), 4)
+        out = dict(I.run(I.compile(g), [("xtx", Value.of_array(F64, (16,), xtx.ravel())),
+                                                  ("xty", Value.of_array(F64, (4,), xty))]))
+        assert [float(out[f"b{i}"].data[0]) for i in range(4)] == want
