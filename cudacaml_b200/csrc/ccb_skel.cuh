@@ -1184,4 +1184,213 @@ __device__ __forceinline__ void matmul_tc(const typename F::P& p) {
   if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
 }
 
+// ------------------------------------------------------------------------
+// F32 matmul on the tcgen05 tensor cores, 2-SM pairs (cta_group::2).
+//
+// A cluster of two CTAs on two SMs owns 256 x 256 output tiles in turn.
+// Each CTA stages its own 128 rows of A and 128 columns of B per 32-wide
+// k-step (32 KiB, a 6-deep ring); one thread of the even CTA (the leader)
+// issues tcgen05.mma.cta_group::2 (M=256, N=256, K=8), which reads both
+// CTAs' shared memory and accumulates each CTA's 128 rows x 256 columns in
+// its own TMEM (two 256-column buffers, as in matmul_tc). Per SM this moves
+// two thirds of the operand bytes of a 128 x 256 single-SM tile for the same
+// flops. Both CTAs' TMA copies (plain loads, no cluster multicast) complete
+// on the leader's stage barrier; the leader's commits release the stage in
+// both CTAs (a commit to each CTA's barrier, addressed through mapa); both
+// CTAs' epilogue warps release an accumulator to the leader.
+// Same operand views, bounds handling and numerics as matmul_tc.
+namespace tc2 {
+constexpr int BM = 256, BN = 256, HALF = 128, BK = 32, STAGES = 6, THREADS = 192;
+constexpr unsigned A_BYTES = HALF * BK * 4, B_BYTES = HALF * BK * 4, STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr unsigned SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+constexpr unsigned TMEM_COLS = 2 * BN;
+
+__device__ __forceinline__ unsigned cta_rank() {
+  unsigned r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// The shared::cluster address of `local` in CTA `rank` of this cluster.
+__device__ __forceinline__ unsigned peer_addr(const void* local, unsigned rank) {
+  unsigned r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(local)), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void tma_load_2d(unsigned dst, const TmaDesc* map, int x, int y, unsigned bar_cluster) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          dst),
+      "l"((unsigned long long)map), "r"(x), "r"(y), "r"(bar_cluster)
+      : "memory");
+}
+__device__ __forceinline__ void mma(unsigned d, u64 a, u64 b, unsigned idesc, unsigned accumulate) {
+  const unsigned z = 0;
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, {%5, %6, %7, %8, %9, %10, %11, %12}, p;\n}\n" ::"r"(d),
+      "l"(a), "l"(b), "r"(idesc), "r"(accumulate), "r"(z), "r"(z), "r"(z), "r"(z), "r"(z), "r"(z), "r"(z), "r"(z));
+}
+// Arrive on barrier `bar` of both CTAs once the MMAs issued so far complete.
+__device__ __forceinline__ void commit_both(u64* bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(peer_addr(bar, 0)) : "memory");
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(peer_addr(bar, 1)) : "memory");
+}
+__device__ __forceinline__ void arrive_leader(u64* bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(peer_addr(bar, 0)) : "memory");
+}
+}  // namespace tc2
+
+template <class F>
+__device__ __forceinline__ void matmul_tc2(const typename F::P& p) {
+  using namespace tc2;
+  extern __shared__ __align__(1024) unsigned char ccb_tc_smem[];
+  const unsigned raw = smem_u32(ccb_tc_smem);
+  const unsigned pad = (1024u - (raw & 1023u)) & 1023u;
+  unsigned char* base = ccb_tc_smem + pad;
+  const unsigned sbase = raw + pad;
+  u64* full = (u64*)(base + STAGES * STAGE_BYTES);
+  u64* empty = full + STAGES;
+  u64* accf = empty + STAGES;
+  u64* acce = accf + 2;
+  unsigned* tslot = (unsigned*)(acce + 2);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const unsigned rank = cta_rank();
+  const bool leader = rank == 0;
+  const long long M = p.M, N = p.N, K = p.K;
+  const int tiles_m = (int)((M + BM - 1) / BM), tiles_n = (int)((N + BN - 1) / BN);
+  const long long ntiles = (long long)tiles_m * tiles_n;
+  const int KT = (int)((K + BK - 1) / BK);
+  const long long pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);   // the leader's expect_tx arrival (+ both CTAs' bytes)
+      mbar_init(&empty[s], 1);  // the leader's commit
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&accf[b], 1);  // the leader's commit
+      mbar_init(&acce[b], 8);  // four epilogue warps of each CTA (used in the leader)
+    }
+    mbar_fence_init();
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tslot)), "r"(TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  tc::fence_before();
+  cluster_sync();  // both CTAs' barriers initialised and TMEM allocated
+  tc::fence_after();
+  const unsigned tmem = *tslot;
+
+  if (warp == 0) {
+    if (lane == 0) {  // TMA producer (both CTAs)
+      unsigned stage = 0, phase = 0;
+      for (long long t = pair; t < ntiles; t += npairs) {
+        int tm, tn;
+        tc::tile_of(t, tiles_m, tiles_n, tm, tn);
+        const int m0 = tm * BM + (int)rank * HALF, n0 = tn * BN + (int)rank * HALF;
+        for (int ks = 0; ks < KT; ++ks) {
+          tc::wait(&empty[stage], phase ^ 1u, p.err);
+          const unsigned sa = sbase + stage * STAGE_BYTES, sb = sa + A_BYTES;
+          const unsigned fb = peer_addr(&full[stage], 0);
+          if (leader) {
+            asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(&full[stage])),
+                         "r"(2u * STAGE_BYTES)
+                         : "memory");
+          }
+          const int k0 = ks * BK;
+          if (F::A_MN) {
+#pragma unroll
+            for (int g = 0; g < HALF / 32; ++g) tma_load_2d(sa + g * 4096u, &p.ta, m0 + 32 * g, k0, fb);
+          } else {
+            tma_load_2d(sa, &p.ta, k0, m0, fb);
+          }
+          if (F::B_MN) {
+#pragma unroll
+            for (int g = 0; g < HALF / 32; ++g) tma_load_2d(sb + g * 4096u, &p.tb, n0 + 32 * g, k0, fb);
+          } else {
+            tma_load_2d(sb, &p.tb, k0, n0, fb);
+          }
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {  // MMA issuer: one thread of the pair
+      const unsigned idesc = (1u << 4) | (2u << 7) | (2u << 10) | ((F::A_MN ? 1u : 0u) << 15) | ((F::B_MN ? 1u : 0u) << 16) |
+                             ((unsigned)(BN >> 3) << 17) | ((unsigned)(BM >> 4) << 24);
+      unsigned stage = 0, phase = 0;
+      int it = 0;
+      for (long long t = pair; t < ntiles; t += npairs, ++it) {
+        const unsigned ab = it & 1, aph = (it >> 1) & 1;
+        tc::wait(&acce[ab], aph ^ 1u, p.err);
+        tc::fence_after();
+        const unsigned d = tmem + ab * BN;
+        for (int ks = 0; ks < KT; ++ks) {
+          tc::wait(&full[stage], phase, p.err);
+          tc::fence_after();
+          const unsigned sa = sbase + stage * STAGE_BYTES, sb = sa + A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < BK / 8; ++kk) {
+            const u64 a = F::A_MN ? tc::desc_mn(sa, kk) : tc::desc_k(sa, kk);
+            const u64 b = F::B_MN ? tc::desc_mn(sb, kk) : tc::desc_k(sb, kk);
+            mma(d, a, b, idesc, (ks | kk) != 0 ? 1u : 0u);
+          }
+          commit_both(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        commit_both(&accf[ab]);
+      }
+    }
+  } else {  // epilogue: warps 2..5 of each CTA, TMEM lane quadrant warp % 4
+    const int q = warp & 3;
+    const bool vec = ((((unsigned long long)p.C) & 15ull) == 0) && (N % 4 == 0);
+    int it = 0;
+    for (long long t = pair; t < ntiles; t += npairs, ++it) {
+      int tm, tn;
+      tc::tile_of(t, tiles_m, tiles_n, tm, tn);
+      const long long row = (long long)tm * BM + (long long)rank * HALF + q * 32 + lane;
+      const long long n0 = (long long)tn * BN;
+      const unsigned ab = it & 1, aph = (it >> 1) & 1;
+      tc::wait(&accf[ab], aph, p.err);
+      __syncwarp();
+      tc::fence_after();
+      for (int c = 0; c < BN && n0 + c < N; c += 32) {
+        float v[32];
+        __syncwarp();
+        tc::ld32(tmem + ((unsigned)(q * 32) << 16) + ab * BN + c, v);
+        if (row < M) {
+          float* dst = p.C + row * N + n0 + c;
+          if (vec && n0 + c + 32 <= N) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 4) *(float4*)(dst + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+          } else {
+            for (int i = 0; i < 32 && n0 + c + i < N; ++i) dst[i] = v[i];
+          }
+        }
+      }
+      tc::fence_before();
+      __syncwarp();
+      if (lane == 0) arrive_leader(&acce[ab]);
+    }
+  }
+  tc::fence_before();
+  __syncthreads();
+  cluster_sync();  // the pair is done with both TMEM allocations
+  tc::fence_after();
+  __syncwarp();
+  if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+}
+
 }  // namespace ccb

@@ -2194,8 +2194,10 @@ class Lowerer {
     const GTensor& x = g.ts[t];
     const TcInfo& ti = tc[t];
     const std::string F = "F" + std::to_string(gi);
-    const std::string fn = "ccb_matmultc_" + std::to_string(gi) + kname_suffix();
     const int64_t M = x.shape[0], N = x.shape[1], K = g.ts[x.dep0].shape[1];
+    // 2-SM pairs (256 x 256 tiles) once both output dimensions fill a pair tile
+    const bool pair = M >= 256 && N >= 256;
+    const std::string fn = (pair ? "ccb_matmultc2_" : "ccb_matmultc_") + std::to_string(gi) + kname_suffix();
     node_buf[t] = add_buf("t" + std::to_string(x.uid), 4, x.numel, BR_NODE, t, false);
     if (node_buf[ti.va] < 0 || node_buf[ti.vb] < 0) bad("lower: internal: tensor-core operand without a buffer");
     std::vector<Field> fields;
@@ -2217,8 +2219,8 @@ class Lowerer {
     if (ti.b_mn) {  // B stored [K][N]: 32 x 32 boxes, eight per 256-column tile
       fb.slot.tdim[0] = N, fb.slot.tdim[1] = K, fb.slot.tstride = N * 4, fb.slot.tbox[1] = 32;
       fb.slot.tswizzle = (int)CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
-    } else {  // B^T stored [N][K]: one 32 x 256 box
-      fb.slot.tdim[0] = K, fb.slot.tdim[1] = N, fb.slot.tstride = K * 4, fb.slot.tbox[1] = 256;
+    } else {  // B^T stored [N][K]: one 32 x 256 box (32 x 128 per CTA of a pair)
+      fb.slot.tdim[0] = K, fb.slot.tdim[1] = N, fb.slot.tstride = K * 4, fb.slot.tbox[1] = pair ? 128 : 256;
     }
     fields.push_back(fa);  // tensor maps first: 64-byte aligned in the block
     fields.push_back(fb);
@@ -2234,12 +2236,18 @@ class Lowerer {
     emit_struct(fields);
     src << "  static constexpr bool A_MN = " << (ti.a_mn ? "true" : "false") << ", B_MN = " << (ti.b_mn ? "true" : "false")
         << ";\n};\n";
-    src << "extern \"C\" __global__ void __launch_bounds__(192, 1) " << fn << "(const __grid_constant__ " << F
-        << "::P p) { ccb::matmul_tc<" << F << ">(p); }\n\n";
+    if (pair) {
+      src << "extern \"C\" __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1) " << fn
+          << "(const __grid_constant__ " << F << "::P p) { ccb::matmul_tc2<" << F << ">(p); }\n\n";
+    } else {
+      src << "extern \"C\" __global__ void __launch_bounds__(192, 1) " << fn << "(const __grid_constant__ " << F
+          << "::P p) { ccb::matmul_tc<" << F << ">(p); }\n\n";
+    }
     LaunchSpec& l = add_launch(fn, fields);
     l.mode = GM_PERSISTENT;
-    l.work = ((M + 127) / 128) * ((N + 255) / 256);
+    l.work = pair ? 2 * ((M + 255) / 256) * ((N + 255) / 256) : ((M + 127) / 128) * ((N + 255) / 256);
     l.per_block = 1;
+    l.grid_multiple = pair ? 2 : 1;
     l.block = 192;
     l.smem = 4 * (128 * 32 * 4 + 256 * 32 * 4) + 1024 + 256;
   }

@@ -91,6 +91,7 @@ struct LaunchSpec {
   int64_t max_grid = 1 << 30;  // persistent: cap (scratch is sized for it)
   int block = 256;
   int smem = 0;  // dynamic shared memory bytes
+  int grid_multiple = 1;  // persistent grids: the grid is a multiple of this (cluster size)
   std::vector<Slot> slots;
 };
 

@@ -296,6 +296,7 @@ int ccb_program_create(const char* graph, int device, int lanes, ccb_program_t* 
       const int64_t want = (l.work + l.per_block - 1) / std::max<int64_t>(1, l.per_block);
       gx = std::max<int64_t>(1, std::min(want, cap));
       gy = 1;
+      if (l.grid_multiple > 1) gx = std::max<int64_t>(l.grid_multiple, gx / l.grid_multiple * l.grid_multiple);
     }
     if (gx > 0x7fffffff || gy > 65535) return cleanup(fail(CCB_ERR_UNSUPPORTED, "launch grid too large for " + l.fn));
     if (std::getenv("CCB_DEBUG_TUNE")) {
