@@ -690,6 +690,14 @@ def run_profile_case(args):
         c = B.compile(X.gather(n, tbl))
         ins = [("idx", Value.of_array(I32, (n,), (X.philox_word0(4, n) & (tbl - 1)).astype(np.int32))),
                ("table", Value.of_array(F32, (tbl,), np.full(tbl, 0.5, np.float32)))]
+    elif args.profile == "lsm":  # the resident LSM driver: n paths x 64 dates, 4-term basis, F64
+        from cudacaml_b200 import lsm as L
+        lp = L.CudaResident(n, 64, L.BASELINE_MARKET, "poly4")
+        for _ in range(2):
+            px = lp.price(7)
+        lp.release()
+        print(json.dumps({"price": px}))
+        return 0
     elif args.profile == "mm_tf32":  # one square tensor-core product
         a = D.param("a", F32, (n, n))
         bm = D.param("b", F32, (n, n))
@@ -717,7 +725,7 @@ def main():
     ap.add_argument("--no-secondary", action="store_true")
     ap.add_argument("--profile", default=None,
                     choices=["greeks64", "greeks32", "reduce", "scan", "rows_reduce", "rows_scan", "scatter", "gather", "mlp",
-                             "mlp_tf32", "mm_tf32"],
+                             "mlp_tf32", "mm_tf32", "lsm"],
                     help="run a small fixed case (3 launches) for an ncu capture, no timing")
     ap.add_argument("--size", type=int, default=1 << 24, help="paths/elements of the --profile case")
     args = ap.parse_args()
