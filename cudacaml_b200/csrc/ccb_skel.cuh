@@ -830,18 +830,34 @@ __device__ __forceinline__ void scan_rows_warp(const typename F::P& p) {
 // out is zero-filled by the executor (a memset) before this runs; every
 // element lands through an atomic add. F provides T, idx(p,i), val(p,i);
 // P provides n (source elements), m (output elements), out, err.
+//
+// Each thread loads SCATTER_BATCH (index, value) pairs, a grid stride apart,
+// before issuing their atomics, so that many loads are in flight per thread.
+constexpr int SCATTER_BATCH = 8;
+
 template <class F>
 __device__ __forceinline__ void scatter_add(const typename F::P& p) {
+  typedef typename F::T T;
   const long long n = p.n;
   const long long nth = (long long)gridDim.x * blockDim.x;
-  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += nth) {
-    const int j = F::idx(p, i);
-    const typename F::T v = F::val(p, i);
-    if ((unsigned)j >= (unsigned long long)p.m) {
-      raise_error(p.err, ERR_SCATTER_OOB);
-      continue;
+  for (long long i0 = (long long)blockIdx.x * blockDim.x + threadIdx.x; i0 < n; i0 += nth * SCATTER_BATCH) {
+    int j[SCATTER_BATCH];
+    T v[SCATTER_BATCH];
+#pragma unroll
+    for (int u = 0; u < SCATTER_BATCH; ++u) {
+      const long long i = i0 + u * nth;
+      j[u] = i < n ? F::idx(p, i) : 0;
+      v[u] = i < n ? F::val(p, i) : T(0);
     }
-    atomicAdd(&p.out[j], v);
+#pragma unroll
+    for (int u = 0; u < SCATTER_BATCH; ++u) {
+      if (i0 + u * nth >= n) break;
+      if ((unsigned)j[u] >= (unsigned long long)p.m) {
+        raise_error(p.err, ERR_SCATTER_OOB);
+        continue;
+      }
+      atomicAdd(&p.out[j[u]], v[u]);
+    }
   }
 }
 
@@ -860,17 +876,27 @@ __device__ __forceinline__ void scatter_add_priv(const typename F::P& p) {
   for (int b = threadIdx.x; b < priv; b += blockDim.x) sh[b] = T(0);
   __syncthreads();
   const long long nth = (long long)gridDim.x * blockDim.x;
-  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += nth) {
-    const int j = F::idx(p, i);
-    const T v = F::val(p, i);
-    if ((unsigned)j >= (unsigned long long)m) {
-      raise_error(p.err, ERR_SCATTER_OOB);
-      continue;
+  for (long long i0 = (long long)blockIdx.x * blockDim.x + threadIdx.x; i0 < n; i0 += nth * SCATTER_BATCH) {
+    int j[SCATTER_BATCH];
+    T v[SCATTER_BATCH];
+#pragma unroll
+    for (int u = 0; u < SCATTER_BATCH; ++u) {
+      const long long i = i0 + u * nth;
+      j[u] = i < n ? F::idx(p, i) : 0;
+      v[u] = i < n ? F::val(p, i) : T(0);
     }
-    if (j < priv)
-      atomicAdd(&sh[j], v);
-    else
-      atomicAdd(&p.out[j], v);
+#pragma unroll
+    for (int u = 0; u < SCATTER_BATCH; ++u) {
+      if (i0 + u * nth >= n) break;
+      if ((unsigned)j[u] >= (unsigned long long)m) {
+        raise_error(p.err, ERR_SCATTER_OOB);
+        continue;
+      }
+      if (j[u] < priv)
+        atomicAdd(&sh[j[u]], v[u]);
+      else
+        atomicAdd(&p.out[j[u]], v[u]);
+    }
   }
   __syncthreads();
   for (int b = threadIdx.x; b < priv; b += blockDim.x) {
@@ -1033,6 +1059,25 @@ __device__ __forceinline__ void ld32(unsigned taddr, float* v) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// Store 32 accumulator columns of one row (cnt of them valid) at flat index
+// i0 of the product, or hand them to the fused map pass (F::EPI).
+template <class F>
+__device__ __forceinline__ void store32(const typename F::P& p, long long i0, const float* v, int cnt, bool vec) {
+  if constexpr (F::EPI) {
+    F::epi32(p, i0, v, cnt, vec);
+  } else {
+    float* dst = p.C + i0;
+    if (vec && cnt == 32) {
+#pragma unroll
+      for (int i = 0; i < 32; i += 4) *(float4*)(dst + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (i < cnt) dst[i] = v[i];
+    }
+  }
+}
+
 __device__ __forceinline__ void tile_of(long long t, int tiles_m, int tiles_n, int& tm, int& tn) {
   const long long band = (long long)GROUP_M * tiles_n;
   const int first = (int)(t / band) * GROUP_M;
@@ -1147,7 +1192,7 @@ __device__ __forceinline__ void matmul_tc(const typename F::P& p) {
     }
   } else {  // epilogue: warps 2..5, TMEM lane quadrant warp % 4
     const int q = warp & 3;
-    const bool vec = ((((unsigned long long)p.C) & 15ull) == 0) && (N % 4 == 0);
+    const bool vec = (N % 4 == 0) && F::vec_ok(p);
     int it = 0;
     for (long long t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
       int tm, tn;
@@ -1162,15 +1207,7 @@ __device__ __forceinline__ void matmul_tc(const typename F::P& p) {
         float v[32];
         __syncwarp();
         ld32(tmem + ((unsigned)(q * 32) << 16) + ab * BN + c, v);
-        if (row < M) {
-          float* dst = p.C + row * N + n0 + c;
-          if (vec && n0 + c + 32 <= N) {
-#pragma unroll
-            for (int i = 0; i < 32; i += 4) *(float4*)(dst + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
-          } else {
-            for (int i = 0; i < 32 && n0 + c + i < N; ++i) dst[i] = v[i];
-          }
-        }
+        if (row < M) store32<F>(p, row * N + n0 + c, v, N - n0 - c < 32 ? (int)(N - n0 - c) : 32, vec);
       }
       fence_before();
       __syncwarp();
@@ -1355,7 +1392,7 @@ __device__ __forceinline__ void matmul_tc2(const typename F::P& p) {
     }
   } else {  // epilogue: warps 2..5 of each CTA, TMEM lane quadrant warp % 4
     const int q = warp & 3;
-    const bool vec = ((((unsigned long long)p.C) & 15ull) == 0) && (N % 4 == 0);
+    const bool vec = (N % 4 == 0) && F::vec_ok(p);
     int it = 0;
     for (long long t = pair; t < ntiles; t += npairs, ++it) {
       int tm, tn;
@@ -1370,15 +1407,7 @@ __device__ __forceinline__ void matmul_tc2(const typename F::P& p) {
         float v[32];
         __syncwarp();
         tc::ld32(tmem + ((unsigned)(q * 32) << 16) + ab * BN + c, v);
-        if (row < M) {
-          float* dst = p.C + row * N + n0 + c;
-          if (vec && n0 + c + 32 <= N) {
-#pragma unroll
-            for (int i = 0; i < 32; i += 4) *(float4*)(dst + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
-          } else {
-            for (int i = 0; i < 32 && n0 + c + i < N; ++i) dst[i] = v[i];
-          }
-        }
+        if (row < M) tc::store32<F>(p, row * N + n0 + c, v, N - n0 - c < 32 ? (int)(N - n0 - c) : 32, vec);
       }
       tc::fence_before();
       __syncwarp();

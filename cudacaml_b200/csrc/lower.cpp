@@ -915,6 +915,8 @@ struct Group {
   int64_t rows = 0, n = 0;  // rows kernels
   int mm_a = -1, mm_b = -1; // matmul operand KNodes (built with INDEX = flat operand index)
   KCtx ctx_b;               // matmul: B operand
+  int epi = -1;             // tensor-core product: the map pass run in its epilogue
+  int fused_into = -1;      // map pass: the product whose epilogue runs it
 };
 
 struct JoinFail {};
@@ -1606,6 +1608,54 @@ class Lowerer {
     }
   }
 
+  // ------------------------------------------------------------ epilogue fusion
+  // Does group gi read tensor t?
+  bool reads_tensor(int gi, int t) const {
+    const Group& gr = groups[gi];
+    if (gr.kind == G_MATMUL_TC) return tc[gr.root].va == t || tc[gr.root].vb == t;
+    if (gr.kind == G_TRANSPOSE) return gr.val == t;
+    for (const KN& k : gr.ctx.n)
+      if (k.op == K_LOAD && k.buf == t) return true;
+    for (const KN& k : gr.ctx_b.n)
+      if (k.op == K_LOAD && k.buf == t) return true;
+    return false;
+  }
+
+  // A map pass right after a tensor-core product, over the product's
+  // elements, storing 4-byte elements and reading nothing but element i of
+  // the product, runs in the product's epilogue: the accumulator feeds the
+  // element body from registers. The element code is the pass's own, so the
+  // results are the bits the separate pass gives. Only products with
+  // K >= kEpiMinK fuse: the four epilogue warps drain a tile while the next
+  // one accumulates, and a short mainloop leaves them no time for a body. A
+  // pass that also reads another tensor stays apart: with one warp per TMEM
+  // lane quadrant those loads are latency-bound (measured on the MLP step:
+  // dZ1 in the epilogue of the K = 1024 product cost 225 us more than the
+  // separate pass).
+  static constexpr int64_t kEpiMinK = 2048;
+  void fuse_epilogues() {
+    for (int gi = 0; gi + 1 < (int)groups.size(); ++gi) {
+      Group& mm = groups[gi];
+      Group& ep = groups[gi + 1];
+      if (mm.kind != G_MATMUL_TC || ep.kind != G_MAPRED) continue;
+      const int t = mm.root;
+      const int64_t MN = g.ts[t].numel;
+      if (g.ts[g.ts[t].dep0].shape[1] < kEpiMinK) continue;
+      if (ep.domain != MN || MN >= (1LL << 31) || !ep.reds.empty() || !ep.tails.empty() || ep.stores.empty()) continue;
+      bool reads_t = false, ok = true;
+      for (const KN& k : ep.ctx.n) {
+        if (k.op != K_LOAD) continue;
+        if (k.buf != t || k.a != ep.ctx.index_node) ok = false;
+        reads_t = true;
+      }
+      for (auto& st : ep.stores)
+        if (g.ts[st.first].numel != MN || dt_size(g.ts[st.first].dt) != 4) ok = false;
+      if (!ok || !reads_t) continue;
+      mm.epi = gi + 1;
+      ep.fused_into = gi;
+    }
+  }
+
   // ------------------------------------------------------------ code generation
   Lowered* out = nullptr;
   std::ostringstream src;
@@ -2198,7 +2248,18 @@ class Lowerer {
     // 2-SM pairs (256 x 256 tiles) once both output dimensions fill a pair tile
     const bool pair = M >= 256 && N >= 256;
     const std::string fn = (pair ? "ccb_matmultc2_" : "ccb_matmultc_") + std::to_string(gi) + kname_suffix();
-    node_buf[t] = add_buf("t" + std::to_string(x.uid), 4, x.numel, BR_NODE, t, false);
+    // with a fused map pass the product itself is stored only when an output
+    // or another pass reads it
+    const int ej = gr.epi;
+    bool store_c = true;
+    if (ej >= 0) {
+      store_c = is_out[t] != 0;
+      for (int q = 0; q < (int)groups.size() && !store_c; ++q)
+        if (q != gi && q != ej && reads_tensor(q, t)) store_c = true;
+      for (auto& st : groups[ej].stores)
+        node_buf[st.first] = add_buf("t" + std::to_string(g.ts[st.first].uid), 4, g.ts[st.first].numel, BR_NODE, st.first, false);
+    }
+    if (store_c) node_buf[t] = add_buf("t" + std::to_string(x.uid), 4, x.numel, BR_NODE, t, false);
     if (node_buf[ti.va] < 0 || node_buf[ti.vb] < 0) bad("lower: internal: tensor-core operand without a buffer");
     std::vector<Field> fields;
     Field fa, fb;
@@ -2224,18 +2285,30 @@ class Lowerer {
     }
     fields.push_back(fa);  // tensor maps first: 64-byte aligned in the block
     fields.push_back(fb);
-    fields.push_back(buf_field("float* __restrict__ C", node_buf[t]));
+    if (store_c) fields.push_back(buf_field("float* __restrict__ C", node_buf[t]));
+    if (ej >= 0)
+      for (auto& st : groups[ej].stores) fields.push_back(out_field(st.first));
     fields.push_back(buf_field("unsigned* err", out->err_buf));
     fields.push_back(i64_field("M", M));
     fields.push_back(i64_field("N", N));
     fields.push_back(i64_field("K", K));
     src << "// matmul " << gi << " on tensor cores (tf32): [" << M << "x" << K << "] . [" << K << "x" << N << "], A "
         << (ti.a_mn ? "MN" : "K") << "-major from n" << g.ts[ti.va].uid << ", B " << (ti.b_mn ? "MN" : "K")
-        << "-major from n" << g.ts[ti.vb].uid << "\n";
+        << "-major from n" << g.ts[ti.vb].uid;
+    if (ej >= 0) src << "; pass " << ej << " in the epilogue" << (store_c ? "" : ", product not stored");
+    src << "\n";
     src << "struct " << F << " {\n";
     emit_struct(fields);
     src << "  static constexpr bool A_MN = " << (ti.a_mn ? "true" : "false") << ", B_MN = " << (ti.b_mn ? "true" : "false")
-        << ";\n};\n";
+        << ";\n";
+    src << "  static constexpr bool EPI = " << (ej >= 0 ? "true" : "false") << ";\n";
+    src << "  static __device__ __forceinline__ bool vec_ok(const P& p) {\n    return true";
+    if (store_c) src << " && ccb::aligned16(p.C)";
+    if (ej >= 0)
+      for (auto& st : groups[ej].stores) src << " && ccb::aligned16(p.o" << st.first << ")";
+    src << ";\n  }\n";
+    if (ej >= 0) emit_tc_epilogue(groups[ej], t, store_c);
+    src << "};\n";
     if (pair) {
       src << "extern \"C\" __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1) " << fn
           << "(const __grid_constant__ " << F << "::P p) { ccb::matmul_tc2<" << F << ">(p); }\n\n";
@@ -2250,6 +2323,42 @@ class Lowerer {
     l.grid_multiple = pair ? 2 : 1;
     l.block = 192;
     l.smem = 4 * (128 * 32 * 4 + 256 * 32 * 4) + 1024 + 256;
+  }
+
+  // epi32(p, i0, v, cnt, vec): the fused map pass over the cnt product
+  // entries v[0..cnt) at flat indices i0.. of one row (cnt = 32 and 16-byte
+  // aligned bases when vec).
+  void emit_tc_epilogue(const Group& ep, int t, bool store_c) {
+    src << "  static __device__ __forceinline__ void epi32(const P& p, long long i0, const float* v, int cnt, bool vec) {\n";
+    src << "    if (vec && cnt == 32) {\n#pragma unroll\n      for (int k = 0; k < 32; k += 4) {\n";
+    src << "        const int i = (int)(i0 + k);\n";
+    for (auto& st : ep.stores) src << "        ccb::V4<" << dt_ctype(g.ts[st.first].dt) << "> S" << st.first << ";\n";
+    for (int j = 0; j < 4; ++j) {
+      Emitter e(ep.ctx, src);
+      e.ind = "        ";
+      e.suffix = "_" + std::to_string(j);
+      e.index_text = j == 0 ? "i" : "(i + " + std::to_string(j) + ")";
+      e.direct[t] = "v[k + " + std::to_string(j) + "]";
+      for (auto& st : ep.stores) {
+        std::string val = e.val(st.second);
+        src << "        S" << st.first << ".v[" << j << "] = " << val << ";\n";
+      }
+    }
+    for (auto& st : ep.stores) src << "        ccb::st4(p.o" << st.first << " + i, S" << st.first << ");\n";
+    if (store_c) src << "        *(float4*)(p.C + i) = make_float4(v[k], v[k + 1], v[k + 2], v[k + 3]);\n";
+    src << "      }\n    } else {\n#pragma unroll\n      for (int k = 0; k < 32; ++k) {\n        if (k >= cnt) break;\n";
+    src << "        const int i = (int)(i0 + k);\n";
+    {
+      Emitter e(ep.ctx, src);
+      e.ind = "        ";
+      e.direct[t] = "v[k]";
+      for (auto& st : ep.stores) {
+        std::string val = e.val(st.second);
+        src << "        p.o" << st.first << "[i] = " << val << ";\n";
+      }
+    }
+    if (store_c) src << "        p.C[i] = v[k];\n";
+    src << "      }\n    }\n  }\n";
   }
 
   void emit_transpose(int gi) {
@@ -2306,7 +2415,9 @@ class Lowerer {
     src << "// generated by cudacaml-b200 for sm_100a: " << g.name << "\n#include \"ccb_skel.cuh\"\n\n";
     for (int gi = 0; gi < (int)groups.size(); ++gi) {
       switch (groups[gi].kind) {
-        case G_MAPRED: emit_mapred(gi); break;
+        case G_MAPRED:
+          if (groups[gi].fused_into < 0) emit_mapred(gi);
+          break;
         case G_SCAN_FLAT:
         case G_SCAN_ROWS: emit_scan(gi); break;
         case G_RED_ROWS: emit_red_rows(gi); break;
@@ -2352,6 +2463,7 @@ int lower_graph(const GGraph& g, Lowered& out) {
     Lowerer L(g);
     L.analyse();
     L.group_all();
+    L.fuse_epilogues();
     L.generate(out);
   } catch (const LowerError& e) {
     return fail(e.code, e.what());

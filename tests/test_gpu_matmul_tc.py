@@ -121,3 +121,44 @@ def test_mlp_multi_allreduce_sum_one_device():
         assert np.array_equal(v.data, want[name].data), name
     with pytest.raises(ValueError):
         M.Multi([0], bsz, lambda k: X.mlp_step(k, din, hid, dout), split=["W1"]).run(ins)
+
+
+FUSION_SHAPES = [(256, 2048, 512, False), (300, 2048, 260, False), (256, 2048, 258, True)]
+
+
+@pytest.mark.parametrize("m,k,n,tb", FUSION_SHAPES, ids=lambda v: str(v))
+def test_epilogue_fusion_matches_separate_pass(m, k, n, tb):
+    """A map pass fused into the product's epilogue gives the bits of the
+    same pass run on the stored product: whole 32-column row chunks (vector
+    path), a last chunk of 4 columns, and rows of 258 columns (no 16-byte
+    alignment: scalar path). The element function has no multiply feeding
+    an add, so FMA contraction cannot differ between the two kernels."""
+    rng = np.random.default_rng(m + k + n)
+    a = (rng.standard_normal((m, k)) / np.sqrt(k)).astype(np.float32)
+    b = rng.standard_normal((n, k) if tb else (k, n)).astype(np.float32)
+    pa, pb = D.param("a", F32, a.shape), D.param("b", F32, b.shape)
+    z = D.matmul(pa, D.transpose(pb) if tb else pb)
+
+    def f(v):
+        return D.div(D.const(F32, 1.0), D.add(D.const(F32, 1.0), D.exp(v)))
+
+    ins = [("a", Value.of_array(F32, a.shape, a)), ("b", Value.of_array(F32, b.shape, b))]
+
+    def run(graph, inputs):
+        c = cuda.compile(graph, matmul="tf32")
+        try:
+            return c.plan(), {k_: v.data.reshape(-1) for k_, v in cuda.run(c, inputs)}
+        finally:
+            cuda.release(c)
+
+    _, prod = run(Graph("p", [("z", z)]), ins)
+    pz = D.param("z", F32, (m, n))
+    _, sep = run(Graph("q", [("t", D.map(f, pz))]), [("z", Value.of_array(F32, (m, n), prod["z"]))])
+    plan, fused = run(Graph("fz", [("t", D.map(f, z))]), ins)
+    assert "ccb_mapreduce_" not in plan
+    assert np.array_equal(fused["t"].view(np.uint32), sep["t"].view(np.uint32))
+    # the product stored beside the pass's result
+    plan, both = run(Graph("fb", [("t", D.map(f, z)), ("z", z)]), ins)
+    assert "ccb_mapreduce_" not in plan
+    assert np.array_equal(both["z"].view(np.uint32), prod["z"].view(np.uint32))
+    assert np.array_equal(both["t"].view(np.uint32), sep["t"].view(np.uint32))

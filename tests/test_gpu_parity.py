@@ -171,6 +171,30 @@ def test_scatter_zipf_and_gather_config():
     diff(X.gather(n, tbl), [("idx", gi), ("table", t)], tol=0.0)
 
 
+@pytest.mark.parametrize("n,bins", [(3_000_007, 1 << 20), (12_345, 100), (5, 3)])
+def test_scatter_i32_exact_ragged(n, bins):
+    # I32 sums are exact in any order: the batched loop's ragged last batch,
+    # privatised (low) and global (high) bins against a numpy histogram
+    idx = X.zipf_indices(11, n, bins)
+    s = (np.arange(n) % 5 - 1).astype(np.int32)
+    g = Graph("sc", [("h", D.scatter_add(D.param("idx", I32, (n,)), D.param("s", I32, (n,)), (bins,)))])
+    c = cuda.compile(g)
+    got = dict(cuda.run(c, [("idx", Value.of_array(I32, (n,), idx)), ("s", Value.of_array(I32, (n,), s))]))["h"].data
+    cuda.release(c)
+    want = np.bincount(idx, weights=s.astype(np.int64), minlength=bins).astype(np.int64)
+    assert np.array_equal(got.astype(np.int64), want)
+
+
+def test_out_of_bounds_scatter_is_reported():
+    idx = D.param("idx", I32, (4,))
+    c = cuda.compile(Graph("s", [("h", D.scatter_add(idx, D.param("s", I32, (4,)), (4,)))]))
+    ones = Value.of_list(I32, (4,), [1, 1, 1, 1])
+    with pytest.raises(R.CcbError):
+        cuda.run(c, [("idx", Value.of_list(I32, (4,), [0, 1, 9, 2])), ("s", ones)])
+    out = dict(cuda.run(c, [("idx", Value.of_list(I32, (4,), [3, 3, 1, 0])), ("s", ones)]))
+    assert out["h"].to_list() == [1, 1, 0, 2]
+
+
 def test_out_of_bounds_gather_is_reported():
     idx = D.param("idx", I32, (4,))
     t = D.param("t", F32, (4,))

@@ -126,7 +126,10 @@ def test_matmul_precision_option_and_default():
     assert "matmultc" not in B.lower_info(g)["plan"]  # F32 arithmetic unless asked
     info = B.lower_info(g, matmul="tf32")
     assert len(re.findall(r"launch ccb_matmultc2?_", info["plan"])) == 5
-    assert info["launches"] == 8  # 5 products + A1, dY(+loss), dZ1 element passes
+    # 5 products + the dY(+loss) and dZ1 passes; A1 = tanh_like(Z1) runs in
+    # the epilogue of the Z1 product (K = 256 here is below the fusion bound)
+    assert info["launches"] == 8
+    assert B.lower_info(X.mlp_step(512, 2048, 512, 128), matmul="tf32")["launches"] == 7
     with pytest.raises(ValueError):
         B.lower_info(g, matmul="bf16")
     assert nvrtc_ok(info["source"], "mlp_tf32") > 0
@@ -162,3 +165,32 @@ def test_tensor_core_eligibility():
     assert not _tc_lines(B.lower_info(mm(F32, 16, 16, 16), matmul="tf32"))      # tiny: exact kernel
     assert not _tc_lines(B.lower_info(mm(F32, 256, 255, 256), matmul="tf32"))   # 1020-byte rows: no TMA
     assert not _tc_lines(B.lower_info(mm(F32, 4, 4096, 4), matmul="tf32"))      # split-K reduction
+
+
+def test_tensor_core_epilogue_fusion():
+    a = D.param("a", F32, (256, 2048))
+    b = D.param("b", F32, (2048, 512))
+    z = D.matmul(a, b)
+    t = D.map(lambda v: D.exp(v), z)
+    # the product read by nothing else: the pass runs in the epilogue, the
+    # product is not stored
+    info = B.lower_info(Graph("f", [("t", t)]), matmul="tf32")
+    assert "launch ccb_mapreduce_" not in info["plan"] and info["launches"] == 1
+    assert "pass 1 in the epilogue, product not stored" in _tc_lines(info)[0]
+    assert info["plan"].count("alloc t") == 1
+    # the product is also an output: stored beside the pass's result
+    info = B.lower_info(Graph("f", [("t", t), ("z", z)]), matmul="tf32")
+    assert info["launches"] == 1 and _tc_lines(info)[0].endswith("pass 1 in the epilogue")
+    assert nvrtc_ok(info["source"], "fused") > 0
+    # passes that stay apart: a reduction, a second input, a neighbour of
+    # element i, a short inner dimension
+    s = D.reduce(D.add, D.const(F32, 0.0), D.reshape((256 * 512,), t))
+    assert B.lower_info(Graph("f", [("s", s)]), matmul="tf32")["launches"] == 2
+    w = D.param("w", F32, (256, 512))
+    two = D.map2(lambda u, v: D.mul(u, v), z, w)
+    assert B.lower_info(Graph("f", [("s", two)]), matmul="tf32")["launches"] == 2
+    sq = D.matmul(a, D.param("c", F32, (2048, 256)))
+    sym = D.map2(lambda u, v: D.add(u, v), sq, D.transpose(sq))
+    assert B.lower_info(Graph("f", [("s", sym)]), matmul="tf32")["launches"] == 2
+    short = D.map(lambda v: D.exp(v), D.matmul(D.param("d", F32, (256, 1024)), D.param("e", F32, (1024, 512))))
+    assert B.lower_info(Graph("f", [("s", short)]), matmul="tf32")["launches"] == 2
