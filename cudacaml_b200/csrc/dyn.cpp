@@ -79,6 +79,13 @@ const Driver& driver() {
     S(cuGetErrorString, "cuGetErrorString")
     S(cuPointerGetAttribute, "cuPointerGetAttribute")
     S(cuTensorMapEncodeTiled, "cuTensorMapEncodeTiled")
+    S(cuStreamBeginCapture, "cuStreamBeginCapture_v2")
+    S(cuStreamEndCapture, "cuStreamEndCapture")
+    S(cuStreamIsCapturing, "cuStreamIsCapturing")
+    S(cuGraphInstantiateWithFlags, "cuGraphInstantiateWithFlags")
+    S(cuGraphLaunch, "cuGraphLaunch")
+    S(cuGraphExecDestroy, "cuGraphExecDestroy")
+    S(cuGraphDestroy, "cuGraphDestroy")
 #undef S
     d.ok = ok;
   });

@@ -56,6 +56,13 @@ struct Driver {
   CCB_DRV(cuGetErrorString)
   CCB_DRV(cuPointerGetAttribute)
   CCB_DRV(cuTensorMapEncodeTiled)
+  CCB_DRV(cuStreamBeginCapture)
+  CCB_DRV(cuStreamEndCapture)
+  CCB_DRV(cuStreamIsCapturing)
+  CCB_DRV(cuGraphInstantiateWithFlags)
+  CCB_DRV(cuGraphLaunch)
+  CCB_DRV(cuGraphExecDestroy)
+  CCB_DRV(cuGraphDestroy)
 #undef CCB_DRV
 };
 

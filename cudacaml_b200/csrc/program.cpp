@@ -24,6 +24,7 @@ struct Lane {
   CUevent done = nullptr;
   std::vector<CUdeviceptr> bufs;
   unsigned* host_err = nullptr;  // pinned slot the error word is copied to
+  bool err_pending = false;      // resident runs since the last copy of the word
   uint64_t epoch = 0;
   // Encoded tensor maps, keyed by (launch, slot), with the base they encode.
   std::unordered_map<int64_t, std::pair<CUdeviceptr, CUtensorMap>> tmaps;
@@ -39,11 +40,21 @@ struct Program {
   int num_launch_ops = 0;
 };
 
-// The device error word of a lane accumulates over runs (each run copies it
-// to the lane's pinned slot, nothing clears it) until a check reports it;
-// then it is cleared, so a chain of runs checked once reports any error
-// raised anywhere in the chain.
-int lane_check(Program& P, int lane) {
+// The device error word of a lane accumulates over runs until a check
+// reports it; then it is cleared, so a chain of runs checked once reports any
+// error raised anywhere in the chain. Runs with host buffers copy the word to
+// the lane's pinned slot as their last step; device-resident runs only mark
+// it pending (no copy between their kernels). An explicit check (`fresh`)
+// always reads the word once `stream` has drained, which also covers runs
+// replayed from a captured graph.
+int lane_check(Program& P, int lane, CUstream stream, bool fresh) {
+  Lane& lnp = P.lanes[lane];
+  if (lnp.err_pending || fresh) {
+    const Driver& d = driver();
+    CCB_CU(d.cuMemcpyDtoHAsync(lnp.host_err, lnp.bufs[P.L.err_buf], 4, stream));
+    CCB_CU(d.cuStreamSynchronize(stream));
+    lnp.err_pending = false;
+  }
   const unsigned e = *P.lanes[lane].host_err;
   if (e == 0) return CCB_OK;
   {
@@ -145,6 +156,16 @@ int issue(Program& P, int lane, const void* const* h_in, void* const* h_out, con
       if (p.bytes) CCB_CU(d.cuMemcpyHtoDAsync(ptr[p.buf], h_in[i], p.bytes, stream));
     }
   }
+  // Under stream capture the launch arguments are frozen into the graph; a
+  // flat scan's per-run epoch would then repeat on every replay.
+  CUstreamCaptureStatus cs = CU_STREAM_CAPTURE_STATUS_NONE;
+  CCB_CU(d.cuStreamIsCapturing(stream, &cs));
+  const bool capturing = cs != CU_STREAM_CAPTURE_STATUS_NONE;
+  if (capturing)
+    for (const LaunchSpec& l : P.L.launches)
+      for (const Slot& sl : l.slots)
+        if (sl.kind == SL_EPOCH)
+          return fail(CCB_ERR_INVALID, "graph capture: " + l.fn + " (a flat scan) cannot be replayed from a graph");
   ln.epoch = ln.epoch % ((1u << 30) - 2) + 1;
   std::vector<uint64_t> blk;
   for (const OpSpec& op : P.L.ops) {
@@ -181,8 +202,13 @@ int issue(Program& P, int lane, const void* const* h_in, void* const* h_out, con
       if (o.bytes) CCB_CU(d.cuMemcpyDtoHAsync(h_out[j], ptr[o.buf], o.bytes, stream));
     }
   }
-  CCB_CU(d.cuMemcpyDtoHAsync(ln.host_err, ln.bufs[P.L.err_buf], 4, stream));
-  CCB_CU(d.cuEventRecord(ln.done, stream));
+  if (h_in || h_out) {
+    CCB_CU(d.cuMemcpyDtoHAsync(ln.host_err, ln.bufs[P.L.err_buf], 4, stream));
+    ln.err_pending = false;
+  } else {
+    ln.err_pending = true;
+  }
+  if (!capturing) CCB_CU(d.cuEventRecord(ln.done, stream));
   return CCB_OK;
 }
 
@@ -412,7 +438,7 @@ int ccb_program_wait(ccb_program_t prog, int lane) {
   CCB_TRY(need_device(P));
   CCB_TRY(check_lane(P, lane));
   CCB_CU(driver().cuEventSynchronize(P->lanes[lane].done));
-  return lane_check(*P, lane);
+  return lane_check(*P, lane, P->lanes[lane].stream, false);
 }
 
 int ccb_program_run(ccb_program_t prog, const void* const* inputs, void* const* outputs) {
@@ -434,8 +460,9 @@ int ccb_program_check(ccb_program_t prog, int lane, ccb_stream_t stream) {
   Program* P = as_prog(prog);
   CCB_TRY(need_device(P));
   CCB_TRY(check_lane(P, lane));
-  CCB_CU(driver().cuStreamSynchronize(stream ? (CUstream)stream : P->lanes[lane].stream));
-  return lane_check(*P, lane);
+  const CUstream s = stream ? (CUstream)stream : P->lanes[lane].stream;
+  CCB_CU(driver().cuStreamSynchronize(s));
+  return lane_check(*P, lane, s, true);
 }
 
 int ccb_program_lane_stream(ccb_program_t prog, int lane, ccb_stream_t* stream) {

@@ -319,6 +319,40 @@ int ccb_stream_wait_event(ccb_stream_t s, ccb_event_t e) {
   return CCB_OK;
 }
 
+int ccb_graph_begin(ccb_stream_t s) {
+  CCB_TRY(ensure_current());
+  if (!s) return fail(CCB_ERR_INVALID, "graph_begin: the legacy default stream cannot be captured");
+  CCB_CU(driver().cuStreamBeginCapture((CUstream)s, CU_STREAM_CAPTURE_MODE_THREAD_LOCAL));
+  return CCB_OK;
+}
+
+int ccb_graph_end(ccb_stream_t s, ccb_graph_t* graph) {
+  CCB_TRY(ensure_current());
+  if (!graph) return fail(CCB_ERR_INVALID, "graph_end: null output");
+  const Driver& d = driver();
+  CUgraph g = nullptr;
+  CCB_CU(d.cuStreamEndCapture((CUstream)s, &g));
+  CUgraphExec e = nullptr;
+  const CUresult r = d.cuGraphInstantiateWithFlags(&e, g, 0);
+  d.cuGraphDestroy(g);
+  if (r != CUDA_SUCCESS) return cu_fail(r, "cuGraphInstantiateWithFlags");
+  *graph = e;
+  return CCB_OK;
+}
+
+int ccb_graph_launch(ccb_graph_t graph, ccb_stream_t s) {
+  CCB_TRY(ensure_current());
+  CCB_CU(driver().cuGraphLaunch((CUgraphExec)graph, (CUstream)s));
+  return CCB_OK;
+}
+
+int ccb_graph_destroy(ccb_graph_t graph) {
+  if (!graph) return CCB_OK;
+  CCB_TRY(ensure_current());
+  CCB_CU(driver().cuGraphExecDestroy((CUgraphExec)graph));
+  return CCB_OK;
+}
+
 static char* dup_string(const std::string& s) {
   char* p = (char*)std::malloc(s.size() + 1);
   std::memcpy(p, s.c_str(), s.size() + 1);

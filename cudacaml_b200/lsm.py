@@ -331,58 +331,80 @@ class CudaResident:
                          "cf_b": R.Buffer(n * 8), "seed": R.Buffer(4), "t": R.Buffer(4 * ns), "beta": R.Buffer(nb * 8),
                          "xtx": R.Buffer(nb * nb * 8), "xty": R.Buffer(nb * 8), "sum": R.Buffer(8)}
             self.bufs["t"].upload(np.arange(ns, dtype=np.int32))  # date t lives at t + 4 t bytes
+        self.graph = None  # the captured price, made by the first price()
 
-    def price(self, seed: int, trace=None) -> float:
-        """Generation, the transpose and all dates run back to back on one
-        stream: per date regress, the graph solve of the normal equations
-        (beta stays on the device) and update. The host only launches; with
-        `trace` the normal equations are also copied out each date (which
-        synchronises)."""
+    def _issue(self, stream, trace=None):
+        """The device work of one price on `stream`: generation from the seed
+        in bufs["seed"], the transpose, every date (regress, the graph solve
+        of the normal equations, update) and the sum of the final cash flows
+        into bufs["sum"]. With `trace` the normal equations are also copied
+        out each date (which synchronises)."""
         cuda, R = self.cuda, self.R
-        n, ns, nb = self.n_paths, self.n_steps, self.nb
+        ns, nb = self.n_steps, self.nb
         b = self.bufs
-        stream = self.regress.lane_stream(0)
-        progs = (self.paths, self.dates, self.final, self.regress, self.solve, self.update)
 
         def bind(c, **ptrs):  # device pointers in the program's param order
             return [ptrs[name] for name, _, _ in c.params]
 
+        cuda.run_device_ptrs(self.paths, bind(self.paths, seed=b["seed"].ptr), [b["S"].ptr], stream)
+        cuda.run_device_ptrs(self.dates, bind(self.dates, S=b["S"].ptr), [b["ST"].ptr], stream)
+        # initial cash flow: intrinsic value at maturity (last column), on the device
+        cuda.run_device_ptrs(self.final, bind(self.final, S=b["S"].ptr), [b["cf_a"].ptr], stream)
+        xtx = np.empty(nb * nb)
+        xty = np.empty(nb)
+        beta_outs = [b["beta"].ptr + 8 * j for j in range(nb)]
+        cur, nxt = b["cf_a"], b["cf_b"]
+        for step in range(ns - 2, -1, -1):
+            t_ptr = b["t"].ptr + 4 * step
+            outs = {"xtx": b["xtx"].ptr, "xty": b["xty"].ptr}
+            cuda.run_device_ptrs(self.regress, bind(self.regress, S=b["ST"].ptr, cf=cur.ptr, t=t_ptr),
+                                 [outs[name] for name, _, _ in self.regress.outputs], stream)
+            if trace is not None:
+                R.check(R.lib().ccb_memcpy_d2h(xtx.ctypes.data, b["xtx"].ptr, xtx.nbytes, stream))
+                R.check(R.lib().ccb_memcpy_d2h(xty.ctypes.data, b["xty"].ptr, xty.nbytes, stream))
+                cuda.check_device(self.regress, stream)
+                trace.append((step, xtx.copy(), xty.copy()))
+            cuda.run_device_ptrs(self.solve, bind(self.solve, xtx=b["xtx"].ptr, xty=b["xty"].ptr),
+                                 [beta_outs[int(name[1:])] for name, _, _ in self.solve.outputs], stream)
+            cuda.run_device_ptrs(self.update, bind(self.update, S=b["ST"].ptr, cf=cur.ptr, t=t_ptr, beta=b["beta"].ptr),
+                                 [nxt.ptr], stream)
+            cur, nxt = nxt, cur
+        # the mean of the discounted cash flows (lsm.ml:303-305): summed on the device
+        cuda.run_device_ptrs(self.total, [cur.ptr], [b["sum"].ptr], stream)
+
+    def price(self, seed: int, trace=None) -> float:
+        """Generation, the transpose and all dates run back to back on one
+        stream. The first call captures that work as a CUDA graph (about 190
+        program runs); every call then uploads the seed, replays the graph
+        with one launch and reads the sum back. With `trace` the work is
+        issued run by run instead, copying the normal equations out each
+        date."""
+        cuda, R = self.cuda, self.R
+        b = self.bufs
+        stream = self.regress.lane_stream(0)
+        progs = (self.paths, self.dates, self.final, self.regress, self.solve, self.update, self.total)
         with R.with_device(self.device):
             seed_h = np.array([seed], np.int32)
             R.check(R.lib().ccb_memcpy_h2d(b["seed"].ptr, seed_h.ctypes.data, 4, stream))
-            cuda.run_device_ptrs(self.paths, bind(self.paths, seed=b["seed"].ptr), [b["S"].ptr], stream)
-            cuda.run_device_ptrs(self.dates, bind(self.dates, S=b["S"].ptr), [b["ST"].ptr], stream)
-            # initial cash flow: intrinsic value at maturity (last column), on the device
-            cuda.run_device_ptrs(self.final, bind(self.final, S=b["S"].ptr), [b["cf_a"].ptr], stream)
-            xtx = np.empty(nb * nb)
-            xty = np.empty(nb)
-            beta_outs = [b["beta"].ptr + 8 * j for j in range(nb)]
-            cur, nxt = b["cf_a"], b["cf_b"]
-            for step in range(ns - 2, -1, -1):
-                t_ptr = b["t"].ptr + 4 * step
-                outs = {"xtx": b["xtx"].ptr, "xty": b["xty"].ptr}
-                cuda.run_device_ptrs(self.regress, bind(self.regress, S=b["ST"].ptr, cf=cur.ptr, t=t_ptr),
-                                     [outs[name] for name, _, _ in self.regress.outputs], stream)
-                if trace is not None:
-                    R.check(R.lib().ccb_memcpy_d2h(xtx.ctypes.data, b["xtx"].ptr, xtx.nbytes, stream))
-                    R.check(R.lib().ccb_memcpy_d2h(xty.ctypes.data, b["xty"].ptr, xty.nbytes, stream))
-                    cuda.check_device(self.regress, stream)
-                    trace.append((step, xtx.copy(), xty.copy()))
-                cuda.run_device_ptrs(self.solve, bind(self.solve, xtx=b["xtx"].ptr, xty=b["xty"].ptr),
-                                     [beta_outs[int(name[1:])] for name, _, _ in self.solve.outputs], stream)
-                cuda.run_device_ptrs(self.update, bind(self.update, S=b["ST"].ptr, cf=cur.ptr, t=t_ptr, beta=b["beta"].ptr),
-                                     [nxt.ptr], stream)
-                cur, nxt = nxt, cur
-            # the mean of the discounted cash flows (lsm.ml:303-305): summed on the device
-            cuda.run_device_ptrs(self.total, [cur.ptr], [b["sum"].ptr], stream)
+            if trace is not None:
+                self._issue(stream, trace)
+            else:
+                if self.graph is None:
+                    with R.Graph.capture(stream) as g:
+                        self._issue(stream)
+                    self.graph = g
+                self.graph.launch(stream)
             tot = np.empty(1)
             R.check(R.lib().ccb_memcpy_d2h(tot.ctypes.data, b["sum"].ptr, 8, stream))
-            for c in progs + (self.total,):  # each program's error word, accumulated over all its runs
+            for c in progs:  # each program's error word, accumulated over all its runs
                 cuda.check_device(c, stream)
-        return self.disc * float(tot[0]) / n
+        return self.disc * float(tot[0]) / self.n_paths
 
     def release(self):
         with self.R.with_device(self.device):
+            if self.graph is not None:
+                self.graph.destroy()
+                self.graph = None
             for buf in self.bufs.values():
                 buf.free()
         self.bufs = {}

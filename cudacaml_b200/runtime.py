@@ -113,6 +113,10 @@ def _declare(L):
         "ccb_noalloc_last_error": (c.c_char_p, []),
         "ccb_group_start": (I, []),
         "ccb_group_end": (I, []),
+        "ccb_graph_begin": (I, [P]),
+        "ccb_graph_end": (I, [P, c.POINTER(P)]),
+        "ccb_graph_launch": (I, [P, P]),
+        "ccb_graph_destroy": (I, [P]),
     }
     for name, (res, args) in sigs.items():
         f = getattr(L, name)
@@ -241,6 +245,48 @@ class Stream:
         if self.h:
             check(lib().ccb_stream_destroy(self.h))
             self.h = None
+
+
+class Graph:
+    """Work captured from a stream and replayed with one launch (a CUDA
+    graph). ``with Graph.capture(stream) as g: ...issue work on stream...``
+    then ``g.launch(stream)`` any number of times; ``destroy`` frees it."""
+
+    def __init__(self, h):
+        self.h = h
+
+    @staticmethod
+    def capture(stream):
+        return _Capture(stream)
+
+    def launch(self, stream):
+        check(lib().ccb_graph_launch(self.h, stream.h if isinstance(stream, Stream) else stream))
+
+    def destroy(self):
+        if self.h:
+            check(lib().ccb_graph_destroy(self.h))
+            self.h = None
+
+
+class _Capture:
+    def __init__(self, stream):
+        self.stream = stream.h if isinstance(stream, Stream) else stream
+        self.graph = None
+
+    def __enter__(self):
+        check(lib().ccb_graph_begin(self.stream))
+        self.graph = Graph(None)
+        return self.graph
+
+    def __exit__(self, et, ev, tb):
+        h = ctypes.c_void_p()
+        rc = lib().ccb_graph_end(self.stream, ctypes.byref(h))
+        if et is None:
+            check(rc)
+            self.graph.h = h.value
+        elif rc == 0 and h.value:  # the capture ended; drop what it held
+            lib().ccb_graph_destroy(h.value)
+        return False
 
 
 class Event:

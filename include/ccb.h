@@ -146,7 +146,8 @@ int ccb_program_run(ccb_program_t prog, const void* const* inputs, void* const* 
  * lib/backend_cuda/executor.ml:181-244): kernels read `inputs[i]` and write
  * `outputs[j]` (caller-owned device pointers of the exact byte size) directly.
  * Issued on `stream` (NULL: the lane's own stream); it does not synchronise.
- * ccb_program_check then synchronises that stream and reads the error word.
+ * ccb_program_check then synchronises that stream and reads the error word
+ * (runs with host buffers copy it as their last step; device runs do not).
  * A lane's error word accumulates over runs until a wait or check reports it
  * (and clears it), so a chain of device runs checked once reports an error
  * raised anywhere in the chain. */
@@ -155,6 +156,22 @@ int ccb_program_run_device(ccb_program_t prog, int lane, const void* const* inpu
 int ccb_program_check(ccb_program_t prog, int lane, ccb_stream_t stream);
 /* Kernel launches per run (for the bench's gpu_launches count). */
 int ccb_program_lane_stream(ccb_program_t prog, int lane, ccb_stream_t* stream);
+
+/* ---------------------------------------------------------------- CUDA graphs
+ * No counterpart in the reference (its executor launches every kernel from
+ * the host). Work issued on `s` between ccb_graph_begin and ccb_graph_end
+ * (program runs with ccb_program_run_device, copies, memsets, events) is
+ * captured instead of run and instantiated once; ccb_graph_launch replays it
+ * with one launch. Pointers and sizes are fixed at capture; device-resident
+ * runs copy no error word, so ccb_program_check after a replay reports errors
+ * raised in it. A run of a program with a flat scan is refused while
+ * capturing (its look-back tags status words with a per-run epoch, which a
+ * replay would repeat). Nothing that synchronises may be issued meanwhile. */
+typedef void* ccb_graph_t;
+int ccb_graph_begin(ccb_stream_t s);
+int ccb_graph_end(ccb_stream_t s, ccb_graph_t* graph);
+int ccb_graph_launch(ccb_graph_t graph, ccb_stream_t s);
+int ccb_graph_destroy(ccb_graph_t graph);
 
 /* ---------------------------------------------------------------- no-allocation sum
  * No counterpart in the reference. For callers that cannot allocate device

@@ -322,6 +322,107 @@ def test_s16_resident_chain_sum():
     cuda.release(cs)
 
 
+def test_resident_chain_reports_an_error_once():
+    # device-resident runs copy no error word; the check after a chain of
+    # them reports an out-of-range gather raised in any run, once
+    idx = D.param("idx", I32, (4,))
+    t = D.param("t", F32, (4,))
+    c = cuda.compile(Graph("g", [("g", D.gather(idx, t))]))
+    tv = cuda.upload(Value.of_list(F32, (4,), [1, 2, 3, 4]))
+    good = cuda.upload(Value.of_list(I32, (4,), [3, 2, 1, 0]))
+    bad = cuda.upload(Value.of_list(I32, (4,), [0, 9, 1, 0]))
+    out = R.Buffer(16)
+    order = [p_ for p_, _, _ in c.params]
+
+    def run(ix):
+        ptrs = {"idx": ix.buf.ptr, "t": tv.buf.ptr}
+        cuda.run_device_ptrs(c, [ptrs[n_] for n_ in order], [out.ptr], None)
+
+    for ix in (good, bad, good, good):
+        run(ix)
+    with pytest.raises(R.CcbError):
+        cuda.check_device(c, None)
+    cuda.check_device(c, None)  # reported once, then cleared
+    run(good)
+    cuda.check_device(c, None)
+    got = np.empty(4, np.float32)
+    out.download(got)
+    assert got.tolist() == [4, 3, 2, 1]
+    for v in (tv, good, bad):
+        cuda.free_resident(v)
+    out.free()
+    cuda.release(c)
+
+
+def test_graph_capture_replays_resident_runs():
+    # two chained resident runs captured once, replayed with new data in the
+    # same buffers; a captured gather error is reported by the check after
+    # the replay; a flat scan is refused while capturing, and the stream is
+    # usable afterwards
+    n = 4096
+    c = cuda.compile(X.saxpy(n, 2.0))
+    s = c.lane_stream(0)
+    x, y, r, t = R.Buffer(4 * n), R.Buffer(4 * n), R.Buffer(4 * n), R.Buffer(4)
+    order = [p_ for p_, _, _ in c.params]
+    outs = [nm for nm, _, _ in c.outputs]
+    bufs = {"r": r.ptr, "s": t.ptr}
+
+    def issue(xp, yp):
+        ptrs = {"x": xp, "y": yp}
+        cuda.run_device_ptrs(c, [ptrs[k] for k in order], [bufs[k] for k in outs], s)
+
+    with R.Graph.capture(s) as g:
+        issue(x.ptr, y.ptr)
+        issue(r.ptr, y.ptr)  # r = 2 (2x + y) + y
+    for k in range(3):
+        xv = (np.arange(n) % 7 + k).astype(np.float32)
+        yv = (np.arange(n) % 5).astype(np.float32)
+        x.upload(xv)
+        y.upload(yv)
+        g.launch(s)
+        cuda.check_device(c, s)
+        got = np.empty(n, np.float32)
+        r.download(got)
+        assert np.array_equal(got, 2 * (2 * xv + yv) + yv)
+    g.destroy()
+    cuda.release(c)
+    for b_ in (x, y, r, t):
+        b_.free()
+
+    gi = cuda.compile(Graph("g", [("g", D.gather(D.param("idx", I32, (4,)), D.param("t", F32, (4,))))]))
+    tv = cuda.upload(Value.of_list(F32, (4,), [1, 2, 3, 4]))
+    ix = cuda.upload(Value.of_list(I32, (4,), [0, 1, 2, 3]))
+    o = R.Buffer(16)
+    si = gi.lane_stream(0)
+    ptrs = {"idx": ix.buf.ptr, "t": tv.buf.ptr}
+    with R.Graph.capture(si) as gg:
+        cuda.run_device_ptrs(gi, [ptrs[p_] for p_, _, _ in gi.params], [o.ptr], si)
+    gg.launch(si)
+    cuda.check_device(gi, si)
+    ix.buf.upload(np.array([0, 7, 2, 3], np.int32))
+    gg.launch(si)
+    with pytest.raises(R.CcbError):
+        cuda.check_device(gi, si)
+    gg.destroy()
+    for v in (tv, ix):
+        cuda.free_resident(v)
+    o.free()
+    cuda.release(gi)
+
+    cs = cuda.compile(X.scan_flat(1 << 20, F32))
+    ss = cs.lane_stream(0)
+    xb, ob = R.Buffer(4 << 20), R.Buffer(4 << 20)
+    with pytest.raises(R.CcbError, match="flat scan"):
+        with R.Graph.capture(ss):
+            cuda.run_device_ptrs(cs, [xb.ptr], [ob.ptr], ss)
+    R.check(R.lib().ccb_memset_d8(xb.ptr, 0, 4 << 20, ss))
+    cuda.run_device_ptrs(cs, [xb.ptr], [ob.ptr], ss)
+    cuda.check_device(cs, ss)
+    xb.free()
+    ob.free()
+    cuda.release(cs)
+
+
 def test_s5_pool_stable():
     n = 4096
     c = cuda.compile(X.saxpy(n, 2.0))
@@ -423,6 +524,11 @@ def test_lsm_drivers_match_interp(basis):
     pc = L.Make(cuda, n, ns, m, basis).price(11, trace=tc)
     res = L.CudaResident(n, ns, m, basis)
     pr = res.price(11, trace=tr)
+    # the captured graph (first untraced call) and its replays: the same bits
+    pg = [res.price(11) for _ in range(3)]
+    assert res.graph is not None
+    assert pg == [pr] * 3
+    assert res.price(12) != pr  # a new seed reaches the replayed generator
     res.release()
     for (si, ai, bi), (sc, ac, bc), (sr, ar, br) in zip(ti, tc, tr):
         assert si == sc == sr
