@@ -311,7 +311,9 @@ int ccb_program_create(const char* graph, int device, int lanes, ccb_program_t* 
     if (r != CUDA_SUCCESS) return cleanup(cu_fail(r, "cuModuleGetFunction"));
     P->fns.push_back(f);
     int64_t gx = l.gx, gy = l.gy;
-    if (l.smem > 48 * 1024) {
+    int static_smem = 0;
+    d.cuFuncGetAttribute(&static_smem, CU_FUNC_ATTRIBUTE_SHARED_SIZE_BYTES, f);
+    if (static_smem + l.smem > 48 * 1024) {  // above the default limit: opt in
       r = d.cuFuncSetAttribute(f, CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES, l.smem);
       if (r != CUDA_SUCCESS) return cleanup(cu_fail(r, "cuFuncSetAttribute(max dynamic shared memory)"));
     }

@@ -185,6 +185,21 @@ def test_scatter_i32_exact_ragged(n, bins):
     assert np.array_equal(got.astype(np.int64), want)
 
 
+@pytest.mark.parametrize("bins", [5, 3000, 1 << 16])
+def test_scatter_f64_tiers(bins):
+    # 8-byte values: 16 per-thread bins, 2048 block-private bins, the rest
+    # global; sums of 2^20 F64 updates against an exact F64 histogram
+    n = (1 << 20) + 17
+    idx = X.zipf_indices(13, n, bins)
+    v = np.random.default_rng(bins).random(n)
+    g = Graph("s64", [("h", D.scatter_add(D.param("idx", I32, (n,)), D.param("s", F64, (n,)), (bins,)))])
+    c = cuda.compile(g)
+    got = dict(cuda.run(c, [("idx", Value.of_array(I32, (n,), idx)), ("s", Value.of_array(F64, (n,), v))]))["h"].data
+    cuda.release(c)
+    want = np.bincount(idx, weights=v, minlength=bins)
+    assert np.all(np.abs(got - want) <= 1e-12 * (1 + np.abs(want)))
+
+
 def test_out_of_bounds_scatter_is_reported():
     idx = D.param("idx", I32, (4,))
     c = cuda.compile(Graph("s", [("h", D.scatter_add(idx, D.param("s", I32, (4,)), (4,)))]))
