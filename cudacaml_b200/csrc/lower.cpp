@@ -1632,15 +1632,26 @@ class Lowerer {
   // lane quadrant those loads are latency-bound (measured on the MLP step:
   // dZ1 in the epilogue of the K = 1024 product cost 225 us more than the
   // separate pass).
+  //
+  // The same holds for a scan whose kernel writes through F::store/store4 (row
+  // scans and the 8-byte flat scan): the pass runs on each scanned value as
+  // it is stored (LSM's S = S0 exp(cumulative log-increments)).
   static constexpr int64_t kEpiMinK = 2048;
   void fuse_epilogues() {
     for (int gi = 0; gi + 1 < (int)groups.size(); ++gi) {
       Group& mm = groups[gi];
       Group& ep = groups[gi + 1];
-      if (mm.kind != G_MATMUL_TC || ep.kind != G_MAPRED) continue;
+      if (ep.kind != G_MAPRED) continue;
       const int t = mm.root;
       const int64_t MN = g.ts[t].numel;
-      if (g.ts[g.ts[t].dep0].shape[1] < kEpiMinK) continue;
+      if (mm.kind == G_MATMUL_TC) {
+        if (g.ts[g.ts[t].dep0].shape[1] < kEpiMinK) continue;
+      } else if (mm.kind == G_SCAN_ROWS || mm.kind == G_SCAN_FLAT) {
+        int srcb = -1;
+        if (staged_scan_source(mm, t, srcb)) continue;  // writes its destination directly
+      } else {
+        continue;
+      }
       if (ep.domain != MN || MN >= (1LL << 31) || !ep.reds.empty() || !ep.tails.empty() || ep.stores.empty()) continue;
       bool reads_t = false, ok = true;
       for (const KN& k : ep.ctx.n) {
@@ -1649,7 +1660,7 @@ class Lowerer {
         reads_t = true;
       }
       for (auto& st : ep.stores)
-        if (g.ts[st.first].numel != MN || dt_size(g.ts[st.first].dt) != 4) ok = false;
+        if (g.ts[st.first].numel != MN || (mm.kind == G_MATMUL_TC && dt_size(g.ts[st.first].dt) != 4)) ok = false;
       if (!ok || !reads_t) continue;
       mm.epi = gi + 1;
       ep.fused_into = gi;
@@ -2056,13 +2067,21 @@ class Lowerer {
     const std::string F = "F" + std::to_string(gi);
     const bool flat = gr.kind == G_SCAN_FLAT;
     const std::string fn = std::string(flat ? "ccb_scan_" : "ccb_scanrows_") + std::to_string(gi) + kname_suffix();
-    node_buf[t] = add_buf("t" + std::to_string(x.uid), dt_size(x.dt), x.numel, BR_NODE, t, false);
+    const int ej = gr.epi;
+    const bool store_t = ej < 0 || must_store(gi, ej, t);
+    if (ej >= 0)
+      for (auto& st : groups[ej].stores)
+        node_buf[st.first] = add_buf("t" + std::to_string(g.ts[st.first].uid), dt_size(g.ts[st.first].dt),
+                                     g.ts[st.first].numel, BR_NODE, st.first, false);
+    if (store_t) node_buf[t] = add_buf("t" + std::to_string(x.uid), dt_size(x.dt), x.numel, BR_NODE, t, false);
     const int items = dt_size(x.dt) == 4 ? 16 : 8;
     const int64_t tile = 256 * items;
     const int64_t ntiles = std::max<int64_t>(1, (gr.domain + tile - 1) / tile);
     std::vector<Field> fields;
     for (int b : loads_of(gr.ctx)) fields.push_back(in_field(b));
-    fields.push_back(out_field(t));
+    if (store_t) fields.push_back(out_field(t));
+    if (ej >= 0)
+      for (auto& st : groups[ej].stores) fields.push_back(out_field(st.first));
     fields.push_back(buf_field("unsigned* err", out->err_buf));
     fields.push_back(i64_field("n", flat ? gr.domain : gr.n));
     fields.push_back(i64_field("rows", gr.rows));
@@ -2082,15 +2101,24 @@ class Lowerer {
       ep.slot.kind = SL_EPOCH;
       fields.push_back(ep);
     }
-    src << "// " << (flat ? "flat scan" : "row scan") << " " << gi << " over " << gr.domain << " elements\n";
+    src << "// " << (flat ? "flat scan" : "row scan") << " " << gi << " over " << gr.domain << " elements";
+    if (ej >= 0) src << "; pass " << ej << " in the store" << (store_t ? "" : ", scan not stored");
+    src << "\n";
     src << "struct " << F << " {\n";
     emit_struct(fields);
     src << "  typedef " << T << " T;\n  static constexpr int VEC = 1;\n";
     emit_source_access(gr, t, T);
-    src << " && ccb::aligned16(p.o" << t << ");\n  }\n";
-    src << "  static __device__ __forceinline__ void store(const P& p, long long i, T v) { p.o" << t << "[i] = v; }\n";
-    src << "  static __device__ __forceinline__ void store4(const P& p, long long i, const T* x) {\n"
-        << "    ccb::V4<T> s; s.v[0] = x[0]; s.v[1] = x[1]; s.v[2] = x[2]; s.v[3] = x[3]; ccb::st4(p.o" << t << " + i, s);\n  }\n";
+    if (store_t) src << " && ccb::aligned16(p.o" << t << ")";
+    if (ej >= 0)
+      for (auto& st : groups[ej].stores) src << " && ccb::aligned16(p.o" << st.first << ")";
+    src << ";\n  }\n";
+    if (ej < 0) {
+      src << "  static __device__ __forceinline__ void store(const P& p, long long i, T v) { p.o" << t << "[i] = v; }\n";
+      src << "  static __device__ __forceinline__ void store4(const P& p, long long i, const T* x) {\n"
+          << "    ccb::V4<T> s; s.v[0] = x[0]; s.v[1] = x[1]; s.v[2] = x[2]; s.v[3] = x[3]; ccb::st4(p.o" << t << " + i, s);\n  }\n";
+    } else {
+      emit_fused_store(groups[ej], t, store_t);
+    }
     src << "};\n";
     std::string call;
     if (flat) {
@@ -2110,6 +2138,47 @@ class Lowerer {
       l.work = gr.rows;
       l.per_block = gr.n >= 1024 ? 1 : 8;
     }
+  }
+
+  // With pass ej fused into group gi's stores, gi's own output is written
+  // only when it is a graph output or another group reads it.
+  bool must_store(int gi, int ej, int t) const {
+    if (is_out[t]) return true;
+    for (int q = 0; q < (int)groups.size(); ++q)
+      if (q != gi && q != ej && reads_tensor(q, t)) return true;
+    return false;
+  }
+
+  // store/store4 of a scan that runs the fused pass ep on each value v
+  // (element i of t) as it is stored.
+  void emit_fused_store(const Group& ep, int t, bool store_t) {
+    src << "  static __device__ __forceinline__ void store(const P& p, long long li, T v) {\n    const int i = (int)li;\n";
+    if (store_t) src << "    p.o" << t << "[i] = v;\n";
+    {
+      Emitter e(ep.ctx, src);
+      e.direct[t] = "v";
+      for (auto& st : ep.stores) {
+        std::string val = e.val(st.second);
+        src << "    p.o" << st.first << "[i] = " << val << ";\n";
+      }
+    }
+    src << "  }\n";
+    src << "  static __device__ __forceinline__ void store4(const P& p, long long li, const T* x) {\n    const int i = (int)li;\n";
+    if (store_t)
+      src << "    { ccb::V4<T> s; s.v[0] = x[0]; s.v[1] = x[1]; s.v[2] = x[2]; s.v[3] = x[3]; ccb::st4(p.o" << t << " + i, s); }\n";
+    for (auto& st : ep.stores) src << "    ccb::V4<" << dt_ctype(g.ts[st.first].dt) << "> S" << st.first << ";\n";
+    for (int j = 0; j < 4; ++j) {
+      Emitter e(ep.ctx, src);
+      e.suffix = "_" + std::to_string(j);
+      e.index_text = j == 0 ? "i" : "(i + " + std::to_string(j) + ")";
+      e.direct[t] = "x[" + std::to_string(j) + "]";
+      for (auto& st : ep.stores) {
+        std::string val = e.val(st.second);
+        src << "    S" << st.first << ".v[" << j << "] = " << val << ";\n";
+      }
+    }
+    for (auto& st : ep.stores) src << "    ccb::st4(p.o" << st.first << " + i, S" << st.first << ");\n";
+    src << "  }\n";
   }
 
   void emit_red_rows(int gi) {
@@ -2256,11 +2325,8 @@ class Lowerer {
     // with a fused map pass the product itself is stored only when an output
     // or another pass reads it
     const int ej = gr.epi;
-    bool store_c = true;
+    const bool store_c = ej < 0 || must_store(gi, ej, t);
     if (ej >= 0) {
-      store_c = is_out[t] != 0;
-      for (int q = 0; q < (int)groups.size() && !store_c; ++q)
-        if (q != gi && q != ej && reads_tensor(q, t)) store_c = true;
       for (auto& st : groups[ej].stores)
         node_buf[st.first] = add_buf("t" + std::to_string(g.ts[st.first].uid), 4, g.ts[st.first].numel, BR_NODE, st.first, false);
     }

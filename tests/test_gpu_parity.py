@@ -438,6 +438,38 @@ def test_graph_capture_replays_resident_runs():
     cuda.release(cs)
 
 
+@pytest.mark.parametrize("dt,rows,n", [(F64, 1000, 64), (F32, 300, 4096 + 5), (F64, 1, 100003)],
+                         ids=["rows-warp-f64", "rows-block-f32", "flat-f64"])
+def test_scan_store_fusion_matches_separate(dt, rows, n):
+    # a map over a scan's output, run in the scan's stores, gives the bits of
+    # the separate pass on the stored scan (no multiply feeding an add)
+    shape = (n,) if rows == 1 else (rows, n)
+    x = ((np.arange(rows * n) % 17 - 8) / 64.0).astype(dt.np).reshape(shape)
+    px = D.param("x", dt, shape)
+    scan = (lambda f, i, s: D.scan(f, i, s)) if rows == 1 else (lambda f, i, s: D.scan_rows(f, i, s))
+    c = scan(D.add, D.const(dt, 0.0), px)
+
+    def f(v):
+        return D.mul(D.const(dt, 1.5), D.exp(v))
+
+    def run(graph, ins):
+        cc = cuda.compile(graph)
+        try:
+            return cc.plan(), {k: v.data for k, v in cuda.run(cc, ins)}
+        finally:
+            cuda.release(cc)
+
+    ins = [("x", Value.of_array(dt, shape, x))]
+    _, sc = run(Graph("s", [("c", c)]), ins)
+    pc = D.param("c", dt, shape)
+    _, sep = run(Graph("m", [("y", D.map(f, pc))]), [("c", Value.of_array(dt, shape, sc["c"].reshape(shape)))])
+    plan, fused = run(Graph("fz", [("y", D.map(f, c))]), ins)
+    assert "ccb_mapreduce_" not in plan
+    assert np.array_equal(fused["y"], sep["y"])
+    plan, both = run(Graph("fb", [("y", D.map(f, c)), ("c", c)]), ins)
+    assert np.array_equal(both["c"], sc["c"]) and np.array_equal(both["y"], sep["y"])
+
+
 def test_s5_pool_stable():
     n = 4096
     c = cuda.compile(X.saxpy(n, 2.0))

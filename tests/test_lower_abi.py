@@ -194,3 +194,22 @@ def test_tensor_core_epilogue_fusion():
     assert B.lower_info(Graph("f", [("s", sym)]), matmul="tf32")["launches"] == 2
     short = D.map(lambda v: D.exp(v), D.matmul(D.param("d", F32, (256, 1024)), D.param("e", F32, (1024, 512))))
     assert B.lower_info(Graph("f", [("s", short)]), matmul="tf32")["launches"] == 2
+
+
+def test_scan_store_fusion():
+    from cudacaml_b200 import lsm as L
+    # LSM's S = S0 exp(cumsum): one row-scan launch, the cumulative sums never stored
+    info = B.lower_info(L.paths_graph(1 << 12, 64, L.BASELINE_MARKET))
+    assert info["launches"] == 1 and "pass 1 in the store, scan not stored" in info["source"]
+    x = D.param("x", F64, (1 << 20,))
+    c = D.scan(D.add, D.const(F64, 0.0), x)
+    y = D.map(lambda v: D.exp(v), c)
+    # flat 8-byte scan: fused; the scan kept when it is an output too
+    assert B.lower_info(Graph("f", [("y", y)]))["launches"] == 1
+    info = B.lower_info(Graph("f", [("y", y), ("c", c)]))
+    assert info["launches"] == 1 and "pass 1 in the store\n" in info["source"]
+    # the staged 4-byte flat scan writes its destination directly: apart
+    x32 = D.param("x", F32, (1 << 20,))
+    y32 = D.map(lambda v: D.exp(v), D.scan(D.add, D.const(F32, 0.0), x32))
+    assert B.lower_info(Graph("f", [("y", y32)]))["launches"] == 2
+    assert nvrtc_ok(info["source"], "scanfused") > 0
