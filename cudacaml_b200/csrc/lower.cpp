@@ -806,6 +806,7 @@ struct Emitter {
   std::string suffix;
   std::unordered_map<int, std::string> name;
   std::unordered_map<int, std::string> direct;  // buffer -> lane expression
+  std::unordered_map<int, std::string> direct_node;  // LOAD node -> lane expression
   std::vector<std::string> redval;               // REDVAL slot -> name
   std::string arg_names[2] = {"a", "b"};
 
@@ -852,6 +853,11 @@ struct Emitter {
       case K_ARG: return arg_names[k.iv];
       case K_REDVAL: return redval.at(k.iv);
       case K_LOAD: {
+        auto dn = direct_node.find(id);
+        if (dn != direct_node.end()) {
+          e = dn->second;
+          break;
+        }
         auto d = direct.find(k.buf);
         if (d != direct.end() && k.a == c.index_node) {
           e = d->second;
@@ -1771,6 +1777,54 @@ class Lowerer {
     return std::vector<int>(bufs.begin(), bufs.end());
   }
 
+  // A load at index i + u, u uniform over the pass (scalars and constants:
+  // LSM's row t of a date-major S at t * n_paths + i), is a contiguous
+  // stream. `terms` are u's summands with their signs; u is their wrapping
+  // I32 sum, as the element index itself is computed.
+  struct OffLoad {
+    int id = -1, buf = -1;
+    std::vector<std::pair<int, int>> terms;  // (sign, node)
+  };
+  static int decompose(const KCtx& c, int x, int sign, std::vector<std::pair<int, int>>& terms) {
+    if (x == c.index_node) return sign > 0 ? 1 : -100;
+    const KN& k = c.n[x];
+    if (!k.variant && !k.late) {
+      terms.push_back({sign, x});
+      return 0;
+    }
+    if (k.op == K_BIN && k.dt == DT_I32 && (k.sub == B_ADD || k.sub == B_SUB))
+      return decompose(c, k.a, sign, terms) + decompose(c, k.b, k.sub == B_ADD ? sign : -sign, terms);
+    return -100;
+  }
+  std::vector<OffLoad> offset_loads(const KCtx& c, const std::vector<int>& roots) {
+    std::vector<OffLoad> out;
+    std::vector<char> seen(c.n.size(), 0);
+    std::function<void(int)> walk = [&](int id) {
+      if (id < 0 || seen[id]) return;
+      seen[id] = 1;
+      const KN& k = c.n[id];
+      if (k.op == K_LOAD && k.a != c.index_node && k.dt != DT_BOOL && (dt_size(k.dt) == 4 || dt_size(k.dt) == 8)) {
+        int x = k.a;
+        if (c.n[x].op == K_CHECK) x = c.n[x].a;
+        OffLoad o;
+        o.id = id;
+        o.buf = k.buf;
+        if (c.n[x].dt == DT_I32 && decompose(c, x, 1, o.terms) == 1) out.push_back(o);
+      }
+      walk(k.a);
+      walk(k.b);
+      walk(k.c);
+    };
+    for (int r : roots) walk(r);
+    return out;
+  }
+  // u of an offset load as an int expression (statements emitted by e)
+  static std::string uniform_text(Emitter& e, const OffLoad& o) {
+    std::string u = "0u";
+    for (auto& t : o.terms) u += std::string(t.first > 0 ? " + " : " - ") + "(unsigned)(" + e.val(t.second) + ")";
+    return "((int)(" + u + "))";
+  }
+
   void emit_mapred(int gi) {
     Group& gr = groups[gi];
     const std::string F = "F" + std::to_string(gi);
@@ -1812,10 +1866,11 @@ class Lowerer {
     for (auto& s : gr.stores) roots.push_back(s.second);
     for (auto& r : gr.reds) roots.push_back(r.var);
     std::vector<int> direct = direct_loads(gr.ctx, roots);
+    const std::vector<OffLoad> offs = offset_loads(gr.ctx, roots);
     src << "  static constexpr int NRED = " << R << ";\n  static constexpr int VEC = 1;\n";
     // Passes that stream data keep 4 vector steps in flight; compute-bound
     // passes (Philox Monte Carlo) unroll 2 to keep the body small.
-    src << "  static constexpr int UNROLL = " << (direct.empty() ? 2 : 4) << ";\n";
+    src << "  static constexpr int UNROLL = " << (direct.empty() && offs.empty() ? 2 : 4) << ";\n";
     src << "  static constexpr bool TAIL = " << (gr.tails.empty() ? "false" : "true") << ";\n";
     // identity / combine
     src << "  static __device__ __forceinline__ acc_t identity(int r) {\n    switch (r) {\n";
@@ -1839,11 +1894,19 @@ class Lowerer {
       }
     }
     src << "    }\n    return a;\n  }\n";
-    // vec_ok
-    src << "  static __device__ __forceinline__ bool vec_ok(const P& p) {\n    return true";
+    // vec_ok: aligned streams; each offset stream inside its buffer and aligned
+    src << "  static __device__ __forceinline__ bool vec_ok(const P& p) {\n    bool ok = true";
     for (int b : direct) src << " && ccb::aligned16(p.b" << b << ")";
     for (auto& s : gr.stores) src << " && ccb::aligned16(p.o" << s.first << ")";
-    src << ";\n  }\n";
+    src << ";\n";
+    for (size_t q = 0; q < offs.size(); ++q) {
+      Emitter e(gr.ctx, src);
+      e.suffix = "_k" + std::to_string(q);
+      const std::string u = uniform_text(e, offs[q]);
+      src << "    { const long long u = " << u << "; ok = ok && u >= 0 && u + p.n <= " << g.ts[offs[q].buf].numel
+          << "LL && ccb::aligned16(p.b" << offs[q].buf << " + u); }\n";
+    }
+    src << "    return ok;\n  }\n";
     // Reductions of one value with one combiner from one identity (the two
     // halves of a symmetric X^T X, say) are accumulated once.
     std::vector<int> alias(R, -1);
@@ -1872,12 +1935,20 @@ class Lowerer {
     // elem4
     src << "  static __device__ __forceinline__ void elem4(const P& p, int i, acc_t* acc) {\n";
     for (int b : direct) src << "    const ccb::V4<" << dt_ctype(g.ts[b].dt) << "> L" << b << " = ccb::ld4(p.b" << b << " + i);\n";
+    for (size_t q = 0; q < offs.size(); ++q) {  // in range and aligned: vec_ok checked
+      Emitter e(gr.ctx, src);
+      e.suffix = "_k" + std::to_string(q);
+      const std::string u = uniform_text(e, offs[q]);
+      src << "    const ccb::V4<" << dt_ctype(g.ts[offs[q].buf].dt) << "> K" << q << " = ccb::ld4(p.b" << offs[q].buf
+          << " + " << u << " + i);\n";
+    }
     for (auto& s : gr.stores) src << "    ccb::V4<" << dt_ctype(g.ts[s.first].dt) << "> S" << s.first << ";\n";
     for (int j = 0; j < 4; ++j) {
       Emitter e(gr.ctx, src);
       e.suffix = "_" + std::to_string(j);
       e.index_text = j == 0 ? "i" : "(i + " + std::to_string(j) + ")";
       for (int b : direct) e.direct[b] = "L" + std::to_string(b) + ".v[" + std::to_string(j) + "]";
+      for (size_t q = 0; q < offs.size(); ++q) e.direct_node[offs[q].id] = "K" + std::to_string(q) + ".v[" + std::to_string(j) + "]";
       for (auto& s : gr.stores) {
         std::string v = e.val(s.second);
         src << "    S" << s.first << ".v[" << j << "] = " << v << ";\n";

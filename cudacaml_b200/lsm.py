@@ -102,22 +102,26 @@ def paths_graph(n_paths: int, n_steps: int, m: Market = MARKET) -> Graph:
     return Graph("lsm_paths", [("S", s)])
 
 
-def _basis(n_paths, n_steps, strike, basis, layout="paths"):
+def _basis(n_paths, n_steps, strike, basis, layout="paths", cf=None, tb=None, s=None):
     """Column t of S, the in-the-money mask and the masked design matrix
     (lsm.ml:170-192). ``layout="paths"`` reads S as the reference stores it,
     [n_paths; n_steps]; ``layout="dates"`` reads its transpose [n_steps;
-    n_paths], where date t is one contiguous row."""
+    n_paths], where date t is one contiguous row. The cash flow `cf`, the
+    per-path date `tb` and `S` default to the params "cf", "t" (broadcast)
+    and "S"."""
     nb = _nb(basis)
     gb = (n_paths, nb)
     kf = lambda v: D.const(F64, v)  # noqa: E731
     ki = lambda v: D.const(I32, v)  # noqa: E731
-    cf = D.param("cf", F64, (n_paths,))
-    tb = D.broadcast((n_paths,), D.scalar("t", I32))
+    if cf is None:
+        cf = D.param("cf", F64, (n_paths,))
+    if tb is None:
+        tb = D.broadcast((n_paths,), D.scalar("t", I32))
     if layout == "paths":
-        s = D.param("S", F64, (n_paths, n_steps))
+        s = s if s is not None else D.param("S", F64, (n_paths, n_steps))
         idx = D.map2(lambda p, tv: D.add(D.mul(p, ki(n_steps)), tv), D.iota((n_paths,)), tb)
     else:
-        s = D.param("S", F64, (n_steps, n_paths))
+        s = s if s is not None else D.param("S", F64, (n_steps, n_paths))
         idx = D.map2(lambda p, tv: D.add(D.mul(tv, ki(n_paths)), p), D.iota((n_paths,)), tb)
     st = D.gather(idx, s)
     itm = D.map(lambda x: D.select(D.lt(x, kf(strike)), kf(1.0), kf(0.0)), st)
@@ -138,22 +142,20 @@ def _basis(n_paths, n_steps, strike, basis, layout="paths"):
     return cf, st, itm, D.map2(D.mul, ph, itm3)
 
 
-def regress_graph(n_paths, n_steps, strike, disc, basis="scaled3", layout="paths") -> Graph:
-    """lsm.ml:201-212."""
-    cf, st, itm, xm = _basis(n_paths, n_steps, strike, basis, layout)
+def _regress(n_paths, n_steps, strike, disc, basis, layout, **kw):
+    """lsm.ml:201-212: the normal equations X^T X and X^T y of one date."""
+    cf, st, itm, xm = _basis(n_paths, n_steps, strike, basis, layout, **kw)
     kf = lambda v: D.const(F64, v)  # noqa: E731
     y = D.map2(lambda c, mk: D.mul(D.mul(kf(disc), c), mk), cf, itm)
     xt = D.transpose(xm)
-    return Graph("lsm_regress", [("xtx", D.matmul(xt, xm)), ("xty", D.matmul(xt, D.reshape((n_paths, 1), y)))])
+    return D.matmul(xt, xm), D.matmul(xt, D.reshape((n_paths, 1), y))
 
 
-def update_graph(n_paths, n_steps, strike, disc, basis="scaled3", layout="paths") -> Graph:
+def _update(n_paths, n_steps, strike, disc, basis, layout, beta, **kw):
     """lsm.ml:219-234: exercise where intrinsic beats the fitted continuation;
     otherwise keep the realised cash flow, discounted."""
-    nb = _nb(basis)
-    cf, st, itm, xm = _basis(n_paths, n_steps, strike, basis, layout)
+    cf, st, itm, xm = _basis(n_paths, n_steps, strike, basis, layout, **kw)
     kf = lambda v: D.const(F64, v)  # noqa: E731
-    beta = D.param("beta", F64, (nb, 1))
     cont = D.reshape((n_paths,), D.matmul(xm, beta))
 
     def exercises(s, c):
@@ -163,7 +165,34 @@ def update_graph(n_paths, n_steps, strike, disc, basis="scaled3", layout="paths"
     exv = D.map2(lambda s, c: D.select(exercises(s, c), D.sub(kf(strike), s), kf(0.0)), st, cont)
     keep = D.map2(lambda s, c: D.select(exercises(s, c), kf(0.0), kf(1.0)), st, cont)
     held = D.map2(lambda k, c: D.mul(k, D.mul(kf(disc), c)), keep, cf)
-    return Graph("lsm_update", [("cf", D.map2(D.add, exv, held))])
+    return D.map2(D.add, exv, held)
+
+
+def regress_graph(n_paths, n_steps, strike, disc, basis="scaled3", layout="paths") -> Graph:
+    """lsm.ml:201-212."""
+    xtx, xty = _regress(n_paths, n_steps, strike, disc, basis, layout)
+    return Graph("lsm_regress", [("xtx", xtx), ("xty", xty)])
+
+
+def update_graph(n_paths, n_steps, strike, disc, basis="scaled3", layout="paths") -> Graph:
+    """lsm.ml:219-234."""
+    beta = D.param("beta", F64, (_nb(basis), 1))
+    return Graph("lsm_update", [("cf", _update(n_paths, n_steps, strike, disc, basis, layout, beta))])
+
+
+def update_regress_graph(n_paths, n_steps, strike, disc, basis="scaled3", layout="dates") -> Graph:
+    """Date t's update (lsm.ml:219-234) followed by date t-1's normal
+    equations (lsm.ml:201-212) on the updated cash flow: the backward loop's
+    update and next regression, which the lowering turns into one pass over
+    the paths (S rows t and t-1, the cash flow read once and written once).
+    The values are those of the two graphs run in turn."""
+    beta = D.param("beta", F64, (_nb(basis), 1))
+    s = D.param("S", F64, (n_steps, n_paths) if layout == "dates" else (n_paths, n_steps))
+    tb = D.broadcast((n_paths,), D.scalar("t", I32))
+    cf = _update(n_paths, n_steps, strike, disc, basis, layout, beta, tb=tb, s=s)
+    tprev = D.map(lambda v: D.sub(v, D.const(I32, 1)), tb)
+    xtx, xty = _regress(n_paths, n_steps, strike, disc, basis, layout, cf=cf, tb=tprev, s=s)
+    return Graph("lsm_update_regress", [("cf", cf), ("xtx", xtx), ("xty", xty)])
 
 
 def solve_graph(nb: int) -> Graph:
@@ -321,6 +350,7 @@ class CudaResident:
         self.dates = cuda.compile_on(device, _dates_graph(n_paths, n_steps))
         self.regress = cuda.compile_on(device, regress_graph(n_paths, n_steps, self.strike, self.disc, basis, "dates"))
         self.update = cuda.compile_on(device, update_graph(n_paths, n_steps, self.strike, self.disc, basis, "dates"))
+        self.upd_reg = cuda.compile_on(device, update_regress_graph(n_paths, n_steps, self.strike, self.disc, basis, "dates"))
         self.final = cuda.compile_on(device, _final_graph(n_paths, n_steps, self.strike))
         self.solve = cuda.compile_on(device, solve_graph(self.nb))
         cfp = D.param("cf", F64, (n_paths,))
@@ -354,20 +384,38 @@ class CudaResident:
         xty = np.empty(nb)
         beta_outs = [b["beta"].ptr + 8 * j for j in range(nb)]
         cur, nxt = b["cf_a"], b["cf_b"]
-        for step in range(ns - 2, -1, -1):
-            t_ptr = b["t"].ptr + 4 * step
-            outs = {"xtx": b["xtx"].ptr, "xty": b["xty"].ptr}
-            cuda.run_device_ptrs(self.regress, bind(self.regress, S=b["ST"].ptr, cf=cur.ptr, t=t_ptr),
-                                 [outs[name] for name, _, _ in self.regress.outputs], stream)
+        outs = {"xtx": b["xtx"].ptr, "xty": b["xty"].ptr}
+
+        def normal_equations(step, prog):
             if trace is not None:
                 R.check(R.lib().ccb_memcpy_d2h(xtx.ctypes.data, b["xtx"].ptr, xtx.nbytes, stream))
                 R.check(R.lib().ccb_memcpy_d2h(xty.ctypes.data, b["xty"].ptr, xty.nbytes, stream))
-                cuda.check_device(self.regress, stream)
+                cuda.check_device(prog, stream)
                 trace.append((step, xtx.copy(), xty.copy()))
             cuda.run_device_ptrs(self.solve, bind(self.solve, xtx=b["xtx"].ptr, xty=b["xty"].ptr),
                                  [beta_outs[int(name[1:])] for name, _, _ in self.solve.outputs], stream)
-            cuda.run_device_ptrs(self.update, bind(self.update, S=b["ST"].ptr, cf=cur.ptr, t=t_ptr, beta=b["beta"].ptr),
-                                 [nxt.ptr], stream)
+
+        # Dates ns-2 .. 0 backwards. The first date's normal equations come
+        # from the regression alone; after that each pass updates date t's
+        # cash flow and sums date t-1's normal equations from it, and the
+        # last date (0) is an update alone.
+        steps = list(range(ns - 2, -1, -1))
+        if steps:
+            t0 = b["t"].ptr + 4 * steps[0]
+            cuda.run_device_ptrs(self.regress, bind(self.regress, S=b["ST"].ptr, cf=cur.ptr, t=t0),
+                                 [outs[name] for name, _, _ in self.regress.outputs], stream)
+            normal_equations(steps[0], self.regress)
+        for k, step in enumerate(steps):
+            t_ptr = b["t"].ptr + 4 * step
+            if k + 1 < len(steps):
+                ur = self.upd_reg
+                dst = {"cf": nxt.ptr, **outs}
+                cuda.run_device_ptrs(ur, bind(ur, S=b["ST"].ptr, cf=cur.ptr, t=t_ptr, beta=b["beta"].ptr),
+                                     [dst[name] for name, _, _ in ur.outputs], stream)
+                normal_equations(step - 1, ur)
+            else:
+                cuda.run_device_ptrs(self.update, bind(self.update, S=b["ST"].ptr, cf=cur.ptr, t=t_ptr, beta=b["beta"].ptr),
+                                     [nxt.ptr], stream)
             cur, nxt = nxt, cur
         # the mean of the discounted cash flows (lsm.ml:303-305): summed on the device
         cuda.run_device_ptrs(self.total, [cur.ptr], [b["sum"].ptr], stream)
@@ -382,7 +430,7 @@ class CudaResident:
         cuda, R = self.cuda, self.R
         b = self.bufs
         stream = self.regress.lane_stream(0)
-        progs = (self.paths, self.dates, self.final, self.regress, self.solve, self.update, self.total)
+        progs = (self.paths, self.dates, self.final, self.regress, self.solve, self.update, self.upd_reg, self.total)
         with R.with_device(self.device):
             seed_h = np.array([seed], np.int32)
             R.check(R.lib().ccb_memcpy_h2d(b["seed"].ptr, seed_h.ctypes.data, 4, stream))
@@ -408,7 +456,7 @@ class CudaResident:
             for buf in self.bufs.values():
                 buf.free()
         self.bufs = {}
-        for c in (self.paths, self.dates, self.regress, self.update, self.final, self.solve, self.total):
+        for c in (self.paths, self.dates, self.regress, self.update, self.upd_reg, self.final, self.solve, self.total):
             self.cuda.release(c)
 
 

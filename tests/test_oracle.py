@@ -252,3 +252,30 @@ def test_lsm_solve_graph_matches_host_solve():
         out = dict(I.run(I.compile(g), [("xtx", Value.of_array(F64, (16,), xtx.ravel())),
                                                   ("xty", Value.of_array(F64, (4,), xty))]))
         assert [float(out[f"b{i}"].data[0]) for i in range(4)] == want
+
+
+def test_lsm_update_regress_graph_is_update_then_regress():
+    # the resident driver's fused pass (update date t, normal equations of
+    # date t-1 on the updated cash flow) against the two graphs run in turn,
+    # on the oracle, bit for bit, both bases
+    from cudacaml_b200 import lsm as L
+    from cudacaml_b200.ir import F64, I32, Value
+    n, ns, t = 512, 8, 5
+    rng = np.random.default_rng(4)
+    for basis, m in (("poly4", L.BASELINE_MARKET), ("scaled3", L.MARKET)):
+        nb = L._nb(basis)
+        disc = 0.99
+        st = m.strike * np.exp(0.2 * rng.standard_normal((ns, n)))
+        cf = np.maximum(m.strike - st[-1], 0.0)
+        beta = rng.standard_normal((nb, 1))
+        common = [("S", Value.of_array(F64, (ns, n), st)), ("cf", Value.of_array(F64, (n,), cf)),
+                  ("beta", Value.of_array(F64, (nb, 1), beta))]
+        fused = dict(I.run(I.compile(L.update_regress_graph(n, ns, m.strike, disc, basis)),
+                           common + [("t", Value.of_list(I32, (), [t]))]))
+        upd = dict(I.run(I.compile(L.update_graph(n, ns, m.strike, disc, basis, "dates")),
+                         common + [("t", Value.of_list(I32, (), [t]))]))
+        reg = dict(I.run(I.compile(L.regress_graph(n, ns, m.strike, disc, basis, "dates")),
+                         [common[0], ("cf", upd["cf"]), ("t", Value.of_list(I32, (), [t - 1]))]))
+        assert np.array_equal(fused["cf"].data, upd["cf"].data)
+        assert np.array_equal(fused["xtx"].data, reg["xtx"].data)
+        assert np.array_equal(fused["xty"].data, reg["xty"].data)
