@@ -285,5 +285,13 @@ def run_device_ptrs(c: Compiled, in_ptrs, out_ptrs, stream=None, lane: int = 0) 
     R.check(R.lib().ccb_program_run_device(c.h, lane, _ptr_array(in_ptrs), _ptr_array(out_ptrs), stream))
 
 
+def run_device_ptrs_events(c: Compiled, in_ptrs, out_ptrs, events, stream=None, lane: int = 0) -> None:
+    """run_device_ptrs, recording events[j] (an R.Event or None) on `stream`
+    as soon as output j is final, so that another stream can wait on it."""
+    hs = [e.h if e is not None else None for e in events]
+    R.check(R.lib().ccb_program_run_device_events(c.h, lane, _ptr_array(in_ptrs), _ptr_array(out_ptrs), stream,
+                                                  _ptr_array(hs)))
+
+
 def check_device(c: Compiled, stream=None, lane: int = 0) -> None:
     R.check(R.lib().ccb_program_check(c.h, lane, stream))

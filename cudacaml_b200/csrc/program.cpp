@@ -125,7 +125,7 @@ int tensor_map(Lane& ln, int64_t key, const Slot& sl, CUdeviceptr base, const CU
 // Issue one run on `stream`: uploads (host runs), zero fills and launches,
 // downloads (host runs) and the error-word readback.
 int issue(Program& P, int lane, const void* const* h_in, void* const* h_out, const void* const* d_in, void* const* d_out,
-          CUstream stream) {
+          CUstream stream, CUevent const* out_events = nullptr) {
   const Driver& d = driver();
   Lane& ln = P.lanes[lane];
   std::vector<CUdeviceptr> ptr = ln.bufs;
@@ -167,11 +167,41 @@ int issue(Program& P, int lane, const void* const* h_in, void* const* h_out, con
         if (sl.kind == SL_EPOCH)
           return fail(CCB_ERR_INVALID, "graph capture: " + l.fn + " (a flat scan) cannot be replayed from a graph");
   ln.epoch = ln.epoch % ((1u << 30) - 2) + 1;
+  // output j's event goes right after the last op that references its
+  // buffer (no later op touches it); outputs copied out after the launches
+  // get theirs after the copies
+  std::vector<std::vector<int>> ev_at(P.L.ops.size());
+  std::vector<int> ev_end;
+  if (out_events) {
+    for (size_t j = 0; j < P.L.outputs.size(); ++j) {
+      if (!out_events[j]) continue;
+      const int b = P.L.outputs[j].buf;
+      bool copied = false;
+      for (auto& c : copies)
+        if (c.second == b && c.first == (CUdeviceptr)(d_out ? d_out[j] : nullptr)) copied = true;
+      int last = -1;
+      for (size_t o = 0; o < P.L.ops.size(); ++o) {
+        const OpSpec& op = P.L.ops[o];
+        if (op.kind == OP_ZERO) {
+          if (op.buf == b) last = (int)o;
+          continue;
+        }
+        for (const Slot& sl : P.L.launches[op.launch].slots)
+          if ((sl.kind == SL_BUF || sl.kind == SL_TMAP) && sl.buf == b) last = (int)o;
+      }
+      if (copied || last < 0)
+        ev_end.push_back((int)j);
+      else
+        ev_at[last].push_back((int)j);
+    }
+  }
   std::vector<uint64_t> blk;
-  for (const OpSpec& op : P.L.ops) {
+  for (size_t oi = 0; oi < P.L.ops.size(); ++oi) {
+    const OpSpec& op = P.L.ops[oi];
     if (op.kind == OP_ZERO) {
       const int64_t n = buf_bytes(P.L.bufs[op.buf]);
       if (n) CCB_CU(d.cuMemsetD8Async(ptr[op.buf], 0, n, stream));
+      for (int j : ev_at[oi]) CCB_CU(d.cuEventRecord(out_events[j], stream));
       continue;
     }
     const LaunchSpec& l = P.L.launches[op.launch];
@@ -191,11 +221,13 @@ int issue(Program& P, int lane, const void* const* h_in, void* const* h_out, con
     void* args[] = {blk.data()};
     CCB_CU(d.cuLaunchKernel(P.fns[op.launch], P.gx[op.launch], P.gy[op.launch], 1, l.block, 1, 1, (unsigned)l.smem, stream,
                             args, nullptr));
+    for (int j : ev_at[oi]) CCB_CU(d.cuEventRecord(out_events[j], stream));
   }
   for (auto& c : copies) {
     const int64_t n = buf_bytes(P.L.bufs[c.second]);
     if (n) CCB_CU(d.cuMemcpyDtoDAsync(c.first, ptr[c.second], n, stream));
   }
+  for (int j : ev_end) CCB_CU(d.cuEventRecord(out_events[j], stream));
   if (h_out) {
     for (size_t j = 0; j < P.L.outputs.size(); ++j) {
       const IOSpec& o = P.L.outputs[j];
@@ -456,6 +488,17 @@ int ccb_program_run_device(ccb_program_t prog, int lane, const void* const* inpu
   if (!P->L.params.empty() && !inputs) return fail(CCB_ERR_INVALID, "run_device: inputs required");
   if (!outputs) return fail(CCB_ERR_INVALID, "run_device: outputs required");
   return issue(*P, lane, nullptr, nullptr, inputs, outputs, stream ? (CUstream)stream : P->lanes[lane].stream);
+}
+
+int ccb_program_run_device_events(ccb_program_t prog, int lane, const void* const* inputs, void* const* outputs,
+                                  ccb_stream_t stream, ccb_event_t const* output_events) {
+  Program* P = as_prog(prog);
+  CCB_TRY(need_device(P));
+  CCB_TRY(check_lane(P, lane));
+  if (!P->L.params.empty() && !inputs) return fail(CCB_ERR_INVALID, "run_device: inputs required");
+  if (!outputs) return fail(CCB_ERR_INVALID, "run_device: outputs required");
+  return issue(*P, lane, nullptr, nullptr, inputs, outputs, stream ? (CUstream)stream : P->lanes[lane].stream,
+               reinterpret_cast<CUevent const*>(output_events));
 }
 
 int ccb_program_check(ccb_program_t prog, int lane, ccb_stream_t stream) {

@@ -103,6 +103,7 @@ def _declare(L):
         "ccb_program_run": (I, [P, c.POINTER(P), c.POINTER(P)]),
         "ccb_program_run_device": (I, [P, I, c.POINTER(P), c.POINTER(P), P]),
         "ccb_program_check": (I, [P, I, P]),
+        "ccb_program_run_device_events": (I, [P, I, c.POINTER(P), c.POINTER(P), P, c.POINTER(P)]),
         "ccb_program_lane_stream": (I, [P, I, c.POINTER(P)]),
         "ccb_comm_init_all": (I, [I, c.POINTER(I), c.POINTER(P)]),
         "ccb_comm_unique_id": (I, [c.POINTER(c.c_ubyte)]),

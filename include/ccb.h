@@ -153,6 +153,14 @@ int ccb_program_run(ccb_program_t prog, const void* const* inputs, void* const* 
  * raised anywhere in the chain. */
 int ccb_program_run_device(ccb_program_t prog, int lane, const void* const* inputs,
                            void* const* outputs, ccb_stream_t stream);
+/* As ccb_program_run_device, and for each output j whose output_events[j] is
+ * not NULL, records that event on `stream` as soon as output j is final (after
+ * the last kernel that touches its buffer), so another stream can start on it
+ * (an all-reduce of one gradient while the next one is computed). No
+ * counterpart in the reference. */
+int ccb_program_run_device_events(ccb_program_t prog, int lane, const void* const* inputs,
+                                  void* const* outputs, ccb_stream_t stream,
+                                  ccb_event_t const* output_events);
 int ccb_program_check(ccb_program_t prog, int lane, ccb_stream_t stream);
 /* Kernel launches per run (for the bench's gpu_launches count). */
 int ccb_program_lane_stream(ccb_program_t prog, int lane, ccb_stream_t* stream);

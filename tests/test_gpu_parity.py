@@ -470,6 +470,43 @@ def test_scan_store_fusion_matches_separate(dt, rows, n):
     assert np.array_equal(both["c"], sc["c"]) and np.array_equal(both["y"], sep["y"])
 
 
+def test_output_events_order_a_second_stream():
+    # each output's event fires once the output is final: a second stream
+    # that waits on it and copies the output sees the final values, for an
+    # output of the first pass (a reduction) and one of the last (a scan);
+    # all partial sums below 2^24, so exact in F32
+    n = 1 << 20
+    x = D.param("x", F32, (n,))
+    g = Graph("ev", [("s", D.reduce(D.add, D.const(F32, 0.0), x)),
+                     ("p", D.scan(D.add, D.const(F32, 0.0), D.map(lambda v: D.mul(v, D.const(F32, 2.0)), x)))])
+    c = cuda.compile(g)
+    st = c.lane_stream(0)
+    other = R.Stream()
+    xv = (np.arange(n) % 7).astype(np.float32)
+    xb = R.Buffer(4 * n)
+    xb.upload(xv)
+    names = [nm for nm, _, _ in c.outputs]
+    outs = {"s": R.Buffer(4), "p": R.Buffer(4 * n)}
+    copies = {"s": R.Buffer(4), "p": R.Buffer(4 * n)}
+    evs = [R.Event() for _ in names]
+    for _ in range(3):
+        cuda.run_device_ptrs_events(c, [xb.ptr], [outs[nm].ptr for nm in names], evs, st)
+        for j, nm in enumerate(names):
+            R.check(R.lib().ccb_stream_wait_event(other.h, evs[j].h))
+            R.check(R.lib().ccb_memcpy_d2d(copies[nm].ptr, outs[nm].ptr, outs[nm].nbytes, other.h))
+        other.synchronize()
+        cuda.check_device(c, st)
+        got_s, got_p = np.empty(1, np.float32), np.empty(n, np.float32)
+        copies["s"].download(got_s)
+        copies["p"].download(got_p)
+        assert got_s[0] == float(xv.astype(np.float64).sum())
+        assert np.array_equal(got_p, np.cumsum(2 * xv.astype(np.float64)).astype(np.float32))
+    for b_ in list(outs.values()) + list(copies.values()) + [xb]:
+        b_.free()
+    other.destroy()
+    cuda.release(c)
+
+
 def test_s5_pool_stable():
     n = 4096
     c = cuda.compile(X.saxpy(n, 2.0))
