@@ -828,6 +828,47 @@ __device__ __forceinline__ void scan_rows_warp(const typename F::P& p) {
   }
 }
 
+// Row scan whose result is only needed transposed (LSM's S, read date by
+// date): a block owns 32 consecutive rows, warp w scans rows w, w+8, w+16,
+// w+24 in 32-column chunks, each chunk's values (through F::value, the fused
+// store pass if any) go to a shared 32 x 33 tile, and the block writes the
+// chunk's 32 columns as rows of the [n; rows] output, 32 consecutive rows of
+// 4 or 8 bytes each. F provides T, U (output element), identity, combine,
+// load(p, i), value(p, i, v), tout(p); P provides n (row length), rows.
+template <class F>
+__device__ __forceinline__ void scan_rows_warp_t(const typename F::P& p) {
+  typedef typename F::T T;
+  typedef typename F::U U;
+  __shared__ U tile[32][33];
+  const long long n = p.n, rows = p.rows;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  U* out = F::tout(p);
+  for (long long row0 = (long long)blockIdx.x * 32; row0 < rows; row0 += (long long)gridDim.x * 32) {
+    T carry[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) carry[q] = F::identity();
+    for (long long c0 = 0; c0 < n; c0 += 32) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int r = warp + 8 * q;
+        const long long row = row0 + r, j = c0 + lane;
+        const bool in = row < rows && j < n;
+        const T x = in ? F::load(p, row * n + j) : F::identity();
+        const T v = F::combine(carry[q], warp_scan_incl<F>(x, lane));
+        if (in) tile[lane][r] = F::value(p, row * n + j, v);
+        carry[q] = __shfl_sync(FULL, v, 31);
+      }
+      __syncthreads();
+      for (int e = threadIdx.x; e < 32 * 32; e += blockDim.x) {
+        const int c = e >> 5, r = e & 31;
+        const long long row = row0 + r, col = c0 + c;
+        if (row < rows && col < n) out[col * rows + row] = tile[c][r];
+      }
+      __syncthreads();
+    }
+  }
+}
+
 // ---------------------------------------------------------------- scatter_add
 // out is zero-filled by the executor (a memset) before this runs; every
 // element lands through an atomic add. F provides T, idx(p,i), val(p,i);

@@ -921,8 +921,11 @@ struct Group {
   int64_t rows = 0, n = 0;  // rows kernels
   int mm_a = -1, mm_b = -1; // matmul operand KNodes (built with INDEX = flat operand index)
   KCtx ctx_b;               // matmul: B operand
-  int epi = -1;             // tensor-core product: the map pass run in its epilogue
-  int fused_into = -1;      // map pass: the product whose epilogue runs it
+  int epi = -1;             // tensor-core product or scan: the map pass run in its stores
+  int fused_into = -1;      // map pass / transpose: the group that runs it
+  int tstore = -1;          // row scan: the transpose group whose output it writes directly
+  int tpost = -1;           // row scan with tstore: the map pass over the transpose it also runs
+  int tload = -1;           // row scan whose tstore is a map pass over the inlined transpose: its LOAD node
 };
 
 struct JoinFail {};
@@ -1673,6 +1676,94 @@ class Lowerer {
     }
   }
 
+  // A short-row scan (warp per row) whose result (after its fused store
+  // pass, if any) is read by nothing but a transpose writes the transpose
+  // itself, through a shared-memory tile (scan_rows_warp_t): the [rows; n]
+  // result is never stored.
+  bool expr_uses_index(int e) const {
+    if (e < 0) return false;
+    const GExpr& x = g.ex[e];
+    return x.kind == E_INDEX || expr_uses_index(x.a) || expr_uses_index(x.b) || expr_uses_index(x.c);
+  }
+  // The next pass's single store is map(f, transpose(t)) with the transpose
+  // inlined as a gather of t read nowhere else, and f blind to the index:
+  // the LOAD node of t in that pass, else -1.
+  int transposed_map_load(int gm, int t) const {
+    if (gm >= (int)groups.size() || groups[gm].kind != G_MAPRED) return -1;
+    const Group& mp = groups[gm];
+    if (!mp.reds.empty() || !mp.tails.empty() || mp.stores.size() != 1) return -1;
+    const GTensor& y = g.ts[mp.stores[0].first];
+    int src = -1;
+    if (y.kind != T_MAP || expr_uses_index(y.body) || mat[y.dep0] || uses[y.dep0] != 1 || !transpose_of(y.dep0, src) ||
+        src != t)
+      return -1;
+    int load = -1;
+    for (int k = 0; k < (int)mp.ctx.n.size(); ++k) {
+      if (mp.ctx.n[k].op != K_LOAD) continue;
+      if (mp.ctx.n[k].buf != t || load >= 0) return -1;
+      load = k;
+    }
+    return load;
+  }
+
+  void fuse_transposed_stores() {
+    for (int gi = 0; gi < (int)groups.size(); ++gi) {
+      Group& sc = groups[gi];
+      if (sc.kind != G_SCAN_ROWS || sc.n >= 1024 || sc.rows < 32) continue;
+      const int t = sc.root;
+      if (sc.epi < 0 && !is_out[t]) {  // the transpose inlined into the next pass
+        const int ld = transposed_map_load(gi + 1, t);
+        int readers = 0;
+        for (int q = 0; q < (int)groups.size(); ++q)
+          if (q != gi && reads_tensor(q, t)) ++readers;
+        if (ld >= 0 && readers == 1) {
+          sc.tstore = gi + 1;
+          sc.tload = ld;
+          groups[gi + 1].fused_into = gi;
+          continue;
+        }
+      }
+      int u = t;
+      if (sc.epi >= 0) {
+        const Group& ep = groups[sc.epi];
+        if (ep.stores.size() != 1 || must_store(gi, sc.epi, t)) continue;
+        u = ep.stores[0].first;
+      }
+      if (is_out[u]) continue;
+      int gt = -1, readers = 0;
+      for (int q = 0; q < (int)groups.size(); ++q) {
+        if (q == gi || q == sc.epi || !reads_tensor(q, u)) continue;
+        ++readers;
+        if (groups[q].kind == G_TRANSPOSE && groups[q].val == u) gt = q;
+      }
+      if (gt < 0 || readers != 1) continue;
+      sc.tstore = gt;
+      groups[gt].fused_into = gi;
+      // A map pass right after the transpose that reads only the transposed
+      // value at its own element and uses the index for nothing else runs
+      // on each value too (LSM: S = S0 exp(.) of the transposed sums).
+      const int tt = groups[gt].root;
+      const int gm = gt + 1;
+      if (gm < (int)groups.size() && groups[gm].kind == G_MAPRED && !is_out[tt]) {
+        const Group& mp = groups[gm];
+        bool ok = mp.domain == g.ts[tt].numel && mp.reds.empty() && mp.tails.empty() && mp.stores.size() == 1 &&
+                  g.ts[mp.stores[0].first].numel == g.ts[tt].numel;
+        for (const KN& k : mp.ctx.n) {
+          const bool uses_index = k.a == mp.ctx.index_node || k.b == mp.ctx.index_node || k.c == mp.ctx.index_node;
+          if (k.op == K_LOAD && !(k.buf == tt && k.a == mp.ctx.index_node)) ok = false;
+          if (uses_index && k.op != K_LOAD) ok = false;
+        }
+        int others = 0;
+        for (int q = 0; q < (int)groups.size(); ++q)
+          if (q != gm && q != gt && q != gi && reads_tensor(q, tt)) ++others;
+        if (ok && others == 0) {
+          sc.tpost = gm;
+          groups[gm].fused_into = gi;
+        }
+      }
+    }
+  }
+
   // ------------------------------------------------------------ code generation
   Lowered* out = nullptr;
   std::ostringstream src;
@@ -2139,11 +2230,18 @@ class Lowerer {
     const bool flat = gr.kind == G_SCAN_FLAT;
     const std::string fn = std::string(flat ? "ccb_scan_" : "ccb_scanrows_") + std::to_string(gi) + kname_suffix();
     const int ej = gr.epi;
-    const bool store_t = ej < 0 || must_store(gi, ej, t);
-    if (ej >= 0)
+    // the transposed tensor this scan writes: the transpose itself, or the
+    // map pass over it that runs in the same stores
+    const int tt = gr.tstore < 0 ? -1
+                   : gr.tload >= 0 ? groups[gr.tstore].stores[0].first
+                   : gr.tpost >= 0 ? groups[gr.tpost].stores[0].first
+                                   : groups[gr.tstore].root;
+    const bool store_t = tt < 0 && (ej < 0 || must_store(gi, ej, t));
+    if (ej >= 0 && tt < 0)
       for (auto& st : groups[ej].stores)
         node_buf[st.first] = add_buf("t" + std::to_string(g.ts[st.first].uid), dt_size(g.ts[st.first].dt),
                                      g.ts[st.first].numel, BR_NODE, st.first, false);
+    if (tt >= 0) node_buf[tt] = add_buf("t" + std::to_string(g.ts[tt].uid), dt_size(g.ts[tt].dt), g.ts[tt].numel, BR_NODE, tt, false);
     if (store_t) node_buf[t] = add_buf("t" + std::to_string(x.uid), dt_size(x.dt), x.numel, BR_NODE, t, false);
     const int items = dt_size(x.dt) == 4 ? 16 : 8;
     const int64_t tile = 256 * items;
@@ -2151,8 +2249,9 @@ class Lowerer {
     std::vector<Field> fields;
     for (int b : loads_of(gr.ctx)) fields.push_back(in_field(b));
     if (store_t) fields.push_back(out_field(t));
-    if (ej >= 0)
+    if (ej >= 0 && tt < 0)
       for (auto& st : groups[ej].stores) fields.push_back(out_field(st.first));
+    if (tt >= 0) fields.push_back(out_field(tt));
     fields.push_back(buf_field("unsigned* err", out->err_buf));
     fields.push_back(i64_field("n", flat ? gr.domain : gr.n));
     fields.push_back(i64_field("rows", gr.rows));
@@ -2174,16 +2273,44 @@ class Lowerer {
     }
     src << "// " << (flat ? "flat scan" : "row scan") << " " << gi << " over " << gr.domain << " elements";
     if (ej >= 0) src << "; pass " << ej << " in the store" << (store_t ? "" : ", scan not stored");
+    if (tt >= 0) src << "; writes the transpose of group " << gr.tstore;
     src << "\n";
     src << "struct " << F << " {\n";
     emit_struct(fields);
     src << "  typedef " << T << " T;\n  static constexpr int VEC = 1;\n";
     emit_source_access(gr, t, T);
     if (store_t) src << " && ccb::aligned16(p.o" << t << ")";
-    if (ej >= 0)
+    if (ej >= 0 && tt < 0)
       for (auto& st : groups[ej].stores) src << " && ccb::aligned16(p.o" << st.first << ")";
     src << ";\n  }\n";
-    if (ej < 0) {
+    if (tt >= 0) {
+      // value of element i as stored (the fused pass applied), and where the transpose goes
+      src << "  typedef " << dt_ctype(g.ts[tt].dt) << " U;\n";
+      src << "  static __device__ __forceinline__ U* tout(const P& p) { return p.o" << tt << "; }\n";
+      src << "  static __device__ __forceinline__ U value(const P& p, long long li, T v) {\n    const int i = (int)li;\n";
+      std::string w = "v";
+      if (gr.tload >= 0) {  // the pass over the inlined transpose, its load replaced by v
+        const Group& mp = groups[gr.tstore];
+        Emitter e(mp.ctx, src);
+        e.suffix = "_m";
+        e.direct_node[gr.tload] = "v";
+        w = e.val(mp.stores[0].second);
+      }
+      if (ej >= 0) {
+        Emitter e(groups[ej].ctx, src);
+        e.suffix = "_e";
+        e.direct[t] = "v";
+        w = e.val(groups[ej].stores[0].second);
+      }
+      if (gr.tpost >= 0) {
+        const Group& mp = groups[gr.tpost];
+        Emitter e(mp.ctx, src);
+        e.suffix = "_m";
+        e.direct[groups[gr.tstore].root] = w;
+        w = e.val(mp.stores[0].second);
+      }
+      src << "    (void)i;\n    return " << w << ";\n  }\n";
+    } else if (ej < 0) {
       src << "  static __device__ __forceinline__ void store(const P& p, long long i, T v) { p.o" << t << "[i] = v; }\n";
       src << "  static __device__ __forceinline__ void store4(const P& p, long long i, const T* x) {\n"
           << "    ccb::V4<T> s; s.v[0] = x[0]; s.v[1] = x[1]; s.v[2] = x[2]; s.v[3] = x[3]; ccb::st4(p.o" << t << " + i, s);\n  }\n";
@@ -2196,6 +2323,8 @@ class Lowerer {
       call = "ccb::scan_flat<" + F + ", " + std::to_string(items) + ">(p);";
     } else if (gr.n >= 1024) {
       call = "ccb::scan_rows_block<" + F + ", " + std::to_string(dt_size(x.dt) == 4 ? 8 : 4) + ">(p);";
+    } else if (tt >= 0) {
+      call = "ccb::scan_rows_warp_t<" + F + ">(p);";
     } else {
       call = "ccb::scan_rows_warp<" + F + ">(p);";
     }
@@ -2207,7 +2336,7 @@ class Lowerer {
     } else {
       l.mode = GM_PERSISTENT;
       l.work = gr.rows;
-      l.per_block = gr.n >= 1024 ? 1 : 8;
+      l.per_block = gr.n >= 1024 ? 1 : tt >= 0 ? 32 : 8;
     }
   }
 
@@ -2566,7 +2695,9 @@ class Lowerer {
         case G_SCATTER: emit_scatter(gi); break;
         case G_MATMUL: emit_matmul(gi); break;
         case G_MATMUL_TC: emit_matmul_tc(gi); break;
-        case G_TRANSPOSE: emit_transpose(gi); break;
+        case G_TRANSPOSE:
+          if (groups[gi].fused_into < 0) emit_transpose(gi);
+          break;
       }
     }
     for (auto& op : g.outputs) {
@@ -2606,6 +2737,7 @@ int lower_graph(const GGraph& g, Lowered& out) {
     L.analyse();
     L.group_all();
     L.fuse_epilogues();
+    L.fuse_transposed_stores();
     L.generate(out);
   } catch (const LowerError& e) {
     return fail(e.code, e.what());

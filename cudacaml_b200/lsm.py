@@ -87,19 +87,32 @@ def _nb(basis: str) -> int:
     return {"scaled3": 3, "poly4": 4}[basis]
 
 
-def paths_graph(n_paths: int, n_steps: int, m: Market = MARKET) -> Graph:
-    """lsm.ml:139-150: column t of S holds time (t+1) dt."""
-    grid = (n_paths, n_steps)
+def _cum_log_paths(n_paths: int, n_steps: int, m: Market):
+    """lsm.ml:139-150: the running sums of the GBM log-increments, [n_paths;
+    n_steps], and the map from them to S."""
     kf = lambda v: D.const(F64, v)  # noqa: E731
     seed = D.scalar("seed", I32)
     dt = m.maturity / n_steps
     drift = (m.rate - 0.5 * m.vol * m.vol) * dt
     vol_dt = m.vol * math.sqrt(dt)
-    z = Rng.normal(F64, seed, grid)
+    z = Rng.normal(F64, seed, (n_paths, n_steps))
     incr = D.map(lambda zi: D.add(kf(drift), D.mul(kf(vol_dt), zi)), z)
-    cum = D.scan_rows(D.add, kf(0.0), incr)
-    s = D.map(lambda c: D.mul(kf(m.s0), D.exp(c)), cum)
-    return Graph("lsm_paths", [("S", s)])
+    return D.scan_rows(D.add, kf(0.0), incr), (lambda c: D.mul(kf(m.s0), D.exp(c)))
+
+
+def paths_graph(n_paths: int, n_steps: int, m: Market = MARKET) -> Graph:
+    """lsm.ml:139-150: column t of S holds time (t+1) dt."""
+    cum, to_s = _cum_log_paths(n_paths, n_steps, m)
+    return Graph("lsm_paths", [("S", D.map(to_s, cum))])
+
+
+def paths_dates_graph(n_paths: int, n_steps: int, m: Market = MARKET) -> Graph:
+    """The same S stored date-major, [n_steps; n_paths] (row t = date t): the
+    map to S applied to the transposed running sums, which the lowering runs
+    as one row scan writing the transposed tiles (no [n_paths; n_steps] copy
+    is stored). The values are paths_graph's, transposed."""
+    cum, to_s = _cum_log_paths(n_paths, n_steps, m)
+    return Graph("lsm_paths", [("ST", D.map(to_s, D.transpose(cum)))])
 
 
 def _basis(n_paths, n_steps, strike, basis, layout="paths", cf=None, tb=None, s=None):
@@ -333,8 +346,9 @@ class CudaResident:
     the normal equations and beta never leave the device. The reference's
     driver brings the normal equations to the host each date for its solve;
     here the same solve runs as a graph (solve_graph) on the device, so the
-    host only launches. S is transposed once after generation so that each
-    date reads one contiguous row; the device buffers are allocated once."""
+    host only launches. S is generated date-major (paths_dates_graph), so
+    each date reads one contiguous row; the device buffers are allocated
+    once."""
 
     def __init__(self, n_paths: int, n_steps: int, m: Market = MARKET, basis: str = "scaled3", device: int = 0):
         from . import backend_cuda as cuda
@@ -346,8 +360,7 @@ class CudaResident:
         self.disc = math.exp(-m.rate * dt)
         self.strike = m.strike
         self.device = device
-        self.paths = cuda.compile_on(device, paths_graph(n_paths, n_steps, m))
-        self.dates = cuda.compile_on(device, _dates_graph(n_paths, n_steps))
+        self.paths = cuda.compile_on(device, paths_dates_graph(n_paths, n_steps, m))
         self.regress = cuda.compile_on(device, regress_graph(n_paths, n_steps, self.strike, self.disc, basis, "dates"))
         self.update = cuda.compile_on(device, update_graph(n_paths, n_steps, self.strike, self.disc, basis, "dates"))
         self.upd_reg = cuda.compile_on(device, update_regress_graph(n_paths, n_steps, self.strike, self.disc, basis, "dates"))
@@ -357,7 +370,7 @@ class CudaResident:
         self.total = cuda.compile_on(device, Graph("lsm_total", [("s", D.reduce(D.add, D.const(F64, 0.0), cfp))]))
         n, ns, nb = n_paths, n_steps, self.nb
         with R.with_device(device):
-            self.bufs = {"S": R.Buffer(n * ns * 8), "ST": R.Buffer(n * ns * 8), "cf_a": R.Buffer(n * 8),
+            self.bufs = {"ST": R.Buffer(n * ns * 8), "cf_a": R.Buffer(n * 8),
                          "cf_b": R.Buffer(n * 8), "seed": R.Buffer(4), "t": R.Buffer(4 * ns), "beta": R.Buffer(nb * 8),
                          "xtx": R.Buffer(nb * nb * 8), "xty": R.Buffer(nb * 8), "sum": R.Buffer(8)}
             self.bufs["t"].upload(np.arange(ns, dtype=np.int32))  # date t lives at t + 4 t bytes
@@ -376,10 +389,9 @@ class CudaResident:
         def bind(c, **ptrs):  # device pointers in the program's param order
             return [ptrs[name] for name, _, _ in c.params]
 
-        cuda.run_device_ptrs(self.paths, bind(self.paths, seed=b["seed"].ptr), [b["S"].ptr], stream)
-        cuda.run_device_ptrs(self.dates, bind(self.dates, S=b["S"].ptr), [b["ST"].ptr], stream)
-        # initial cash flow: intrinsic value at maturity (last column), on the device
-        cuda.run_device_ptrs(self.final, bind(self.final, S=b["S"].ptr), [b["cf_a"].ptr], stream)
+        cuda.run_device_ptrs(self.paths, bind(self.paths, seed=b["seed"].ptr), [b["ST"].ptr], stream)
+        # initial cash flow: intrinsic value at maturity (the last date's row), on the device
+        cuda.run_device_ptrs(self.final, bind(self.final, S=b["ST"].ptr), [b["cf_a"].ptr], stream)
         xtx = np.empty(nb * nb)
         xty = np.empty(nb)
         beta_outs = [b["beta"].ptr + 8 * j for j in range(nb)]
@@ -430,7 +442,7 @@ class CudaResident:
         cuda, R = self.cuda, self.R
         b = self.bufs
         stream = self.regress.lane_stream(0)
-        progs = (self.paths, self.dates, self.final, self.regress, self.solve, self.update, self.upd_reg, self.total)
+        progs = (self.paths, self.final, self.regress, self.solve, self.update, self.upd_reg, self.total)
         with R.with_device(self.device):
             seed_h = np.array([seed], np.int32)
             R.check(R.lib().ccb_memcpy_h2d(b["seed"].ptr, seed_h.ctypes.data, 4, stream))
@@ -456,19 +468,15 @@ class CudaResident:
             for buf in self.bufs.values():
                 buf.free()
         self.bufs = {}
-        for c in (self.paths, self.dates, self.regress, self.update, self.upd_reg, self.final, self.solve, self.total):
+        for c in (self.paths, self.regress, self.update, self.upd_reg, self.final, self.solve, self.total):
             self.cuda.release(c)
 
 
-def _dates_graph(n_paths, n_steps) -> Graph:
-    """S [n_paths; n_steps] -> its transpose [n_steps; n_paths] (Dsl.transpose)."""
-    return Graph("lsm_dates", [("ST", D.transpose(D.param("S", F64, (n_paths, n_steps))))])
-
-
 def _final_graph(n_paths, n_steps, strike) -> Graph:
-    """max(K - S[:, n_steps - 1], 0): the initial cash flow, on the device."""
-    s = D.param("S", F64, (n_paths, n_steps))
-    idx = D.map(lambda p: D.add(D.mul(p, D.const(I32, n_steps)), D.const(I32, n_steps - 1)), D.iota((n_paths,)))
+    """max(K - S at maturity, 0): the initial cash flow, on the device, from
+    the last row of the date-major S [n_steps; n_paths]."""
+    s = D.param("S", F64, (n_steps, n_paths))
+    idx = D.map(lambda p: D.add(p, D.const(I32, (n_steps - 1) * n_paths)), D.iota((n_paths,)))
     last = D.gather(idx, s)
     return Graph("lsm_final", [("cf", D.map(lambda x: D.max(D.sub(D.const(F64, strike), x), D.const(F64, 0.0)), last))])
 

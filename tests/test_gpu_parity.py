@@ -507,6 +507,39 @@ def test_output_events_order_a_second_stream():
     cuda.release(c)
 
 
+@pytest.mark.parametrize("dt,rows,n", [(F64, 1000, 64), (F32, 70, 100), (F64, 4096 + 3, 31), (F32, 33, 1000)],
+                         ids=["f64-1000x64", "f32-70x100", "f64-4099x31", "f32-33x1000"])
+def test_row_scan_transposed_store_matches_separate(dt, rows, n):
+    # a row scan whose result is read only transposed writes the transpose
+    # through shared-memory tiles: ragged row tiles (rows % 32) and column
+    # chunks (n % 32), bare and with a map over the transpose, against the
+    # scan stored and transposed by separate launches
+    x = ((np.arange(rows * n) % 23 - 11) / 32.0).astype(dt.np).reshape(rows, n)
+    px = D.param("x", dt, (rows, n))
+    c = D.scan_rows(D.add, D.const(dt, 0.0), px)
+
+    def f(v):
+        return D.mul(D.const(dt, 1.5), D.exp(v))
+
+    def run(graph, ins):
+        cc = cuda.compile(graph)
+        try:
+            return cc.plan(), {k: v.data for k, v in cuda.run(cc, ins)}
+        finally:
+            cuda.release(cc)
+
+    ins = [("x", Value.of_array(dt, (rows, n), x))]
+    _, sc = run(Graph("s", [("c", c)]), ins)
+    ref_t = sc["c"].reshape(rows, n).T.copy()
+    _, sep = run(Graph("m", [("y", D.map(f, D.param("t", dt, (n, rows))))]), [("t", Value.of_array(dt, (n, rows), ref_t))])
+    plan, tr = run(Graph("t", [("t", D.transpose(c))]), ins)
+    assert plan.count("launch") == 1
+    assert np.array_equal(tr["t"].reshape(n, rows), ref_t)
+    plan, fused = run(Graph("fy", [("y", D.map(f, D.transpose(c)))]), ins)
+    assert plan.count("launch") == 1
+    assert np.array_equal(fused["y"], sep["y"])
+
+
 def test_s5_pool_stable():
     n = 4096
     c = cuda.compile(X.saxpy(n, 2.0))

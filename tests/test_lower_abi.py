@@ -213,3 +213,23 @@ def test_scan_store_fusion():
     y32 = D.map(lambda v: D.exp(v), D.scan(D.add, D.const(F32, 0.0), x32))
     assert B.lower_info(Graph("f", [("y", y32)]))["launches"] == 2
     assert nvrtc_ok(info["source"], "scanfused") > 0
+
+
+def test_row_scan_writes_its_transpose():
+    from cudacaml_b200 import lsm as L
+    # LSM's date-major S: one row-scan launch writes the transposed tiles
+    info = B.lower_info(L.paths_dates_graph(1 << 12, 64, L.BASELINE_MARKET))
+    assert info["launches"] == 1 and "scan_rows_warp_t" in info["source"]
+    assert info["plan"].count("alloc t") == 1  # only the [64; 4096] result
+    x = D.param("x", F32, (1000, 40))
+    c = D.scan_rows(D.add, D.const(F32, 0.0), x)
+    # a materialised transpose (an output) and a transpose used by the map
+    # over it both fuse; a map that uses the element index does not
+    t = D.transpose(c)
+    assert B.lower_info(Graph("t", [("t", t)]))["launches"] == 1
+    assert B.lower_info(Graph("t", [("y", D.map(lambda v: D.exp(v), t))]))["launches"] == 1
+    idx_map = D.map(lambda v: D.add(v, D.cast(F32, D.index())), t)
+    assert B.lower_info(Graph("t", [("y", idx_map)]))["launches"] == 2
+    # the scan itself also an output: stored, then transposed apart
+    assert B.lower_info(Graph("t", [("t", t), ("c", c)]))["launches"] == 2
+    assert nvrtc_ok(B.lower_info(L.paths_dates_graph(1 << 12, 64, L.BASELINE_MARKET))["source"], "pt") > 0
