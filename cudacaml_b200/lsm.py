@@ -208,6 +208,28 @@ def update_regress_graph(n_paths, n_steps, strike, disc, basis="scaled3", layout
     return Graph("lsm_update_regress", [("cf", cf), ("xtx", xtx), ("xty", xty)])
 
 
+def _with_solve(name, pairs, nb):
+    """Graph of `pairs` (which hold "xtx" [nb; nb] and "xty" [nb; 1]) plus the
+    solved beta b0 .. b{nb-1}: the solve becomes scalar tails of the same
+    pass, run by its last block once the sums are final."""
+    d = dict(pairs)
+    bs = _solve(D.reshape((nb * nb,), d["xtx"]), D.reshape((nb,), d["xty"]), nb)
+    return Graph(name, list(pairs) + [(f"b{i}", b) for i, b in enumerate(bs)])
+
+
+def regress_solve_graph(n_paths, n_steps, strike, disc, basis="scaled3", layout="dates") -> Graph:
+    """regress_graph and solve_graph in one pass (the first date)."""
+    xtx, xty = _regress(n_paths, n_steps, strike, disc, basis, layout)
+    return _with_solve("lsm_regress_solve", [("xtx", xtx), ("xty", xty)], _nb(basis))
+
+
+def update_regress_solve_graph(n_paths, n_steps, strike, disc, basis="scaled3", layout="dates") -> Graph:
+    """update_regress_graph and the solve of its normal equations in one
+    pass: one launch per date."""
+    g = update_regress_graph(n_paths, n_steps, strike, disc, basis, layout)
+    return _with_solve("lsm_update_regress_solve", list(g.outputs), _nb(basis))
+
+
 def solve_graph(nb: int) -> Graph:
     """The normal-equation solve of ``_beta`` as a graph, so that the
     resident driver keeps beta on the device: the ridge and the "fewer than nb
@@ -219,6 +241,12 @@ def solve_graph(nb: int) -> Graph:
     one single-element pass. Outputs b0 .. b{nb-1}, each [1]."""
     xtx = D.param("xtx", F64, (nb * nb,))
     xty = D.param("xty", F64, (nb,))
+    return Graph("lsm_solve", [(f"b{i}", b) for i, b in enumerate(_solve(xtx, xty, nb))])
+
+
+def _solve(xtx, xty, nb: int):
+    """solve_graph's arithmetic on tensors xtx [nb*nb] and xty [nb]: the list
+    of the nb one-element beta tensors."""
     one = (1,)
     kf = lambda v: D.const(F64, v)  # noqa: E731
 
@@ -294,7 +322,7 @@ def solve_graph(nb: int) -> Graph:
         x[i] = f2(D.div, acc, a[i][i])
     for i in range(nb):
         bad = bor(bad, flag1(lambda e: D.not_(D.eq(D.sub(e, e), kf(0.0))), x[i]))
-    return Graph("lsm_solve", [(f"b{i}", pick(bad, D.full(F64, one, 0.0), x[i])) for i in range(nb)])
+    return [pick(bad, D.full(F64, one, 0.0), x[i]) for i in range(nb)]
 
 
 def _beta(xtx, xty, nb):
@@ -361,17 +389,18 @@ class CudaResident:
         self.strike = m.strike
         self.device = device
         self.paths = cuda.compile_on(device, paths_dates_graph(n_paths, n_steps, m))
-        self.regress = cuda.compile_on(device, regress_graph(n_paths, n_steps, self.strike, self.disc, basis, "dates"))
         self.update = cuda.compile_on(device, update_graph(n_paths, n_steps, self.strike, self.disc, basis, "dates"))
-        self.upd_reg = cuda.compile_on(device, update_regress_graph(n_paths, n_steps, self.strike, self.disc, basis, "dates"))
+        self.reg_solve = cuda.compile_on(device, regress_solve_graph(n_paths, n_steps, self.strike, self.disc, basis, "dates"))
+        self.upd_reg = cuda.compile_on(device, update_regress_solve_graph(n_paths, n_steps, self.strike, self.disc, basis,
+                                                                          "dates"))
         self.final = cuda.compile_on(device, _final_graph(n_paths, n_steps, self.strike))
-        self.solve = cuda.compile_on(device, solve_graph(self.nb))
         cfp = D.param("cf", F64, (n_paths,))
         self.total = cuda.compile_on(device, Graph("lsm_total", [("s", D.reduce(D.add, D.const(F64, 0.0), cfp))]))
         n, ns, nb = n_paths, n_steps, self.nb
         with R.with_device(device):
             self.bufs = {"ST": R.Buffer(n * ns * 8), "cf_a": R.Buffer(n * 8),
                          "cf_b": R.Buffer(n * 8), "seed": R.Buffer(4), "t": R.Buffer(4 * ns), "beta": R.Buffer(nb * 8),
+                         "beta_b": R.Buffer(nb * 8),
                          "xtx": R.Buffer(nb * nb * 8), "xty": R.Buffer(nb * 8), "sum": R.Buffer(8)}
             self.bufs["t"].upload(np.arange(ns, dtype=np.int32))  # date t lives at t + 4 t bytes
         self.graph = None  # the captured price, made by the first price()
@@ -394,9 +423,13 @@ class CudaResident:
         cuda.run_device_ptrs(self.final, bind(self.final, S=b["ST"].ptr), [b["cf_a"].ptr], stream)
         xtx = np.empty(nb * nb)
         xty = np.empty(nb)
-        beta_outs = [b["beta"].ptr + 8 * j for j in range(nb)]
         cur, nxt = b["cf_a"], b["cf_b"]
-        outs = {"xtx": b["xtx"].ptr, "xty": b["xty"].ptr}
+        beta, beta_next = b["beta"], b["beta_b"]  # read by this date's update, written for the next
+
+        def outs_of(prog, cf_out, beta_out):
+            o = {"cf": cf_out, "xtx": b["xtx"].ptr, "xty": b["xty"].ptr}
+            o.update({f"b{j}": beta_out.ptr + 8 * j for j in range(nb)})
+            return [o[name] for name, _, _ in prog.outputs]
 
         def normal_equations(step, prog):
             if trace is not None:
@@ -404,29 +437,27 @@ class CudaResident:
                 R.check(R.lib().ccb_memcpy_d2h(xty.ctypes.data, b["xty"].ptr, xty.nbytes, stream))
                 cuda.check_device(prog, stream)
                 trace.append((step, xtx.copy(), xty.copy()))
-            cuda.run_device_ptrs(self.solve, bind(self.solve, xtx=b["xtx"].ptr, xty=b["xty"].ptr),
-                                 [beta_outs[int(name[1:])] for name, _, _ in self.solve.outputs], stream)
 
-        # Dates ns-2 .. 0 backwards. The first date's normal equations come
-        # from the regression alone; after that each pass updates date t's
-        # cash flow and sums date t-1's normal equations from it, and the
-        # last date (0) is an update alone.
+        # Dates ns-2 .. 0 backwards, one launch each: the first date's normal
+        # equations and their solve; then per date the update with the last
+        # beta, the next date's normal equations from the updated cash flow
+        # and their solve; the last date (0) an update alone.
         steps = list(range(ns - 2, -1, -1))
         if steps:
+            rs = self.reg_solve
             t0 = b["t"].ptr + 4 * steps[0]
-            cuda.run_device_ptrs(self.regress, bind(self.regress, S=b["ST"].ptr, cf=cur.ptr, t=t0),
-                                 [outs[name] for name, _, _ in self.regress.outputs], stream)
-            normal_equations(steps[0], self.regress)
+            cuda.run_device_ptrs(rs, bind(rs, S=b["ST"].ptr, cf=cur.ptr, t=t0), outs_of(rs, None, beta), stream)
+            normal_equations(steps[0], rs)
         for k, step in enumerate(steps):
             t_ptr = b["t"].ptr + 4 * step
             if k + 1 < len(steps):
                 ur = self.upd_reg
-                dst = {"cf": nxt.ptr, **outs}
-                cuda.run_device_ptrs(ur, bind(ur, S=b["ST"].ptr, cf=cur.ptr, t=t_ptr, beta=b["beta"].ptr),
-                                     [dst[name] for name, _, _ in ur.outputs], stream)
+                cuda.run_device_ptrs(ur, bind(ur, S=b["ST"].ptr, cf=cur.ptr, t=t_ptr, beta=beta.ptr),
+                                     outs_of(ur, nxt.ptr, beta_next), stream)
                 normal_equations(step - 1, ur)
+                beta, beta_next = beta_next, beta
             else:
-                cuda.run_device_ptrs(self.update, bind(self.update, S=b["ST"].ptr, cf=cur.ptr, t=t_ptr, beta=b["beta"].ptr),
+                cuda.run_device_ptrs(self.update, bind(self.update, S=b["ST"].ptr, cf=cur.ptr, t=t_ptr, beta=beta.ptr),
                                      [nxt.ptr], stream)
             cur, nxt = nxt, cur
         # the mean of the discounted cash flows (lsm.ml:303-305): summed on the device
@@ -441,8 +472,8 @@ class CudaResident:
         date."""
         cuda, R = self.cuda, self.R
         b = self.bufs
-        stream = self.regress.lane_stream(0)
-        progs = (self.paths, self.final, self.regress, self.solve, self.update, self.upd_reg, self.total)
+        stream = self.reg_solve.lane_stream(0)
+        progs = (self.paths, self.final, self.reg_solve, self.update, self.upd_reg, self.total)
         with R.with_device(self.device):
             seed_h = np.array([seed], np.int32)
             R.check(R.lib().ccb_memcpy_h2d(b["seed"].ptr, seed_h.ctypes.data, 4, stream))
@@ -468,7 +499,7 @@ class CudaResident:
             for buf in self.bufs.values():
                 buf.free()
         self.bufs = {}
-        for c in (self.paths, self.regress, self.update, self.upd_reg, self.final, self.solve, self.total):
+        for c in (self.paths, self.reg_solve, self.update, self.upd_reg, self.final, self.total):
             self.cuda.release(c)
 
 

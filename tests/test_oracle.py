@@ -279,3 +279,31 @@ def test_lsm_update_regress_graph_is_update_then_regress():
         assert np.array_equal(fused["cf"].data, upd["cf"].data)
         assert np.array_equal(fused["xtx"].data, reg["xtx"].data)
         assert np.array_equal(fused["xty"].data, reg["xty"].data)
+
+
+def test_lsm_update_regress_solve_graph_is_the_three_in_turn():
+    # one launch per date on the device: update, next normal equations and
+    # their solve; on the oracle, bit for bit against the graphs in turn
+    from cudacaml_b200 import lsm as L
+    from cudacaml_b200.ir import F64, I32, Value
+    n, ns, t = 512, 8, 5
+    rng = np.random.default_rng(6)
+    for basis, m in (("poly4", L.BASELINE_MARKET), ("scaled3", L.MARKET)):
+        nb = L._nb(basis)
+        st = m.strike * np.exp(0.2 * rng.standard_normal((ns, n)))
+        cf = np.maximum(m.strike - st[-1], 0.0)
+        beta = rng.standard_normal((nb, 1))
+        tv = lambda k: ("t", Value.of_list(I32, (), [k]))  # noqa: E731
+        common = [("S", Value.of_array(F64, (ns, n), st)), ("cf", Value.of_array(F64, (n,), cf)),
+                  ("beta", Value.of_array(F64, (nb, 1), beta))]
+        fused = dict(I.run(I.compile(L.update_regress_solve_graph(n, ns, m.strike, 0.99, basis)), common + [tv(t)]))
+        ur = dict(I.run(I.compile(L.update_regress_graph(n, ns, m.strike, 0.99, basis)), common + [tv(t)]))
+        sol = dict(I.run(I.compile(L.solve_graph(nb)), [("xtx", Value.of_array(F64, (nb * nb,), ur["xtx"].data)),
+                                                         ("xty", Value.of_array(F64, (nb,), ur["xty"].data))]))
+        for k in ("cf", "xtx", "xty"):
+            assert np.array_equal(fused[k].data, ur[k].data), k
+        for i in range(nb):
+            assert np.array_equal(fused[f"b{i}"].data, sol[f"b{i}"].data), i
+        first = dict(I.run(I.compile(L.regress_solve_graph(n, ns, m.strike, 0.99, basis)), common[:2] + [tv(t)]))
+        reg = dict(I.run(I.compile(L.regress_graph(n, ns, m.strike, 0.99, basis, "dates")), common[:2] + [tv(t)]))
+        assert np.array_equal(first["xtx"].data, reg["xtx"].data)
