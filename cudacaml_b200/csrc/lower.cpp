@@ -1958,7 +1958,13 @@ class Lowerer {
     for (auto& r : gr.reds) roots.push_back(r.var);
     std::vector<int> direct = direct_loads(gr.ctx, roots);
     const std::vector<OffLoad> offs = offset_loads(gr.ctx, roots);
-    src << "  static constexpr int NRED = " << R << ";\n  static constexpr int VEC = 1;\n";
+    // A pass that neither loads nor stores elements (a Monte-Carlo estimator:
+    // Philox draws folded into reductions) gains nothing from the 4-wide
+    // element path, whose copies of the body (13 with the unrolled and tail
+    // loops) overflow the instruction cache: it runs one element at a time
+    // (F64 Greeks 2^28 paths: 2.68 -> 2.60 ms).
+    const bool scalar_only = direct.empty() && offs.empty() && gr.stores.empty();
+    src << "  static constexpr int NRED = " << R << ";\n  static constexpr int VEC = " << (scalar_only ? 0 : 1) << ";\n";
     // Passes that stream data keep 4 vector steps in flight; compute-bound
     // passes (Philox Monte Carlo) unroll 2 to keep the body small.
     src << "  static constexpr int UNROLL = " << (direct.empty() && offs.empty() ? 2 : 4) << ";\n";
