@@ -1080,6 +1080,13 @@ __device__ __forceinline__ void tma_load_2d(unsigned dst, const TmaDesc* map, in
       "l"((unsigned long long)map), "r"(x), "r"(y), "r"(smem_u32(bar))
       : "memory");
 }
+__device__ __forceinline__ void tma_load_3d(unsigned dst, const TmaDesc* map, int x, int y, int z, u64* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(
+          dst),
+      "l"((unsigned long long)map), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
+      : "memory");
+}
 __device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
@@ -1210,13 +1217,19 @@ __device__ __forceinline__ void matmul_tc(const typename F::P& p) {
           const int k0 = ks * BK;
           if (F::A_MN) {
 #pragma unroll
-            for (int g = 0; g < BM / 32; ++g) tma_load_2d(sa + g * 4096u, &p.ta, m0 + 32 * g, k0, &full[stage]);
+            if constexpr (F::A3)
+              tma_load_3d(sa, &p.ta, 0, k0, m0 / 32, &full[stage]);
+            else
+              for (int g = 0; g < BM / 32; ++g) tma_load_2d(sa + g * 4096u, &p.ta, m0 + 32 * g, k0, &full[stage]);
           } else {
             tma_load_2d(sa, &p.ta, k0, m0, &full[stage]);
           }
           if (F::B_MN) {
 #pragma unroll
-            for (int g = 0; g < BN / 32; ++g) tma_load_2d(sb + g * 4096u, &p.tb, n0 + 32 * g, k0, &full[stage]);
+            if constexpr (F::B3)
+              tma_load_3d(sb, &p.tb, 0, k0, n0 / 32, &full[stage]);
+            else
+              for (int g = 0; g < BN / 32; ++g) tma_load_2d(sb + g * 4096u, &p.tb, n0 + 32 * g, k0, &full[stage]);
           } else {
             tma_load_2d(sb, &p.tb, k0, n0, &full[stage]);
           }
@@ -1330,6 +1343,13 @@ __device__ __forceinline__ void tma_load_2d(unsigned dst, const TmaDesc* map, in
       "l"((unsigned long long)map), "r"(x), "r"(y), "r"(bar_cluster)
       : "memory");
 }
+__device__ __forceinline__ void tma_load_3d(unsigned dst, const TmaDesc* map, int x, int y, int z, unsigned bar_cluster) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(
+          dst),
+      "l"((unsigned long long)map), "r"(x), "r"(y), "r"(z), "r"(bar_cluster)
+      : "memory");
+}
 __device__ __forceinline__ void mma(unsigned d, u64 a, u64 b, unsigned idesc, unsigned accumulate) {
   const unsigned z = 0;
   asm volatile(
@@ -1410,13 +1430,19 @@ __device__ __forceinline__ void matmul_tc2(const typename F::P& p) {
           const int k0 = ks * BK;
           if (F::A_MN) {
 #pragma unroll
-            for (int g = 0; g < HALF / 32; ++g) tma_load_2d(sa + g * 4096u, &p.ta, m0 + 32 * g, k0, fb);
+            if constexpr (F::A3)
+              tma_load_3d(sa, &p.ta, 0, k0, m0 / 32, fb);
+            else
+              for (int g = 0; g < HALF / 32; ++g) tma_load_2d(sa + g * 4096u, &p.ta, m0 + 32 * g, k0, fb);
           } else {
             tma_load_2d(sa, &p.ta, k0, m0, fb);
           }
           if (F::B_MN) {
 #pragma unroll
-            for (int g = 0; g < HALF / 32; ++g) tma_load_2d(sb + g * 4096u, &p.tb, n0 + 32 * g, k0, fb);
+            if constexpr (F::B3)
+              tma_load_3d(sb, &p.tb, 0, k0, n0 / 32, fb);
+            else
+              for (int g = 0; g < HALF / 32; ++g) tma_load_2d(sb + g * 4096u, &p.tb, n0 + 32 * g, k0, fb);
           } else {
             tma_load_2d(sb, &p.tb, k0, n0, fb);
           }

@@ -75,9 +75,10 @@ struct Slot {
   int kind = SL_BUF;
   int buf = -1;
   int64_t val = 0;
-  int64_t tdim[2] = {0, 0};
-  int64_t tstride = 0;
-  int tbox[2] = {0, 0};
+  int64_t tdim[3] = {0, 0, 1};
+  int64_t tstride = 0, tstride2 = 0;  // bytes between dim-1 / dim-2 steps
+  int tbox[3] = {0, 0, 1};
+  int trank = 2;
   int tswizzle = 3;  // CUtensorMapSwizzle: 3 = 128B, 4 = 128B with 32-byte atoms
 };
 

@@ -108,11 +108,12 @@ int tensor_map(Lane& ln, int64_t key, const Slot& sl, CUdeviceptr base, const CU
   if (base & 15)
     return fail(CCB_ERR_INVALID, "tensor-core matmul operand at a device address that is not 16-byte aligned");
   CUtensorMap m;
-  const cuuint64_t dims[2] = {(cuuint64_t)sl.tdim[0], (cuuint64_t)sl.tdim[1]};
-  const cuuint64_t strides[1] = {(cuuint64_t)sl.tstride};
-  const cuuint32_t box[2] = {(cuuint32_t)sl.tbox[0], (cuuint32_t)sl.tbox[1]};
-  const cuuint32_t estr[2] = {1, 1};
-  CCB_CU(driver().cuTensorMapEncodeTiled(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void*)base, dims, strides, box, estr,
+  const cuuint64_t dims[3] = {(cuuint64_t)sl.tdim[0], (cuuint64_t)sl.tdim[1], (cuuint64_t)sl.tdim[2]};
+  const cuuint64_t strides[2] = {(cuuint64_t)sl.tstride, (cuuint64_t)sl.tstride2};
+  const cuuint32_t box[3] = {(cuuint32_t)sl.tbox[0], (cuuint32_t)sl.tbox[1], (cuuint32_t)sl.tbox[2]};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  CCB_CU(driver().cuTensorMapEncodeTiled(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, (cuuint32_t)sl.trank, (void*)base, dims, strides,
+                                         box, estr,
                                          CU_TENSOR_MAP_INTERLEAVE_NONE, (CUtensorMapSwizzle)sl.tswizzle,
                                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE));
   auto& slot = ln.tmaps[key];
