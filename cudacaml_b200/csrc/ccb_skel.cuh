@@ -1105,8 +1105,8 @@ __device__ __forceinline__ u64 desc_k(unsigned tile, int kk) { return sdesc(tile
 // MN-major tile: 32-element (128-byte) rows along MN, one row per k; 4-row
 // atoms 512 bytes apart (SBO) and 32-element MN blocks 4096 bytes apart (LBO);
 // k-step kk covers rows 8kk..8kk+7.
-__device__ __forceinline__ u64 desc_mn(unsigned tile, int kk) {
-  return sdesc(tile + kk * 1024u, 4096u, 512u, LAYOUT_SW128_BASE32B);
+__device__ __forceinline__ u64 desc_mn(unsigned tile, int kk, unsigned lbo = 4096u) {
+  return sdesc(tile + kk * 1024u, lbo, 512u, LAYOUT_SW128_BASE32B);
 }
 __device__ __forceinline__ void mma(unsigned d, u64 a, u64 b, unsigned idesc, unsigned accumulate) {
   const unsigned z = 0;
@@ -1317,9 +1317,8 @@ __device__ __forceinline__ void matmul_tc(const typename F::P& p) {
 // CTAs' epilogue warps release an accumulator to the leader.
 // Same operand views, bounds handling and numerics as matmul_tc.
 namespace tc2 {
-constexpr int BM = 256, BN = 256, HALF = 128, BK = 32, STAGES = 6, THREADS = 192;
-constexpr unsigned A_BYTES = HALF * BK * 4, B_BYTES = HALF * BK * 4, STAGE_BYTES = A_BYTES + B_BYTES;
-constexpr unsigned SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+constexpr int BM = 256, BN = 256, HALF = 128, THREADS = 192;
+constexpr unsigned RING_BYTES = 6u * 32768u;  // the stage ring: 6 x 32 KiB or 3 x 64 KiB
 constexpr unsigned TMEM_COLS = 2 * BN;
 
 __device__ __forceinline__ unsigned cta_rank() {
@@ -1370,6 +1369,15 @@ __device__ __forceinline__ void arrive_leader(u64* bar) {
 template <class F>
 __device__ __forceinline__ void matmul_tc2(const typename F::P& p) {
   using namespace tc2;
+  // k-step of BK (32 or 64): a stage holds this CTA's 128 rows of A and 128
+  // columns of B over BK; K-major operands come as BK/32 boxes 32 wide (the
+  // 128-byte swizzle span), MN-major ones as one 3-D copy (or 2-D boxes) of
+  // 32-element MN blocks BK rows deep.
+  constexpr int BK = F::BK;
+  constexpr unsigned A_BYTES = HALF * BK * 4, B_BYTES = HALF * BK * 4, STAGE_BYTES = A_BYTES + B_BYTES;
+  constexpr int STAGES = (int)(RING_BYTES / STAGE_BYTES);
+  constexpr unsigned KCHUNK = HALF * 32 * 4;  // one 32-wide K-major box: 16 KiB
+  constexpr unsigned MNBLK = 32 * BK * 4;     // one 32-element MN block: 4 or 8 KiB
   extern __shared__ __align__(1024) unsigned char ccb_tc_smem[];
   const unsigned raw = smem_u32(ccb_tc_smem);
   const unsigned pad = (1024u - (raw & 1023u)) & 1023u;
@@ -1428,23 +1436,27 @@ __device__ __forceinline__ void matmul_tc2(const typename F::P& p) {
                          : "memory");
           }
           const int k0 = ks * BK;
-          if (F::A_MN) {
-#pragma unroll
-            if constexpr (F::A3)
+          if constexpr (F::A_MN) {
+            if constexpr (F::A3) {
               tma_load_3d(sa, &p.ta, 0, k0, m0 / 32, fb);
-            else
-              for (int g = 0; g < HALF / 32; ++g) tma_load_2d(sa + g * 4096u, &p.ta, m0 + 32 * g, k0, fb);
-          } else {
-            tma_load_2d(sa, &p.ta, k0, m0, fb);
-          }
-          if (F::B_MN) {
+            } else {
 #pragma unroll
-            if constexpr (F::B3)
-              tma_load_3d(sb, &p.tb, 0, k0, n0 / 32, fb);
-            else
-              for (int g = 0; g < HALF / 32; ++g) tma_load_2d(sb + g * 4096u, &p.tb, n0 + 32 * g, k0, fb);
+              for (int g = 0; g < HALF / 32; ++g) tma_load_2d(sa + g * MNBLK, &p.ta, m0 + 32 * g, k0, fb);
+            }
           } else {
-            tma_load_2d(sb, &p.tb, k0, n0, fb);
+#pragma unroll
+            for (int c = 0; c < BK / 32; ++c) tma_load_2d(sa + c * KCHUNK, &p.ta, k0 + 32 * c, m0, fb);
+          }
+          if constexpr (F::B_MN) {
+            if constexpr (F::B3) {
+              tma_load_3d(sb, &p.tb, 0, k0, n0 / 32, fb);
+            } else {
+#pragma unroll
+              for (int g = 0; g < HALF / 32; ++g) tma_load_2d(sb + g * MNBLK, &p.tb, n0 + 32 * g, k0, fb);
+            }
+          } else {
+#pragma unroll
+            for (int c = 0; c < BK / 32; ++c) tma_load_2d(sb + c * KCHUNK, &p.tb, k0 + 32 * c, n0, fb);
           }
           if (++stage == STAGES) {
             stage = 0;
@@ -1470,8 +1482,8 @@ __device__ __forceinline__ void matmul_tc2(const typename F::P& p) {
           const unsigned sa = sbase + stage * STAGE_BYTES, sb = sa + A_BYTES;
 #pragma unroll
           for (int kk = 0; kk < BK / 8; ++kk) {
-            const u64 a = F::A_MN ? tc::desc_mn(sa, kk) : tc::desc_k(sa, kk);
-            const u64 b = F::B_MN ? tc::desc_mn(sb, kk) : tc::desc_k(sb, kk);
+            const u64 a = F::A_MN ? tc::desc_mn(sa, kk, MNBLK) : tc::desc_k(sa + (kk >> 2) * KCHUNK, kk & 3);
+            const u64 b = F::B_MN ? tc::desc_mn(sb, kk, MNBLK) : tc::desc_k(sb + (kk >> 2) * KCHUNK, kk & 3);
             mma(d, a, b, idesc, (ks | kk) != 0 ? 1u : 0u);
           }
           commit_both(&empty[stage]);
