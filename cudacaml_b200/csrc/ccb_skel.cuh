@@ -424,7 +424,8 @@ __device__ __forceinline__ void scan_flat(const typename F::P& p) {
 
 // ---------------------------------------------------------------- staged flat scan (TMA)
 // Persistent single-pass scan of a 4-byte source buffer. Each CTA keeps three
-// 32 KiB tiles in flight in shared memory: one arriving by a 1-D bulk async
+// tiles of STRIPS x 4 KiB (the lowering uses 6: 24 KiB, 3 CTAs per SM) in
+// flight in shared memory: one arriving by a 1-D bulk async
 // copy (cp.async.bulk, the TMA engine; never multicast), one whose aggregate
 // it publishes, and one it finishes. Publishing tile k's aggregate before
 // walking back for tile k-1 gives every predecessor a full iteration to
@@ -519,13 +520,14 @@ __device__ __forceinline__ typename F::T walk_back(const typename F::P& p, unsig
   return prefix;
 }
 
-template <class F>
+template <class F, int STRIPS>
 __device__ __forceinline__ void scan_flat_staged(const typename F::P& p) {
   typedef typename F::T T;
   static_assert(sizeof(T) == 4, "staged scan is for 4-byte element types");
-  constexpr int BLOCK = 256, NBUF = 3, STRIPS = 8, STRIP = BLOCK * 4, TILE = STRIP * STRIPS;
+  constexpr int BLOCK = 256, NBUF = 3, STRIP = BLOCK * 4, TILE = STRIP * STRIPS;
   constexpr int NW = BLOCK / 32;
-  static_assert(STRIPS * NW == 64, "the chunk-total scan folds 2 entries per lane");
+  constexpr int NE = STRIPS * NW, PER = (NE + 31) / 32;  // chunk totals, PER per lane in the fold
+  static_assert(NE <= 32 * 4, "at most 4 chunk totals per lane");
   extern __shared__ __align__(128) unsigned char smem_raw[];
   T* buf = reinterpret_cast<T*>(smem_raw);
   u64* bars = reinterpret_cast<u64*>(smem_raw + (size_t)NBUF * TILE * sizeof(T));
@@ -604,14 +606,24 @@ __device__ __forceinline__ void scan_flat_staged(const typename F::P& p) {
       }
       __syncthreads();
       if (warp == 0) {
-        // 64 warp totals in (strip, warp) order, two per lane
-        const T w0 = s_ws[2 * lane], w1 = s_ws[2 * lane + 1];
-        const T pair = F::combine(w0, w1);
-        const T incl = warp_scan_incl<F>(pair, lane);
+        // NE warp totals in (strip, warp) order, PER consecutive ones per lane
+        T w[PER];
+        T part = F::identity();
+#pragma unroll
+        for (int q = 0; q < PER; ++q) {
+          const int e = PER * lane + q;
+          w[q] = e < NE ? s_ws[e] : F::identity();
+          part = F::combine(part, w[q]);
+        }
+        const T incl = warp_scan_incl<F>(part, lane);
         T ex = __shfl_up_sync(FULL, incl, 1);
         if (lane == 0) ex = F::identity();
-        s_off[2 * lane] = ex;
-        s_off[2 * lane + 1] = F::combine(ex, w0);
+#pragma unroll
+        for (int q = 0; q < PER; ++q) {
+          const int e = PER * lane + q;
+          if (e < NE) s_off[e] = ex;
+          ex = F::combine(ex, w[q]);
+        }
         if (lane == 31) publish_aggregate<F>(p, (unsigned)tc, incl);
         agg_cur = __shfl_sync(FULL, incl, 31);
       }

@@ -2176,7 +2176,11 @@ class Lowerer {
     const std::string F = "F" + std::to_string(gi);
     const std::string fn = "ccb_scanstaged_" + std::to_string(gi) + kname_suffix();
     node_buf[t] = add_buf("t" + std::to_string(x.uid), dt_size(x.dt), x.numel, BR_NODE, t, false);
-    constexpr int64_t TILE = 8192;
+    // 24 KiB tiles (6 strips of 256 x 4 elements): 3 CTAs/SM with the
+    // 3-deep ring (2^28 F32: 0.432 ms; 32 KiB tiles at 2 CTAs/SM 0.453,
+    // 20 KiB 0.47, 28 KiB 0.48)
+    constexpr int strips = 6;
+    const int64_t TILE = 1024 * strips;
     const int64_t ntiles = std::max<int64_t>(1, (gr.domain + TILE - 1) / TILE);
     const std::string pre = "g" + std::to_string(gi);
     std::vector<Field> fields;
@@ -2212,7 +2216,7 @@ class Lowerer {
     src << "  static __device__ __forceinline__ T* dst(const P& p) { return p.o" << t << "; }\n";
     src << "};\n";
     src << "extern \"C\" __global__ void __launch_bounds__(256) " << fn << "(const " << F << "::P p) { ccb::scan_flat_staged<" << F
-        << ">(p); }\n\n";
+        << ", " << strips << ">(p); }\n\n";
     LaunchSpec& l = add_launch(fn, fields);
     l.mode = GM_PERSISTENT;
     l.work = ntiles;

@@ -581,9 +581,9 @@ def test_s19_multi_same_device_and_counter_split():
     assert abs(pm - p1) <= 1e-9 * (1 + abs(p1))
 
 
-@pytest.mark.parametrize("n", [1, 4, 8191, 8192, 8193, 3 * 8192 + 5, 1 << 16, (1 << 20) + 7])
+@pytest.mark.parametrize("n", [1, 4, 6143, 6144, 6145, 8192, 3 * 6144 + 5, 1 << 16, (1 << 20) + 7])
 def test_flat_scan_tile_edges_i32_exact(n):
-    # the staged scan's 8192-element tiles: ragged last tiles, one-tile and
+    # the staged scan's 6144-element tiles: ragged last tiles, one-tile and
     # multi-tile cases, bit-exact for I32 (wrapping add)
     x = (X.philox_word0(9, n) & 1023).astype(np.int32)
     g = X.scan_flat(n, I32)
@@ -605,7 +605,7 @@ def test_flat_scan_max_and_repeat_runs():
         assert np.array_equal(got, np.maximum.accumulate(x))
 
 
-@pytest.mark.parametrize("n", [1 << 20, (1 << 20) + 32, 3 * 296 * 8192 + 96, (1 << 24) + 4096])
+@pytest.mark.parametrize("n", [1 << 20, (1 << 20) + 32, 3 * 444 * 6144 + 96, (1 << 24) + 4096])
 def test_flat_scan_large_i32_exact(n):
     # larger flat scans: a partial last tile, a few hundred tiles, thousands of
     # tiles; bit-exact I32, three launches of one program (epoch-tagged
