@@ -162,6 +162,16 @@ __device__ __forceinline__ void map_reduce(const typename F::P& p) {
     }
     for (; g < n4; g += nth) F::elem4(p, g << 2, acc);
     for (int i = (n4 << 2) + tid; i < n; i += nth) F::elem(p, i, acc);
+  } else if constexpr (F::VEC == 0 && F::PAIRS) {
+    // two independent elements per iteration: two dependency chains for
+    // the scheduler, three copies of the body; each thread still folds its
+    // elements in the same order
+    int i = tid;
+    for (; i + nth < n; i += 2 * nth) {
+      F::elem(p, i, acc);
+      F::elem(p, i + nth, acc);
+    }
+    if (i < n) F::elem(p, i, acc);
   } else {
     for (int i = tid; i < n; i += nth) F::elem(p, i, acc);
   }

@@ -1965,6 +1965,9 @@ class Lowerer {
     // (F64 Greeks 2^28 paths: 2.68 -> 2.60 ms).
     const bool scalar_only = direct.empty() && offs.empty() && gr.stores.empty();
     src << "  static constexpr int NRED = " << R << ";\n  static constexpr int VEC = " << (scalar_only ? 0 : 1) << ";\n";
+    // F64 estimators take two elements per iteration (F64 Greeks 2.59 ->
+    // 2.53 ms; no gain in F32)
+    src << "  static constexpr bool PAIRS = " << (scalar_only && R > 0 && dt_size(acc) == 8 ? "true" : "false") << ";\n";
     // Passes that stream data keep 4 vector steps in flight; compute-bound
     // passes (Philox Monte Carlo) unroll 2 to keep the body small.
     src << "  static constexpr int UNROLL = " << (direct.empty() && offs.empty() ? 2 : 4) << ";\n";
