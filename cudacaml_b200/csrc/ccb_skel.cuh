@@ -1050,6 +1050,97 @@ __device__ __forceinline__ void matmul_tiled(const typename F::P& p) {
     }
 }
 
+// C[M,N] = A[M,K] . B[K,N] for 4-byte T on the CUDA cores, each output still
+// accumulated in ascending k: 128 x 128 output tile per 256-thread block,
+// 8 x 8 outputs per thread (rows ty*4+i and 64+ty*4+i, columns tx*4+j and
+// 64+tx*4+j, read as 16-byte fragments), K staged 8 at a time in two
+// shared buffers (the next step's elements are loaded into registers while
+// this one is multiplied). Tiles are loaded along the operand's contiguous
+// dimension: F::A_MN when A is a transposed view (a(r,k) = At[k][r]),
+// F::B_KM when B is one (b(k,c) = Bt[c][k]); rows of the shared tiles are
+// padded to 132 elements so the transposing stores hit distinct banks.
+template <class F>
+__device__ __forceinline__ void matmul_tiled128(const typename F::P& p) {
+  typedef typename F::T T;
+  static_assert(sizeof(T) == 4, "4-byte elements");
+  constexpr int BM = 128, BN = 128, BK = 8, LD = BM + 4;
+  __shared__ __align__(16) T As[2][BK][LD];
+  __shared__ __align__(16) T Bs[2][BK][LD];
+  const long long M = p.M, N = p.N, K = p.K;
+  const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+  const long long row0 = (long long)blockIdx.y * BM, col0 = (long long)blockIdx.x * BN;
+  T ra[4], rb[4];
+  // element q of this thread's share of a k-step: (row or column, k)
+  auto a_rc = [&](int q, int& r, int& k) {
+    const int e = tid + 256 * q;
+    if (F::A_MN) { r = e & 127; k = e >> 7; } else { r = e >> 3; k = e & 7; }
+  };
+  auto b_rc = [&](int q, int& c, int& k) {
+    const int e = tid + 256 * q;
+    if (F::B_KM) { c = e >> 3; k = e & 7; } else { c = e & 127; k = e >> 7; }
+  };
+  auto load = [&](long long k0) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      int r, k, c, kb;
+      a_rc(q, r, k);
+      ra[q] = (row0 + r < M && k0 + k < K) ? F::a(p, row0 + r, k0 + k) : T(0);
+      b_rc(q, c, kb);
+      rb[q] = (col0 + c < N && k0 + kb < K) ? F::b(p, k0 + kb, col0 + c) : T(0);
+    }
+  };
+  auto stash = [&](int buf) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      int r, k, c, kb;
+      a_rc(q, r, k);
+      As[buf][k][r] = ra[q];
+      b_rc(q, c, kb);
+      Bs[buf][kb][c] = rb[q];
+    }
+  };
+  T acc[8][8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[i][j] = T(0);
+  const int steps = (int)((K + BK - 1) / BK);
+  load(0);
+  stash(0);
+  __syncthreads();
+  for (int s = 0; s < steps; ++s) {
+    const int buf = s & 1;
+    if (s + 1 < steps) load((long long)(s + 1) * BK);
+#pragma unroll
+    for (int kk = 0; kk < BK; ++kk) {
+      T a[8], b[8];
+      const float4 a0 = *reinterpret_cast<const float4*>(&As[buf][kk][ty * 4]);
+      const float4 a1 = *reinterpret_cast<const float4*>(&As[buf][kk][64 + ty * 4]);
+      const float4 b0 = *reinterpret_cast<const float4*>(&Bs[buf][kk][tx * 4]);
+      const float4 b1 = *reinterpret_cast<const float4*>(&Bs[buf][kk][64 + tx * 4]);
+      memcpy(a, &a0, 16);
+      memcpy(a + 4, &a1, 16);
+      memcpy(b, &b0, 16);
+      memcpy(b + 4, &b1, 16);
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] += a[i] * b[j];
+    }
+    if (s + 1 < steps) stash(buf ^ 1);
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const long long r = row0 + (i < 4 ? ty * 4 + i : 64 + ty * 4 + i - 4);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const long long c = col0 + (j < 4 ? tx * 4 + j : 64 + tx * 4 + j - 4);
+      if (r < M && c < N) F::store(p, r, c, acc[i][j]);
+    }
+  }
+}
+
 // ------------------------------------------------------------------------
 // F32 matmul on the tcgen05 tensor cores (kind::tf32), persistent.
 //

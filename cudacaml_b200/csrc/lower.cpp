@@ -2514,13 +2514,27 @@ class Lowerer {
     }
     src << "  static __device__ __forceinline__ void store(const P& p, long long r, long long c, T v) { p.o" << t
         << "[r * p.N + c] = v; }\n";
+    // 4-byte products of at least one 128 x 128 tile take the register-
+    // blocked kernel; tiles load along the operand's contiguous dimension
+    // (a transposed view of a buffer is read along its own rows)
+    const bool big = dt_size(x.dt) == 4 && M >= 128 && N >= 128;
+    int src_t = -1;
+    const bool a_mn = big && transpose_of(x.dep0, src_t);
+    const bool b_km = big && transpose_of(x.dep1, src_t);
+    if (big) src << "  static constexpr bool A_MN = " << (a_mn ? "true" : "false") << ", B_KM = " << (b_km ? "true" : "false") << ";\n";
     src << "};\n";
-    src << "extern \"C\" __global__ void __launch_bounds__(256) " << fn << "(const " << F << "::P p) { ccb::matmul_tiled<" << F
-        << ">(p); }\n\n";
+    if (big) {
+      src << "extern \"C\" __global__ void __launch_bounds__(256, 2) " << fn << "(const " << F << "::P p) { ccb::matmul_tiled128<"
+          << F << ">(p); }\n\n";
+    } else {
+      src << "extern \"C\" __global__ void __launch_bounds__(256) " << fn << "(const " << F << "::P p) { ccb::matmul_tiled<" << F
+          << ">(p); }\n\n";
+    }
     LaunchSpec& l = add_launch(fn, fields);
     l.mode = GM_FIXED;
-    l.gx = std::max<int64_t>(1, (N + 63) / 64);
-    l.gy = std::max<int64_t>(1, (M + 63) / 64);
+    const int tile = big ? 128 : 64;
+    l.gx = std::max<int64_t>(1, (N + tile - 1) / tile);
+    l.gy = std::max<int64_t>(1, (M + tile - 1) / tile);
   }
 
   // F32 product on the tensor cores (ccb::matmul_tc): operands by TMA from

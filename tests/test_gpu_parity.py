@@ -540,6 +540,31 @@ def test_row_scan_transposed_store_matches_separate(dt, rows, n):
     assert np.array_equal(fused["y"], sep["y"])
 
 
+@pytest.mark.parametrize("m,k,n", [(128, 16, 128), (300, 200, 260), (256, 1000, 384), (1024, 777, 512)],
+                         ids=lambda v: str(v))
+@pytest.mark.parametrize("ta,tb", [(False, False), (True, False), (False, True), (True, True)],
+                         ids=["AB", "AtB", "ABt", "AtBt"])
+def test_f32_product_register_blocked(m, k, n, ta, tb):
+    # the CUDA-core product of 128 x 128 tiles (F32, matmul="f32"): ragged
+    # tiles and k-steps, every operand order, within the F32 summation bound
+    # k * 2^-24 * sum|a||b| of the F64 product of the same inputs
+    rng = np.random.default_rng(m + 3 * k + 7 * n + 2 * ta + tb)
+    a = rng.standard_normal((m, k)).astype(np.float32)
+    b = rng.standard_normal((k, n)).astype(np.float32)
+    pa = D.param("a", F32, (k, m) if ta else (m, k))
+    pb = D.param("b", F32, (n, k) if tb else (k, n))
+    g = Graph("mm128", [("c", D.matmul(D.transpose(pa) if ta else pa, D.transpose(pb) if tb else pb))])
+    c = cuda.compile(g)
+    assert "matmul_tiled128" in cuda.source(g)
+    out = dict(cuda.run(c, [("a", Value.of_array(F32, pa.shape, np.ascontiguousarray(a.T if ta else a))),
+                            ("b", Value.of_array(F32, pb.shape, np.ascontiguousarray(b.T if tb else b)))]))["c"]
+    cuda.release(c)
+    got = out.data.reshape(m, n).astype(np.float64)
+    exact = a.astype(np.float64) @ b.astype(np.float64)
+    mag = np.abs(a.astype(np.float64)) @ np.abs(b.astype(np.float64))
+    assert np.all(np.abs(got - exact) <= (k + 2) * 2.0 ** -24 * mag + 1e-30)
+
+
 def test_s5_pool_stable():
     n = 4096
     c = cuda.compile(X.saxpy(n, 2.0))
