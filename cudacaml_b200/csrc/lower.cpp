@@ -1130,6 +1130,45 @@ class Lowerer {
     }
   }
 
+  // A 4-byte product big enough for matmul_tiled128 re-reads every operand
+  // element once per 128-wide tile of the other side, so an operand that is
+  // an expression (F32-mode MLP: tanh_like(Z1), dZ1 with its exp) is
+  // materialised once, like a tensor-core operand: traced through views to
+  // the tensor it reads, which is stored, and the trace's order (row-major
+  // or transposed) picks the tile load layout.
+  struct SimtInfo {
+    bool on = false, a_mn = false, b_km = false;
+  };
+  std::vector<SimtInfo> simt;
+  void plan_simt_operands() {
+    const int T = (int)g.ts.size();
+    simt.assign(T, SimtInfo());
+    for (int t = 0; t < T; ++t) {
+      const GTensor& x = g.ts[t];
+      if (x.kind != T_MATMUL || dt_size(x.dt) != 4 || small_k(t) || tc[t].on) continue;
+      const int64_t M = x.shape[0], N = x.shape[1], K = g.ts[x.dep0].shape[1];
+      if ((M * N <= 32 && K >= 2048) || M < 128 || N < 128) continue;
+      Aff fa, fb;
+      const int va = peel(x.dep0, M, K, fa), vb = peel(x.dep1, K, N, fb);
+      auto is = [](const Aff& f, int64_t a, int64_t b) { return f.ok && f.a == a && f.b == b && f.k == 0; };
+      SimtInfo si;
+      si.on = true;
+      if (g.ts[va].numel == M * K && g.ts[va].dt == x.dt && (is(fa, K, 1) || is(fa, 1, M))) {
+        mat[va] = 1;
+        si.a_mn = !is(fa, K, 1);
+      } else {
+        mat[x.dep0] = 1;
+      }
+      if (g.ts[vb].numel == K * N && g.ts[vb].dt == x.dt && (is(fb, N, 1) || is(fb, 1, K))) {
+        mat[vb] = 1;
+        si.b_km = !is(fb, N, 1);
+      } else {
+        mat[x.dep1] = 1;
+      }
+      simt[t] = si;
+    }
+  }
+
   void analyse() {
     const int T = (int)g.ts.size();
     uses.assign(T, 0);
@@ -1149,6 +1188,7 @@ class Lowerer {
       if (mat[t] && x.dt == DT_BOOL) bad("Value.create: Bool tensors are not storable (node n" + std::to_string(x.uid) + ")");
     }
     plan_tensor_core();
+    plan_simt_operands();
   }
 
   // ------------------------------------------------------------ element builder
@@ -2517,10 +2557,9 @@ class Lowerer {
     // 4-byte products of at least one 128 x 128 tile take the register-
     // blocked kernel; tiles load along the operand's contiguous dimension
     // (a transposed view of a buffer is read along its own rows)
-    const bool big = dt_size(x.dt) == 4 && M >= 128 && N >= 128;
-    int src_t = -1;
-    const bool a_mn = big && transpose_of(x.dep0, src_t);
-    const bool b_km = big && transpose_of(x.dep1, src_t);
+    const bool big = simt[t].on;
+    const bool a_mn = big && simt[t].a_mn;
+    const bool b_km = big && simt[t].b_km;
     if (big) src << "  static constexpr bool A_MN = " << (a_mn ? "true" : "false") << ", B_KM = " << (b_km ? "true" : "false") << ";\n";
     src << "};\n";
     if (big) {
