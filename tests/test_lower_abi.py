@@ -233,3 +233,28 @@ def test_row_scan_writes_its_transpose():
     # the scan itself also an output: stored, then transposed apart
     assert B.lower_info(Graph("t", [("t", t), ("c", c)]))["launches"] == 2
     assert nvrtc_ok(B.lower_info(L.paths_dates_graph(1 << 12, 64, L.BASELINE_MARKET))["source"], "pt") > 0
+
+
+def test_cuda_core_product_kernels():
+    # 4-byte products of at least 128 x 128 take the register-blocked kernel,
+    # with tiles loaded along each operand's contiguous dimension; smaller
+    # ones and F64 keep the 64 x 64 kernel
+    def mm(dt, m, k, n, ta=False, tb=False):
+        a = D.param("a", dt, (k, m) if ta else (m, k))
+        b = D.param("b", dt, (n, k) if tb else (k, n))
+        return Graph("m", [("c", D.matmul(D.transpose(a) if ta else a, D.transpose(b) if tb else b))])
+
+    src = B.lower_info(mm(F32, 256, 64, 256))["source"]
+    assert "matmul_tiled128" in src and "A_MN = false, B_KM = false" in src
+    assert "A_MN = true, B_KM = true" in B.lower_info(mm(F32, 256, 64, 256, True, True))["source"]
+    assert "matmul_tiled128" not in B.lower_info(mm(F32, 100, 64, 256))["source"]
+    assert "matmul_tiled128" not in B.lower_info(mm(F64, 256, 64, 256))["source"]
+    # an operand expression is stored once before the product reads it
+    x = D.param("x", F32, (256, 64))
+    e = D.map(lambda v: D.exp(v), D.param("w", F32, (64, 256)))
+    info = B.lower_info(Graph("m", [("c", D.matmul(x, e))]))
+    assert info["launches"] == 2 and "launch ccb_mapreduce_" in info["plan"]
+    # the F32-mode MLP step: the TF32 step's structure, 5 products + 3 passes
+    info = B.lower_info(X.mlp_step(512, 256, 512, 128))
+    assert info["launches"] == 8 and info["source"].count("matmul_tiled128<") == 5
+    assert nvrtc_ok(info["source"], "mlp_f32") > 0
