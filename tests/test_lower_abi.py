@@ -258,3 +258,18 @@ def test_cuda_core_product_kernels():
     info = B.lower_info(X.mlp_step(512, 256, 512, 128))
     assert info["launches"] == 8 and info["source"].count("matmul_tiled128<") == 5
     assert nvrtc_ok(info["source"], "mlp_f32") > 0
+
+
+def test_offset_streams_are_vector_loads():
+    # row t of a [rows; n] buffer, t a scalar: read as one 16-byte stream,
+    # checked once (range and alignment) by vec_ok; a row index that is not
+    # uniform (i-dependent) stays a checked scalar gather
+    rows, n = 64, 4096
+    m = D.param("m", F32, (rows, n))
+    tb = D.broadcast((n,), D.scalar("t", I32))
+    idx = D.map2(lambda p, tv: D.add(D.mul(tv, D.const(I32, n)), p), D.iota((n,)), tb)
+    src = B.lower_info(Graph("row", [("r", D.gather(idx, m))]))["source"]
+    assert "K0 = ccb::ld4(p.b" in src and "u + p.n <= " in src
+    rev = D.map(lambda p: D.sub(D.const(I32, n - 1), p), D.iota((n,)))
+    src = B.lower_info(Graph("rev", [("r", D.gather(rev, D.reshape((rows * n,), m)))]))["source"]
+    assert "K0 = " not in src

@@ -307,3 +307,14 @@ def test_lsm_update_regress_solve_graph_is_the_three_in_turn():
         first = dict(I.run(I.compile(L.regress_solve_graph(n, ns, m.strike, 0.99, basis)), common[:2] + [tv(t)]))
         reg = dict(I.run(I.compile(L.regress_graph(n, ns, m.strike, 0.99, basis, "dates")), common[:2] + [tv(t)]))
         assert np.array_equal(first["xtx"].data, reg["xtx"].data)
+
+
+def test_lsm_paths_dates_graph_is_the_transpose():
+    # the date-major paths program gives paths_graph's S transposed, bit for bit
+    from cudacaml_b200 import lsm as L
+    from cudacaml_b200.ir import I32, Value
+    n, ns = 300, 12
+    seed = [("seed", Value.of_list(I32, (), [7]))]
+    s = dict(I.run(I.compile(L.paths_graph(n, ns, L.BASELINE_MARKET)), seed))["S"].data.reshape(n, ns)
+    st = dict(I.run(I.compile(L.paths_dates_graph(n, ns, L.BASELINE_MARKET)), seed))["ST"].data.reshape(ns, n)
+    assert np.array_equal(st, s.T)
