@@ -318,3 +318,15 @@ def test_lsm_paths_dates_graph_is_the_transpose():
     s = dict(I.run(I.compile(L.paths_graph(n, ns, L.BASELINE_MARKET)), seed))["S"].data.reshape(n, ns)
     st = dict(I.run(I.compile(L.paths_dates_graph(n, ns, L.BASELINE_MARKET)), seed))["ST"].data.reshape(ns, n)
     assert np.array_equal(st, s.T)
+
+
+def test_lsm_known_answers_on_the_oracle():
+    # test_lsm.ml's known answers for the reference market (binomial 6.09,
+    # European put 5.5735) and the S17 band: the generic LSM driver over the
+    # oracle, 2^14 paths x 50 dates, within 0.15 of the binomial price
+    from cudacaml_b200 import lsm as L
+    binom = L.binomial_american_put(L.MARKET)
+    assert abs(binom - 6.09) < 0.005
+    assert abs(L.european_put(L.MARKET) - 5.5735) < 1e-3
+    px = L.Make(I, 1 << 14, 50, L.MARKET, "scaled3").price(11)
+    assert abs(px - binom) <= 0.15 and px >= L.european_put(L.MARKET) - 0.05
