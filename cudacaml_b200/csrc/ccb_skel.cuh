@@ -1329,20 +1329,22 @@ __device__ __forceinline__ void matmul_tc(const typename F::P& p) {
           mbar_expect_tx(&full[stage], STAGE_BYTES);
           const int k0 = ks * BK;
           if (F::A_MN) {
-#pragma unroll
-            if constexpr (F::A3)
+            if constexpr (F::A3) {
               tma_load_3d(sa, &p.ta, 0, k0, m0 / 32, &full[stage]);
-            else
+            } else {
+#pragma unroll
               for (int g = 0; g < BM / 32; ++g) tma_load_2d(sa + g * 4096u, &p.ta, m0 + 32 * g, k0, &full[stage]);
+            }
           } else {
             tma_load_2d(sa, &p.ta, k0, m0, &full[stage]);
           }
           if (F::B_MN) {
-#pragma unroll
-            if constexpr (F::B3)
+            if constexpr (F::B3) {
               tma_load_3d(sb, &p.tb, 0, k0, n0 / 32, &full[stage]);
-            else
+            } else {
+#pragma unroll
               for (int g = 0; g < BN / 32; ++g) tma_load_2d(sb + g * 4096u, &p.tb, n0 + 32 * g, k0, &full[stage]);
+            }
           } else {
             tma_load_2d(sb, &p.tb, k0, n0, &full[stage]);
           }
