@@ -13,7 +13,9 @@ Additions, all opt-in:
   same seed (device d draws Philox counters [d*n/D, (d+1)*n/D)), so D devices
   compute exactly the paths one device would. The reference instead asks the
   caller to reseed each device (multi.mli:39-44). The graph is rewritten to
-  add a scalar ``__ctr_base`` parameter to every Rng counter.
+  add a scalar ``__ctr_base`` parameter (the device's first path) to every
+  per-path Rng counter, scaled by the draw's elements per path, so
+  multi-step grids split correctly too.
 * ``allreduce_mean(names, inputs)`` recombines scalar outputs with one NCCL
   all-reduce over NVLink instead of a host loop.
 * ``allreduce_sum(names, inputs)`` sums whole outputs across the devices on
@@ -38,9 +40,20 @@ from .ir import I32, Graph, Tensor, Value, numel
 CTR_BASE = "__ctr_base"
 
 
-def offset_counters(g: Graph, key: str) -> Graph:
+def offset_counters(g: Graph, key: str, rows: int | None = None) -> Graph:
     """Rewrite every Rng.u32 counter ``map2 f (iota s) (broadcast s key)`` to
-    count from a scalar parameter ``__ctr_base`` (rng.ml:49-59)."""
+    count from a scalar parameter ``__ctr_base`` (rng.ml:49-59).
+
+    ``__ctr_base`` is the first *path* (leading-axis row) the program
+    computes. Rng.u32's counter is the flat element index (the iota of the
+    draw's shape), so a draw of shape ``(paths, k1, ...)`` counts from
+    ``__ctr_base * k1 * ...``: a program built for rows [b, b + paths) draws
+    the same counters as those rows of the unsplit program, also for
+    multi-step grids. A 1-D draw counts from ``__ctr_base`` itself.
+
+    ``rows=None`` offsets every draw keyed by ``key``; with ``rows`` set only
+    draws whose leading dimension equals ``rows`` (the per-device path count)
+    move, and any other draw is shared, as it is in the unsplit program."""
     base = D.scalar(CTR_BASE, I32)
     memo = {}
 
@@ -48,8 +61,10 @@ def offset_counters(g: Graph, key: str) -> Graph:
         if t.kind != "map2":
             return False
         i, k = t.deps
-        return (i.kind == "iota" and k.kind == "broadcast" and k.deps[0].kind == "param"
-                and k.deps[0].name == key)
+        if not (i.kind == "iota" and k.kind == "broadcast" and k.deps[0].kind == "param"
+                and k.deps[0].name == key):
+            return False
+        return rows is None or (len(i.shape) > 0 and i.shape[0] == rows)
 
     def go(t: Tensor) -> Tensor:
         if t.uid in memo:
@@ -57,7 +72,9 @@ def offset_counters(g: Graph, key: str) -> Graph:
         deps = [go(d) for d in t.deps]
         if is_counter(t):
             it = t.deps[0]
-            deps[0] = D.map2(D.add, it, D.broadcast(it.shape, base))
+            row = numel(it.shape[1:])
+            start = base if row == 1 else D.map(lambda b: D.mul(b, D.const(I32, row)), base)
+            deps[0] = D.map2(D.add, it, D.broadcast(it.shape, start))
         if all(a is b for a, b in zip(deps, t.deps)):
             new = t
         else:
@@ -113,7 +130,7 @@ class Multi:
         for ordinal in devices:
             g = build(self.per)
             if counter_key is not None:
-                g = offset_counters(g, counter_key)
+                g = offset_counters(g, counter_key, rows=self.per)
             self.slots.append(B.compile_on(ordinal, g, matmul=matmul))
         self._comms = None
 
