@@ -606,6 +606,29 @@ def test_s19_multi_same_device_and_counter_split():
     assert abs(pm - p1) <= 1e-9 * (1 + abs(p1))
 
 
+def test_s19_multi_counter_split_multistep_grid():
+    # (paths, steps) draws: the counter base is scaled by the steps per path,
+    # so two programs draw exactly the unsplit program's words
+    from cudacaml_b200 import multi as M
+    n, steps = 1 << 12, 8
+    key = D.scalar("seed", I32)
+    words = lambda k: Graph("w", [("w", Rng.u32(key, (k, steps)))])  # noqa: E731
+    c = cuda.compile(words(n))
+    w1 = dict(cuda.run(c, [("seed", Value.of_list(I32, (), [42]))]))["w"].data
+    cuda.release(c)
+    t = M.Multi([0, 0], n, words, counter_key="seed")
+    per = t.run([("seed", Value.of_list(I32, (), [42]))])
+    t.release()
+    assert np.array_equal(M.concat([dict(o)["w"] for o in per]).data, w1)
+    g1 = cuda.compile(X.call_mc_paths(n, steps, F64))
+    p1 = X.scalar_out(cuda.run(g1, X.bs_inputs(F64, seed=42)), "price")
+    cuda.release(g1)
+    t = M.Multi([0, 0], n, lambda k: X.call_mc_paths(k, steps, F64), counter_key="seed")
+    pm = M.mean_scalar([dict(o)["price"] for o in t.run(X.bs_inputs(F64, seed=42))])
+    t.release()
+    assert abs(pm - p1) <= 1e-9 * (1 + abs(p1))
+
+
 @pytest.mark.parametrize("n", [1, 4, 6143, 6144, 6145, 8192, 3 * 6144 + 5, 1 << 16, (1 << 20) + 7])
 def test_flat_scan_tile_edges_i32_exact(n):
     # the staged scan's 6144-element tiles: ragged last tiles, one-tile and
