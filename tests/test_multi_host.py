@@ -101,6 +101,49 @@ def test_multi_slices_inputs_like_one_device(devices, devs):
         t.run([("x", x), ("y", y)])
 
 
+def test_multi_mean_scalar_and_i32_across_device_lists(devices):
+    # test/unit/test_multigpu.ml: 2 * mean of the per-device sums is the
+    # single sum; an I32 program with negative division splits the same on
+    # [0; 0] and [0; 1]
+    n = 8192
+    x = Value.of_array(F32, (n,), np.arange(n, dtype=np.float32))
+    y = Value.of_array(F32, (n,), (n - np.arange(n)).astype(np.float32))
+    s = run(X.saxpy(n, 2.0), [("x", x), ("y", y)])["s"].get(0)
+    t = M.Multi([0, 0], n, lambda k: X.saxpy(k, 2.0))
+    per = t.run([("x", x), ("y", y)])
+    assert len(per) == 2
+    assert abs(2.0 * M.mean_scalar([dict(o)["s"] for o in per]) - s) <= 1e-5 * abs(s)
+    t.release()
+
+    def i32_prog(k):
+        e = D.param("x", I32, (k,))
+        return Graph("i32", [("r", D.map(lambda v: D.div(D.sub(v, D.const(I32, 4)), D.const(I32, 2)), e))])
+
+    xi = Value.of_array(I32, (n,), np.arange(n, dtype=np.int32) - 100)
+    want = run(i32_prog(n), [("x", xi)])["r"].data
+    for devs in ([0, 0], [0, 1]):
+        t = M.Multi(devs, n, i32_prog)
+        got = M.concat([dict(o)["r"] for o in t.run([("x", xi)])]).data
+        t.release()
+        assert np.array_equal(got, want)
+    # truncating division, as the reference's Int32.div: (-101 - 4) / 2 = -52
+    assert want[0] == -52
+
+
+def test_multi_run_per_device_one_seed_each(devices):
+    # test/unit/test_multigpu.ml "per-device inputs": the reference's way to
+    # decorrelate devices is one seed per device; prices differ and each is
+    # within the reference's band of the closed form
+    n = 1 << 14
+    t = M.Multi([0, 0], n, lambda k: X.call_mc(k, F32))
+    per = t.run_per_device(lambda d: X.bs_inputs(F32, seed=d + 1))
+    t.release()
+    prices = [dict(o)["price"].get(0) for o in per]
+    cf = X.analytic()["price"]
+    assert all(abs(p - cf) <= 1.0 for p in prices)
+    assert prices[0] != prices[1]
+
+
 @pytest.mark.parametrize("d", [2, 4])
 def test_multi_counter_split_draws_bit_exact(devices, d):
     # rank-1 and multi-step draws split by path; the shared draw stays whole
