@@ -276,14 +276,31 @@ class Graph:
         raise KeyError(name)
 
     def to_dot(self) -> str:
-        lines = [f'digraph "{self.name}" {{']
+        """Graphviz text in the reference's format (graph.ml:115-150): one
+        node per tensor labelled ``n<uid> <Kind> <shape> <dtype>``, one edge
+        per dependency, names escaped."""
+        lines = [f'digraph "{_dot_escape(self.name)}" {{']
         for t in self.order:
-            lines.append(f'  n{t.uid} [label="n{t.uid} {t.kind} {shape_to_string(t.shape)} {t.dtype.value}"];')
+            label = f"n{t.uid} {_dot_kind(t)} {shape_to_string(t.shape)} {t.dtype.value}"
+            lines.append(f'  n{t.uid} [label="{_dot_escape(label)}"];')
         for t in self.order:
             for d in t.deps:
                 lines.append(f"  n{d.uid} -> n{t.uid};")
         lines.append("}")
         return "\n".join(lines) + "\n"
+
+
+_DOT_KIND = {"iota": "Iota", "map": "Map", "map2": "Map2", "reduce": "Reduce", "scan": "Scan",
+             "gather": "Gather", "scatter_add": "Scatter_add", "matmul": "Matmul", "reshape": "Reshape",
+             "broadcast": "Broadcast"}
+
+
+def _dot_kind(t: Tensor) -> str:
+    return f"Param {t.name}" if t.kind == "param" else _DOT_KIND[t.kind]
+
+
+def _dot_escape(s: str) -> str:
+    return s.replace("\\", "\\\\").replace('"', '\\"').replace("\n", "\\n")
 
 
 # ---------------------------------------------------------------------------
@@ -338,11 +355,17 @@ class Value:
     def byte_size(self) -> int:
         return self.numel * self.dtype.size_in_bytes
 
+    def _index(self, i: int, what: str) -> int:
+        # flat row-major index in [0, numel): no negative (from-the-end) indexing
+        if not 0 <= i < self.data.size:
+            raise IndexError(f"Value.{what}: index {i} out of bounds for {self.data.size} elements")
+        return i
+
     def get(self, i: int):
-        return self.data[i].item()
+        return self.data[self._index(i, "get")].item()
 
     def set(self, i: int, v) -> None:
-        self.data[i] = v
+        self.data[self._index(i, "set")] = v
 
     def to_list(self):
         return self.data.tolist()
