@@ -1,9 +1,11 @@
 """The oracle's evaluation rules pinned by the reference interpreter's own
-known answers (test/unit/test_interp.ml and test_expr_ops.ml, line cited per
-case): element maps, index and iota, the sequential left fold from init,
-empty reductions, inclusive scans, gathers and their bounds, comparisons and
-logic through select, F32 rounding, truncating I32 division, erfinv at the
-edges, and the input checks. CPU only.
+known answers (test/unit/test_interp.ml, test_expr_ops.ml, test_matmul.ml,
+test_rows.ml, test_scatter.ml and test_black_scholes.ml, line cited per case):
+element maps, index and iota, the sequential left fold from init, empty
+reductions, inclusive scans, gathers and their bounds, comparisons and logic
+through select, F32 rounding, truncating I32 division, erfinv at the edges,
+the input checks, products and their gradients, the DSL's rank and shape
+checks, and the multi-step Black-Scholes band. CPU only.
 """
 import math
 
@@ -153,3 +155,74 @@ def test_erfinv_inverts_erf_and_edges():  # test_expr_ops.ml:85-98
     x = D.param("x", F32, (1,))
     v = out(Graph("g", [("r", D.map(D.erfinv, x))]), [("x", f32([0.5]))])[0]
     assert abs(v - 0.4769362762) <= 1e-6
+
+
+def test_matmul_identity_and_5x7_7x3():  # test_matmul.ml:95-100
+    a = [1.0, 2, 3, 4, 5, 6, 7, 8, 9]
+    A, B = D.param("a", F64, (3, 3)), D.param("b", F64, (3, 3))
+    ident = list(np.eye(3).reshape(-1))
+    g = Graph("mm", [("c", D.matmul(A, B))])
+    assert out(g, [("a", Value.of_list(F64, (3, 3), a)), ("b", Value.of_list(F64, (3, 3), ident))], "c") == a
+    av = [float((i * 7) % 11) - 5.0 for i in range(35)]
+    bv = [float((i * 5) % 13) / 4.0 for i in range(21)]
+    A, B = D.param("a", F64, (5, 7)), D.param("b", F64, (7, 3))
+    got = out(Graph("mm", [("c", D.matmul(A, B))]),
+              [("a", Value.of_list(F64, (5, 7), av)), ("b", Value.of_list(F64, (7, 3), bv))], "c")
+    want = (np.array(av).reshape(5, 7) @ np.array(bv).reshape(7, 3)).reshape(-1)
+    assert np.allclose(got, want, rtol=0, atol=1e-12)
+
+
+def test_matmul_shape_checks():  # test_matmul.ml:101-104
+    with pytest.raises(ValueError):
+        D.matmul(D.param("a", F64, (2, 3)), D.param("b", F64, (2, 3)))
+    with pytest.raises(ValueError):
+        D.matmul(D.param("a", F64, (6,)), D.param("b", F64, (6,)))
+    with pytest.raises(ValueError):
+        D.matmul(D.param("a", F64, (2, 2, 2)), D.param("b", F64, (2, 2)))
+
+
+def test_matmul_gradients_by_central_difference():  # test_matmul.ml:140-145
+    from cudacaml_b200 import grad as G
+    ins = [("a", Value.of_list(F64, (2, 3), [1.0, -2.0, 0.5, 3.0, 1.5, -1.0])),
+           ("b", Value.of_list(F64, (3, 2), [0.3, 1.5, -1.0, 2.0, 0.7, -0.2]))]
+    zero = D.const(F64, 0.0)
+    for wrap in (lambda a: a, lambda a: D.map(D.exp, a)):
+        a, b = D.param("a", F64, (2, 3)), D.param("b", F64, (3, 2))
+        g = Graph("g", [("s", D.reduce(D.add, zero, D.matmul(wrap(a), b)))])
+        o = dict(run(G.grad(g, "s", ["a", "b"]), ins))
+        for w in ("a", "b"):
+            base = dict(ins)[w]
+            h = 1e-6
+            for i in range(base.numel):
+                def s_at(delta):
+                    v = base.data.copy()
+                    v[i] += delta
+                    bumped = [(n, Value.of_array(F64, base.shape, v) if n == w else x) for n, x in ins]
+                    return dict(run(g, bumped))["s"].get(0)
+                e = (s_at(h) - s_at(-h)) / (2 * h)
+                assert abs(e - o[G.grad_name("s", w)].get(i)) <= 1e-5 * (1 + abs(e)), (w, i)
+
+
+def test_rows_rank_checks_and_scatter_shapes():  # test_rows.ml:81-87, test_scatter.ml:47-49
+    zero = D.const(F32, 0.0)
+    v = D.param("v", F32, (5,))
+    r3 = D.param("w", F32, (2, 2, 2))
+    for bad in (lambda: D.reduce_rows(D.add, zero, v), lambda: D.scan_rows(D.add, zero, v),
+                lambda: D.transpose(v), lambda: D.transpose(r3)):
+        with pytest.raises(ValueError):
+            bad()
+    with pytest.raises(ValueError):
+        D.scatter_add(D.param("idx", I32, (6,)), D.param("src", F32, (5,)), (4,))
+
+
+def test_bs_paths_band_and_greeks_graph_structure():  # test_black_scholes.ml:24-43
+    from cudacaml_b200 import backend_cuda as B
+    cf = X.analytic()
+    o = dict(run(X.call_mc_paths(16384, 8, F64), X.bs_inputs(F64, seed=42)))
+    assert abs(o["price"].get(0) - cf["price"]) <= 0.5
+    g = X.call_greeks(4096, F64)
+    assert sorted(n for n, _ in g.params) == ["rate", "s0", "seed", "vol"]
+    assert len(g.outputs) == 4
+    assert B.lower_info(g)["kernels"] < 40  # the reference's bound; this backend makes one
+    for name in ("bs_mc", "bs_paths", "bs_greeks"):
+        assert X.find(name) is not None
