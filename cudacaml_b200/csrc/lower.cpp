@@ -75,6 +75,29 @@ static int lookup(const char* const* names, int n, const std::string& s, const c
   bad(std::string("wire: unknown ") + what + " " + s);
   return 0;
 }
+// Names are one token on the wire, '%', whitespace and control bytes written
+// as %XX (two hex digits); decode them back to the caller's bytes.
+static std::string wire_name(const std::string& s) {
+  std::string out;
+  out.reserve(s.size());
+  for (size_t i = 0; i < s.size(); ++i) {
+    if (s[i] != '%') {
+      out += s[i];
+      continue;
+    }
+    auto hex = [&](char c) -> int {
+      if (c >= '0' && c <= '9') return c - '0';
+      if (c >= 'a' && c <= 'f') return c - 'a' + 10;
+      if (c >= 'A' && c <= 'F') return c - 'A' + 10;
+      return -1;
+    };
+    int hi = i + 2 < s.size() ? hex(s[i + 1]) : -1, lo = i + 2 < s.size() ? hex(s[i + 2]) : -1;
+    if (hi < 0 || lo < 0) bad("wire: bad %XX escape in name " + s);
+    out += (char)(hi * 16 + lo);
+    i += 2;
+  }
+  return out;
+}
 static const char* const kBin[] = {"add", "sub", "mul", "div", "min", "max", "bit_and", "bit_or", "bit_xor", "shl", "shr"};
 static const char* const kUn[] = {"neg", "sqrt", "exp", "log", "abs", "sin", "cos", "erf", "erfinv"};
 static const char* const kCmp[] = {"eq", "ne", "lt", "le", "gt", "ge"};
@@ -109,6 +132,7 @@ int parse_graph(const char* text, GGraph& g) {
         header = true;
       } else if (tag == "name") {
         ls >> g.name;
+        g.name = wire_name(g.name);
       } else if (tag == "opt") {
         std::string key, val;
         ls >> key >> val;
@@ -186,7 +210,10 @@ int parse_graph(const char* text, GGraph& g) {
         t.kind = lookup(kTk, 11, kind, "tensor kind");
         int64_t a, b, x, y, z, w;
         switch (t.kind) {
-          case T_PARAM: ls >> t.name; break;
+          case T_PARAM:
+            ls >> t.name;
+            t.name = wire_name(t.name);
+            break;
           case T_IOTA: break;
           case T_MAP:
             ls >> a >> x >> z;
@@ -230,7 +257,7 @@ int parse_graph(const char* text, GGraph& g) {
         std::string nm;
         int64_t id;
         ls >> nm >> id;
-        g.outputs.push_back({nm, T(id)});
+        g.outputs.push_back({wire_name(nm), T(id)});
       } else if (tag == "end") {
         ended = true;
       } else {

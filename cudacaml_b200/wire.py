@@ -27,7 +27,9 @@ every expression node is written once, before its users, under its own id.
     o <output name> <tid>
     end
 
-Tensor lines are in the graph's topological order; names contain no spaces.
+Tensor lines are in the graph's topological order. Names (graph, params,
+outputs) are one token each: '%', whitespace and control characters are
+escaped as %XX per UTF-8 byte, so any non-empty name crosses unchanged.
 """
 from __future__ import annotations
 
@@ -123,6 +125,15 @@ def to_wire(g: Graph, matmul: str = "f32") -> str:
 
 
 def _check_name(n: str) -> str:
-    if not n or any(c.isspace() for c in n):
-        raise ValueError(f"wire: name {n!r} must be non-empty with no whitespace")
-    return n
+    """A name as one whitespace-free token: '%', whitespace and control
+    characters are written as %XX (each UTF-8 byte), every other character
+    as itself, so ordinary names read the same in the text."""
+    if not n:
+        raise ValueError("wire: a name must be non-empty")
+    out = []
+    for c in n:
+        if c == "%" or c.isspace() or ord(c) < 0x20 or ord(c) == 0x7F:
+            out.extend("%%%02X" % b for b in c.encode("utf-8"))
+        else:
+            out.append(c)
+    return "".join(out)

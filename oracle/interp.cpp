@@ -19,6 +19,7 @@
 // takes, ml:255-256) with a per-element memo over the expression DAG.
 //
 // Build: see oracle/Makefile (g++ -O2 -ffp-contract=off, no fast-math).
+#include <cctype>
 #include <cmath>
 #include <cstdint>
 #include <cstring>
@@ -191,6 +192,23 @@ struct Graph {
 };
 
 // ---------------------------------------------------------------- parsing
+// A name is one token on the wire with '%', whitespace and control bytes
+// written as %XX; decode it back to the caller's bytes.
+std::string wire_name(const std::string& s) {
+  std::string out;
+  for (size_t i = 0; i < s.size(); ++i) {
+    if (s[i] != '%') {
+      out += s[i];
+      continue;
+    }
+    if (i + 2 >= s.size() || !std::isxdigit((unsigned char)s[i + 1]) || !std::isxdigit((unsigned char)s[i + 2]))
+      throw std::runtime_error("oracle: bad %XX escape in name " + s);
+    out += (char)std::stoi(s.substr(i + 1, 2), nullptr, 16);
+    i += 2;
+  }
+  return out;
+}
+
 void parse(Graph& g, const char* text) {
   std::istringstream in(text);
   std::string line;
@@ -215,6 +233,7 @@ void parse(Graph& g, const char* text) {
       header = true;
     } else if (tag == "name") {
       ls >> g.name;
+      g.name = wire_name(g.name);
     } else if (tag == "e") {
       int64_t id;
       std::string dts, kind;
@@ -270,6 +289,7 @@ void parse(Graph& g, const char* text) {
       int64_t a, b, x, y, z, w;
       if (t.kind == "param") {
         ls >> t.name;
+        t.name = wire_name(t.name);
       } else if (t.kind == "iota") {
       } else if (t.kind == "map") {
         ls >> a >> x >> z;
@@ -304,7 +324,7 @@ void parse(Graph& g, const char* text) {
       std::string nm;
       int64_t id;
       ls >> nm >> id;
-      g.outputs.push_back({nm, T(id)});
+      g.outputs.push_back({wire_name(nm), T(id)});
     } else if (tag == "end") {
       ended = true;
     } else {

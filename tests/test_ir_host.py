@@ -178,3 +178,46 @@ def test_broadcast_deps_and_dot_name():
     b = D.broadcast((4,), s)
     assert len(b.deps) == 1 and b.deps[0].uid == s.uid
     assert "Broadcast" in Graph("b", [("r", b)]).to_dot()
+
+
+# ---------------------------------------------------------------------------
+# Names cross the wire unchanged
+# ---------------------------------------------------------------------------
+ODD_NAMES = ["spot price", "a%b", "tab\there", "two\nlines", "prix €", "dloss/dW1"]
+
+
+def test_wire_escapes_only_what_must_be_escaped():
+    from cudacaml_b200.wire import to_wire
+    x = D.param("spot price", F32, (2,))
+    text = to_wire(Graph("my graph", [("dloss/dW1", D.map(D.neg, x)), ("50%", x)]))
+    assert "name my%20graph" in text.splitlines()
+    assert any(line.endswith("param spot%20price") for line in text.splitlines())
+    assert any(line.startswith("o dloss/dW1 ") for line in text.splitlines())
+    assert any(line.startswith("o 50%25 ") for line in text.splitlines())
+    with pytest.raises(ValueError):
+        to_wire(Graph("g", [("", x)]))
+
+
+@pytest.mark.parametrize("name", ODD_NAMES)
+def test_any_name_round_trips_through_the_oracle_and_lowering(name):
+    x = D.param(name, F32, (3,))
+    g = Graph(name, [("out " + name, D.map(D.neg, x)), (name + " sum", D.reduce(D.add, D.const(F32, 0.0), x))])
+    o = I.run(I.compile(g), [(name, Value.of_list(F32, (3,), [1.0, 2.0, 3.0]))])
+    assert [n for n, _ in o] == ["out " + name, name + " sum"]
+    assert dict(o)["out " + name].to_list() == [-1.0, -2.0, -3.0]
+    info = B.lower_info(g)
+    assert info["kernels"] == 1
+    assert f"upload {name} ->" in info["plan"]
+
+
+def test_malformed_escapes_are_rejected():
+    import ctypes
+    from cudacaml_b200 import runtime as R
+    for bad in (b"x%G1", b"x%4", b"x%"):
+        text = b"ccbgraph 1\nname g\nt 1 f32 1 4 param " + bad + b"\no r 1\nend\n"
+        h = ctypes.c_void_p()
+        assert R.lib().ccb_program_lower(text, ctypes.byref(h)) != 0
+        assert "escape" in R.lib().ccb_last_error().decode()
+        err = ctypes.create_string_buffer(1024)
+        assert not I.lib().ccbo_load(text, err, 1024)
+        assert "escape" in err.value.decode()
