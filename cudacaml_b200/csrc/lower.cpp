@@ -1718,7 +1718,9 @@ class Lowerer {
       Group& mm = groups[gi];
       Group& ep = groups[gi + 1];
       if (ep.kind != G_MAPRED) continue;
+      if (mm.kind != G_MATMUL_TC && mm.kind != G_SCAN_ROWS && mm.kind != G_SCAN_FLAT) continue;
       const int t = mm.root;
+      if (t < 0) continue;
       const int64_t MN = g.ts[t].numel;
       if (mm.kind == G_MATMUL_TC) {
         if (g.ts[g.ts[t].dep0].shape[1] < kEpiMinK) continue;
