@@ -1,5 +1,6 @@
 """``Differential.check``: run a graph on a reference backend and a candidate
-and compare every output by name (lib/backend/differential.ml:80-88).
+and compare every output by name (lib/backend/differential.ml:80-88), with
+the reference's mismatch messages (differential.ml:36-61).
 
 Floats use the relative-plus-absolute band |g - e| <= tol * (1 + |e|) with
 NaN == NaN (differential.ml:6-8); integers must be exactly equal
@@ -8,6 +9,8 @@ NaN == NaN (differential.ml:6-8); integers must be exactly equal
 from __future__ import annotations
 
 import numpy as np
+
+from .ir import shape_to_string
 
 
 def float_close(tolerance: float, e, g):
@@ -23,14 +26,15 @@ def compare_one(tolerance, output, e, g):
     if e.dtype is not g.dtype:
         return f"output {output}: dtype mismatch: expected {e.dtype.value}, got {g.dtype.value}"
     if tuple(e.shape) != tuple(g.shape):
-        return f"output {output}: shape mismatch: expected {list(e.shape)}, got {list(g.shape)}"
+        return (f"output {output}: shape mismatch: expected {shape_to_string(e.shape)}, "
+                f"got {shape_to_string(g.shape)}")
     if e.dtype.is_float:
         ok = float_close(tolerance, e.data, g.data)
     else:
         ok = e.data == g.data
     if not np.all(ok):
         i = int(np.argmin(ok))
-        return f"output {output}[{i}]: expected {e.data[i]!r}, got {g.data[i]!r} (tol {tolerance:g})"
+        return f"output {output}[{i}]: expected {float(e.data[i]):g}, got {float(g.data[i]):g} (tol {tolerance:g})"
     return None
 
 
