@@ -76,8 +76,10 @@ static int lookup(const char* const* names, int n, const std::string& s, const c
   return 0;
 }
 // Names are one token on the wire, '%', whitespace and control bytes written
-// as %XX (two hex digits); decode them back to the caller's bytes.
+// as %XX (two hex digits), the empty name as a lone '%'; decode them back to
+// the caller's bytes.
 static std::string wire_name(const std::string& s) {
+  if (s == "%") return std::string();
   std::string out;
   out.reserve(s.size());
   for (size_t i = 0; i < s.size(); ++i) {

@@ -29,7 +29,8 @@ every expression node is written once, before its users, under its own id.
 
 Tensor lines are in the graph's topological order. Names (graph, params,
 outputs) are one token each: '%', whitespace and control characters are
-escaped as %XX per UTF-8 byte, so any non-empty name crosses unchanged.
+escaped as %XX per UTF-8 byte, and the empty name is the lone token %, so
+any name crosses unchanged.
 """
 from __future__ import annotations
 
@@ -127,9 +128,10 @@ def to_wire(g: Graph, matmul: str = "f32") -> str:
 def _check_name(n: str) -> str:
     """A name as one whitespace-free token: '%', whitespace and control
     characters are written as %XX (each UTF-8 byte), every other character
-    as itself, so ordinary names read the same in the text."""
+    as itself, so ordinary names read the same in the text. The empty name
+    is the lone token '%' (a literal '%' is always '%25')."""
     if not n:
-        raise ValueError("wire: a name must be non-empty")
+        return "%"
     out = []
     for c in n:
         if c == "%" or c.isspace() or ord(c) < 0x20 or ord(c) == 0x7F:

@@ -193,8 +193,10 @@ struct Graph {
 
 // ---------------------------------------------------------------- parsing
 // A name is one token on the wire with '%', whitespace and control bytes
-// written as %XX; decode it back to the caller's bytes.
+// written as %XX and the empty name as a lone '%'; decode it back to the
+// caller's bytes.
 std::string wire_name(const std::string& s) {
+  if (s == "%") return std::string();
   std::string out;
   for (size_t i = 0; i < s.size(); ++i) {
     if (s[i] != '%') {
