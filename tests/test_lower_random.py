@@ -1,5 +1,5 @@
-"""Seeded random graphs through the native lowering, NVRTC for sm_100a and
-the oracle, and mutated wire text through both parsers.
+"""Seeded random graphs and zero-size tensors through the native lowering,
+NVRTC for sm_100a and the oracle, and mutated wire text through both parsers.
 
 Every random graph must lower; a sample of them must compile for sm_100a;
 the oracle must evaluate them, outputs in the graph's order. Mutated graph
@@ -177,3 +177,35 @@ def test_mutated_wire_text_is_lowered_or_refused(seed):
             else:
                 assert err.value
     assert refused > 0
+
+
+def zero_size_graphs():
+    z = D.const(F32, 0.0)
+    x0 = D.param("x", F32, (0,))
+    out = [("map", Graph("g", [("r", D.map(D.neg, x0)), ("s", D.reduce(D.add, D.const(F32, 5.0), x0))])),
+           ("scan", Graph("g", [("p", D.scan(D.add, z, x0))])),
+           ("gather", Graph("g", [("r", D.gather(D.param("i", I32, (0,)), D.param("x", F32, (5,))))])),
+           ("scatter", Graph("g", [("h", D.scatter_add(D.param("i", I32, (0,)), x0, (4,)))]))]
+    for r, c in ((0, 4), (4, 0), (0, 0)):
+        m = D.param("m", F32, (r, c))
+        out.append((f"rows{r}x{c}", Graph("g", [("r", D.reduce_rows(D.add, D.const(F32, 2.0), m)),
+                                                  ("q", D.scan_rows(D.add, z, m)), ("t", D.transpose(m))])))
+    for mm, k, n in ((0, 4, 3), (3, 0, 3), (3, 4, 0), (256, 0, 256)):
+        out.append((f"matmul{mm}x{k}x{n}", Graph("g", [("c", D.matmul(D.param("a", F32, (mm, k)),
+                                                                      D.param("b", F32, (k, n))))])))
+    return out
+
+
+@pytest.mark.parametrize("name,g", zero_size_graphs(), ids=[n for n, _ in zero_size_graphs()])
+def test_zero_size_tensors_lower_compile_and_evaluate(name, g):
+    # the reference's rules at size 0: a reduction is its init (row by row
+    # for [rows; 0]), a product over K = 0 is zeros, everything else is empty
+    assert B.lower_info(g)["kernels"] >= 1
+    nvrtc_compiles(g)
+    out = dict(I.run(I.compile(g), [(n, Value.create(t.dtype, t.shape)) for n, t in g.params]))
+    if name == "map":
+        assert out["r"].shape == (0,) and out["s"].to_list() == [5.0]
+    if name == "rows4x0":
+        assert out["r"].to_list() == [2.0] * 4 and out["q"].shape == (4, 0) and out["t"].shape == (0, 4)
+    if name.startswith("matmul"):
+        assert not np.any(out["c"].data)
