@@ -3,8 +3,8 @@ NVRTC for sm_100a and the oracle, and mutated wire text through both parsers.
 
 Every random graph must lower; a sample of them must compile for sm_100a;
 the oracle must evaluate them, outputs in the graph's order. Mutated graph
-text must come back as either
-a lowered program or an error status, never a crash. CPU only.
+text must come back as either a lowered program or an error status, never a
+crash. CPU only.
 """
 import ctypes
 import random
