@@ -149,31 +149,35 @@ __device__ __forceinline__ void map_reduce(const typename F::P& p) {
   constexpr int R = F::NRED;
   T acc[R > 0 ? R : 1];
   F::init(acc);
-  const int n = (int)p.n;
-  const int tid = blockIdx.x * blockDim.x + threadIdx.x;
-  const int nth = gridDim.x * blockDim.x;
+  // Indices are unsigned: n < 2^31 (element indices are int32) and a
+  // grid-stride step adds far less than 2^31, so `i + step` never wraps
+  // before the bound check. A signed index would overflow past INT_MAX for n
+  // near 2^31 and pass `i < n` with a negative value.
+  const unsigned n = (unsigned)p.n;
+  const unsigned tid = blockIdx.x * blockDim.x + threadIdx.x;
+  const unsigned nth = gridDim.x * blockDim.x;
   if (F::VEC && F::vec_ok(p)) {
-    constexpr int U = F::UNROLL;
-    const int n4 = n >> 2;
-    int g = tid;
+    constexpr unsigned U = F::UNROLL;
+    const unsigned n4 = n >> 2;
+    unsigned g = tid;
     for (; g + (U - 1) * nth < n4; g += U * nth) {
 #pragma unroll
-      for (int u = 0; u < U; ++u) F::elem4(p, (g + u * nth) << 2, acc);
+      for (unsigned u = 0; u < U; ++u) F::elem4(p, (int)((g + u * nth) << 2), acc);
     }
-    for (; g < n4; g += nth) F::elem4(p, g << 2, acc);
-    for (int i = (n4 << 2) + tid; i < n; i += nth) F::elem(p, i, acc);
+    for (; g < n4; g += nth) F::elem4(p, (int)(g << 2), acc);
+    for (unsigned i = (n4 << 2) + tid; i < n; i += nth) F::elem(p, (int)i, acc);
   } else if constexpr (F::VEC == 0 && F::PAIRS) {
     // two independent elements per iteration: two dependency chains for
     // the scheduler, three copies of the body; each thread still folds its
     // elements in the same order
-    int i = tid;
+    unsigned i = tid;
     for (; i + nth < n; i += 2 * nth) {
-      F::elem(p, i, acc);
-      F::elem(p, i + nth, acc);
+      F::elem(p, (int)i, acc);
+      F::elem(p, (int)(i + nth), acc);
     }
-    if (i < n) F::elem(p, i, acc);
+    if (i < n) F::elem(p, (int)i, acc);
   } else {
-    for (int i = tid; i < n; i += nth) F::elem(p, i, acc);
+    for (unsigned i = tid; i < n; i += nth) F::elem(p, (int)i, acc);
   }
   if constexpr (R > 0) {
     reduce_finish<F>(p, acc);
