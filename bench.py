@@ -605,7 +605,7 @@ def run_ours(args):
     def flush(s):
         rc = R.lib().ccb_sum_f32_noalloc(flush_buf.ptr, flush_n, flush_out.ptr, s)
         if rc != 0:
-            raise RuntimeError(R.lib().ccb_noalloc_last_error().decode())
+            raise RuntimeError(R.lib().ccb_last_error().decode())
 
     head = measure_greeks(args, F64, rank, world, local, dist, comm, flush)
     cf = X.analytic()

@@ -73,6 +73,7 @@ const Driver& driver() {
     S(cuModuleUnload, "cuModuleUnload")
     S(cuModuleGetFunction, "cuModuleGetFunction")
     S(cuLaunchKernel, "cuLaunchKernel")
+    S(cuFuncGetParamInfo, "cuFuncGetParamInfo")
     S(cuFuncSetAttribute, "cuFuncSetAttribute")
     S(cuFuncGetAttribute, "cuFuncGetAttribute")
     S(cuOccupancyMaxActiveBlocksPerMultiprocessor, "cuOccupancyMaxActiveBlocksPerMultiprocessor")

@@ -50,6 +50,7 @@ struct Driver {
   CCB_DRV(cuModuleUnload)
   CCB_DRV(cuModuleGetFunction)
   CCB_DRV(cuLaunchKernel)
+  CCB_DRV(cuFuncGetParamInfo)
   CCB_DRV(cuFuncSetAttribute)
   CCB_DRV(cuFuncGetAttribute)
   CCB_DRV(cuOccupancyMaxActiveBlocksPerMultiprocessor)

@@ -24,7 +24,13 @@
 //    no ordering between them) race on it and produce wrong sums;
 //  * the first call on a device does the set-up for that device
 //    (cudaGetSymbolAddress of the array and an occupancy query); make that
-//    first call before any stream capture begins.
+//    first call before any stream capture begins;
+//  * the device address found at set-up is kept for the life of the process:
+//    after a reset of a device's primary context (cudaDeviceReset,
+//    cuDevicePrimaryCtxReset) it is stale, so do not call this entry point on
+//    a device whose context was reset since its first call.
+// Errors are reported like every other entry point of the library: an int
+// status and the message of ccb_last_error() on the calling thread.
 #include <cuda_runtime.h>
 
 #include <mutex>
@@ -32,16 +38,20 @@
 
 #include "ccb_skel.cuh"
 
+namespace ccb {
+void set_error(const std::string& msg);  // the library's thread-local message (runtime.cpp)
+}
+
 namespace {
 
 constexpr int kMaxBlocks = 4096;
 constexpr int kBlock = 256;
 
-// [0, kMaxBlocks) float partials, then the ticket, then the error word.
+// [0, kMaxBlocks) float partials, then the last-block ticket. A sum reads
+// no data-dependent index and waits on nothing, so it has no error word.
 struct Scratch {
   float partials[kMaxBlocks];
   unsigned ticket;
-  unsigned err;
 };
 static __device__ __align__(256) Scratch g_scratch;
 
@@ -51,7 +61,6 @@ struct FSum {
     float* __restrict__ out;
     float* partials;
     unsigned* ticket;
-    unsigned* err;
     long long n;
   };
   typedef float acc_t;
@@ -85,10 +94,10 @@ struct DeviceSetup {
 constexpr int kMaxDevices = 64;
 DeviceSetup g_setup[kMaxDevices];
 std::mutex g_mu;
-thread_local std::string g_err;
 
+// Status codes as in ccb.h: CCB_ERR_INVALID 1, CCB_ERR_NO_DEVICE 2, CCB_ERR_DRIVER 3.
 int fail(int code, const std::string& m) {
-  g_err = m;
+  ccb::set_error(m);
   return code;
 }
 
@@ -121,8 +130,6 @@ int setup(int dev, DeviceSetup** out) {
 
 extern "C" {
 
-const char* ccb_noalloc_last_error(void) { return g_err.c_str(); }
-
 int ccb_sum_f32_noalloc(const float* x, long long n, float* out, void* stream) {
   if (n < 0 || n > 2147483647LL)
     return fail(1, "ccb_sum_f32_noalloc: n = " + std::to_string(n) + " is outside [0, 2^31 - 1] (int32 element indices)");
@@ -136,14 +143,13 @@ int ccb_sum_f32_noalloc(const float* x, long long n, float* out, void* stream) {
   if (rc) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   // The ticket must start at zero; the array keeps whatever the last call left.
-  e = cudaMemsetAsync(&s->scratch->ticket, 0, 2 * sizeof(unsigned), st);
+  e = cudaMemsetAsync(&s->scratch->ticket, 0, sizeof(unsigned), st);
   if (e != cudaSuccess) return fail(3, std::string("cudaMemsetAsync: ") + cudaGetErrorString(e));
   FSum::P p;
   p.x = x;
   p.out = out;
   p.partials = s->scratch->partials;
   p.ticket = &s->scratch->ticket;
-  p.err = &s->scratch->err;
   p.n = n;
   long long want = (n + (long long)kBlock * 8 - 1) / ((long long)kBlock * 8);
   if (want < 1) want = 1;

@@ -395,9 +395,31 @@ int ccb_module_get_function(ccb_module_t mod, const char* name, ccb_function_t* 
   return CCB_OK;
 }
 
+// The kernel's parameter count, from the loaded function's own metadata:
+// cuFuncGetParamInfo answers for every index below the count and refuses the
+// first one past it.
+static int param_count(CUfunction f, int* count) {
+  const Driver& d = driver();
+  int k = 0;
+  for (;; ++k) {
+    size_t off = 0, sz = 0;
+    if (d.cuFuncGetParamInfo(f, (size_t)k, &off, &sz) != CUDA_SUCCESS) break;
+    if (k > 4096) return fail(CCB_ERR_DRIVER, "cuFuncGetParamInfo: parameter count not found");
+  }
+  *count = k;
+  return CCB_OK;
+}
+
 int ccb_launch(ccb_function_t fn, unsigned gx, unsigned gy, unsigned gz, unsigned bx, unsigned by, unsigned bz,
-               unsigned smem, ccb_stream_t s, void** args) {
+               unsigned smem, ccb_stream_t s, void** args, int nargs) {
   CCB_TRY(ensure_current());
+  if (!fn) return fail(CCB_ERR_INVALID, "ccb_launch: null function");
+  if (nargs < 0 || (nargs > 0 && !args)) return fail(CCB_ERR_INVALID, "ccb_launch: bad argument block");
+  int want = 0;
+  CCB_TRY(param_count((CUfunction)fn, &want));
+  if (want != nargs)
+    return fail(CCB_ERR_INVALID, "ccb_launch: the kernel takes " + std::to_string(want) + " arguments, " +
+                                     std::to_string(nargs) + " given");
   CCB_CU(driver().cuLaunchKernel((CUfunction)fn, gx, gy, gz, bx, by, bz, smem, (CUstream)s, args, nullptr));
   return CCB_OK;
 }

@@ -81,7 +81,7 @@ def _declare(L):
         "ccb_module_compile": (I, [c.c_char_p, c.c_char_p, c.POINTER(P), c.POINTER(c.c_void_p)]),
         "ccb_module_unload": (I, [P]),
         "ccb_module_get_function": (I, [P, c.c_char_p, c.POINTER(P)]),
-        "ccb_launch": (I, [P, c.c_uint, c.c_uint, c.c_uint, c.c_uint, c.c_uint, c.c_uint, c.c_uint, P, c.POINTER(P)]),
+        "ccb_launch": (I, [P, c.c_uint, c.c_uint, c.c_uint, c.c_uint, c.c_uint, c.c_uint, c.c_uint, P, c.POINTER(P), I]),
         "ccb_nvrtc_check": (I, [c.c_char_p, c.c_char_p, c.POINTER(SZ), c.POINTER(c.c_void_p)]),
         "ccb_free_string": (None, [c.c_void_p]),
         "ccb_program_create": (I, [c.c_char_p, I, I, c.POINTER(P)]),
@@ -111,7 +111,6 @@ def _declare(L):
         "ccb_comm_destroy": (I, [P]),
         "ccb_allreduce": (I, [P, P, P, SZ, I, I, P]),
         "ccb_sum_f32_noalloc": (I, [P, c.c_longlong, P, P]),
-        "ccb_noalloc_last_error": (c.c_char_p, []),
         "ccb_group_start": (I, []),
         "ccb_group_end": (I, []),
         "ccb_graph_begin": (I, [P]),

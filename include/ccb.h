@@ -90,14 +90,17 @@ int ccb_stream_wait_event(ccb_stream_t s, ccb_event_t e);
 /* ---------------------------------------------------------------- modules
  * Replaces lib/runtime/jit.mli and lib/runtime/launch.mli: NVRTC for sm_100a
  * with the skeleton header on the include path, cuModuleLoadData, and a
- * launch that takes a by-value argument block. */
+ * launch that takes a by-value argument block (Launch.run's `args` list,
+ * lib/runtime/launch.ml:9-13): `args[i]` points at the value of parameter i
+ * and `nargs` is the list's length, checked against the kernel's own
+ * parameter count (CCB_ERR_INVALID when they differ, before any launch). */
 typedef void* ccb_module_t;
 typedef void* ccb_function_t;
 int ccb_module_compile(const char* source, const char* name, ccb_module_t* mod, char** log);
 int ccb_module_unload(ccb_module_t mod);
 int ccb_module_get_function(ccb_module_t mod, const char* name, ccb_function_t* fn);
 int ccb_launch(ccb_function_t fn, unsigned gx, unsigned gy, unsigned gz, unsigned bx, unsigned by,
-               unsigned bz, unsigned smem, ccb_stream_t s, void** args);
+               unsigned bz, unsigned smem, ccb_stream_t s, void** args, int nargs);
 /* Compile source to an sm_100a CUBIN without loading it (works without a GPU). */
 int ccb_nvrtc_check(const char* source, const char* name, size_t* cubin_bytes, char** log);
 void ccb_free_string(char* s);
@@ -194,10 +197,12 @@ int ccb_graph_destroy(ccb_graph_t graph);
  * plus a ticket, about 16 KiB) is held by every GPU that loads the library
  * until exit and is shared by all calls on a device: calls that overlap on
  * the GPU race and give wrong sums. The first call on a device does that
- * device's set-up; make it before any stream capture. Errors: 1 invalid
- * argument, 2 no device, 3 CUDA error; message in ccb_noalloc_last_error(). */
+ * device's set-up (it finds the array's device address once and keeps it);
+ * make it before any stream capture, and do not call the entry point on a
+ * device whose primary context was reset since then (cudaDeviceReset): the
+ * kept address is stale. Errors: CCB_ERR_INVALID, CCB_ERR_NO_DEVICE,
+ * CCB_ERR_DRIVER, with the message in ccb_last_error(). */
 int ccb_sum_f32_noalloc(const float* x, long long n, float* out, void* stream);
-const char* ccb_noalloc_last_error(void);
 
 /* ---------------------------------------------------------------- NCCL
  * New: the reference has no collective (lib/backend_cuda/multi.ml:51-109

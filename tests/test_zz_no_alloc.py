@@ -7,8 +7,10 @@ device pointers but no allocator. For them, ccb_sum_f32_noalloc computes the
 same flat F32 sum as a compiled `reduce add` graph, with its scratch in a
 fixed device array instead of an allocation. This checks it through the C-ABI
 against the regular entry point (ccb_program_run_device) on two calls in a
-row, with the tolerance the other F32-sum tests use. It is collected last so
-that a run stopping at its first failure has run every other test already.
+row, with the tolerance the other F32-sum tests use, and checks with the
+driver's own count of free device memory (cuMemGetInfo) that calls after the
+first allocate nothing. It is collected last so that a run stopping at its
+first failure has run every other test already.
 """
 import ctypes
 
@@ -26,8 +28,17 @@ TOL = 1e-5  # Differential's default band, |g - e| <= tol * (1 + |e|)
 
 def _noalloc_sum(x_ptr, n, out_ptr):
     rc = R.lib().ccb_sum_f32_noalloc(x_ptr, n, out_ptr, None)
-    assert rc == 0, R.lib().ccb_noalloc_last_error().decode()
+    assert rc == 0, R.lib().ccb_last_error().decode()
     R.check(R.lib().ccb_stream_synchronize(None))
+
+
+def _free_device_bytes():
+    """Free memory of the current device as the driver counts it. Any device
+    allocation (cudaMalloc takes at least a 2 MiB page) lowers it."""
+    cu = ctypes.CDLL("libcuda.so.1")
+    free, total = ctypes.c_size_t(), ctypes.c_size_t()
+    assert cu.cuMemGetInfo_v2(ctypes.byref(free), ctypes.byref(total)) == 0
+    return free.value
 
 
 def test_noalloc_sum_matches_program_path_twice():
@@ -38,6 +49,9 @@ def test_noalloc_sum_matches_program_path_twice():
     ref_out = R.Buffer(4)
     out = R.Buffer(4)
     try:
+        # The first call on a device does its set-up (the runtime may load the
+        # module that holds the scratch array); from then on nothing allocates.
+        _noalloc_sum(x.ptr, 1, out.ptr)
         for call, seed in enumerate((3, 11)):
             host = X.philox_normal(seed, n)
             x.upload(host)
@@ -45,9 +59,10 @@ def test_noalloc_sum_matches_program_path_twice():
             cuda.check_device(c, None)
             want = np.empty(1, np.float32)
             ref_out.download(want)
-            live = R.live_count()
+            live, free = R.live_count(), _free_device_bytes()
             _noalloc_sum(x.ptr, n, out.ptr)
             assert R.live_count() == live
+            assert _free_device_bytes() == free, "the no-allocation sum allocated device memory"
             got = np.empty(1, np.float32)
             out.download(got)
             e, g = float(want[0]), float(got[0])
@@ -75,7 +90,9 @@ def test_noalloc_sum_edge_sizes_and_limit():
             assert float(got[0]) == float(sum(range(n)))
         rc = R.lib().ccb_sum_f32_noalloc(x.ptr, 1 << 31, out.ptr, None)
         assert rc == 1
-        assert "2^31" in R.lib().ccb_noalloc_last_error().decode()
+        assert "2^31" in R.lib().ccb_last_error().decode()
+        assert R.lib().ccb_sum_f32_noalloc(None, 5, out.ptr, None) == 1
+        assert "null pointer" in R.lib().ccb_last_error().decode()
     finally:
         x.free()
         out.free()
