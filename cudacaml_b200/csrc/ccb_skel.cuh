@@ -27,7 +27,15 @@ typedef long long i64;
 
 enum : unsigned { ERR_GATHER_OOB = 1u, ERR_SCATTER_OOB = 2u, ERR_LOOKBACK = 4u };
 constexpr unsigned FULL = 0xffffffffu;
-constexpr unsigned LOOKBACK_SPIN_LIMIT = 1u << 21;
+// Poll limits of the bounded waits. A translation unit may set smaller ones
+// before including this header (the tests that make a wait run out do).
+#ifndef CCB_LOOKBACK_SPIN_LIMIT
+#define CCB_LOOKBACK_SPIN_LIMIT (1u << 21)
+#endif
+#ifndef CCB_MBAR_SPIN_LIMIT
+#define CCB_MBAR_SPIN_LIMIT (1u << 22)
+#endif
+constexpr unsigned LOOKBACK_SPIN_LIMIT = CCB_LOOKBACK_SPIN_LIMIT;
 
 __device__ __forceinline__ void raise_error(unsigned* err, unsigned code) { atomicOr(err, code); }
 
@@ -451,7 +459,7 @@ __device__ __forceinline__ void scan_flat(const typename F::P& p) {
 // F provides T (4 bytes), identity(), combine(a,b), src(p), dst(p); P provides
 // n, tile_counter, done_counter, status, epoch, err.
 constexpr unsigned ERR_TMA = 8u;
-constexpr unsigned MBAR_SPIN_LIMIT = 1u << 22;
+constexpr unsigned MBAR_SPIN_LIMIT = CCB_MBAR_SPIN_LIMIT;
 
 __device__ __forceinline__ unsigned smem_u32(const void* ptr) { return (unsigned)__cvta_generic_to_shared(ptr); }
 __device__ __forceinline__ void mbar_init(u64* bar, unsigned count) {

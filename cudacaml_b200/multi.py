@@ -85,6 +85,21 @@ def offset_counters(g: Graph, key: str, rows: int | None = None) -> Graph:
     return Graph(g.name, [(n, go(t)) for n, t in g.outputs])
 
 
+def path_range(n: int, d: int, i: int) -> tuple[int, int]:
+    """Device ``i`` of ``d``'s share of ``n`` paths: ``(first path, count)``,
+    the counters ``[i*n/d, (i+1)*n/d)``. Rng counters are I32 element indices,
+    so the whole range must stay below 2^31; a larger one would wrap and
+    repeat draws, and is refused instead."""
+    if d <= 0 or not 0 <= i < d:
+        raise ValueError(f"Multi: device {i} of {d}")
+    if n % d != 0:
+        raise ValueError(f"Multi.create: n = {n} is not divisible by {d} devices")
+    per = n // d
+    if n > 1 << 31:
+        raise ValueError(f"Multi: {n} paths exceed the I32 counter range (2^31)")
+    return i * per, per
+
+
 def concat(values):
     """Concatenate along the leading axis (multi.ml:51-92)."""
     if not values:
@@ -120,6 +135,8 @@ class Multi:
             raise ValueError("Multi.create: devices must not be empty")
         if n % d != 0:
             raise ValueError(f"Multi.create: n = {n} is not divisible by {d} devices")
+        if counter_key is not None:
+            path_range(n, d, 0)  # the split counter range must fit the I32 counters
         self.devices = devices
         self.n = n
         self.per = n // d
@@ -152,7 +169,8 @@ class Multi:
             else:
                 out.append((name, v))
         if self.counter_key is not None:
-            out.append((CTR_BASE, Value.of_list(I32, (), [i * self.per])))
+            base, _ = path_range(self.n, len(self.devices), i)
+            out.append((CTR_BASE, Value.of_list(I32, (), [base])))
         return out
 
     def run_per_device(self, inputs_fn):
