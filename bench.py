@@ -1,19 +1,28 @@
 #!/usr/bin/env python3
 """Benchmark: Black-Scholes Monte-Carlo price with pathwise Greeks (Grad.grad
-wrt s0, vol, rate), 2^28 paths per GPU, F64 (F32 reported alongside) -- the
+wrt s0, vol, rate) over 2^28 paths, F64 (F32 reported alongside) -- the
 configuration the reference metric "MC paths/s" is quoted on (BASELINE
 configs[1]). F64 is the headline because at 2^28 paths the reference's own F32
-normal generator produces a few infinite normals (see "secondary"). One step = one run of
-the Greeks graph (one fused forward+adjoint launch) over 2^28 paths, plus, on
-N > 1 GPUs, the NCCL all-reduce that recombines the four scalar outputs.
+normal generator produces a few infinite normals (see "secondary"). One step =
+one run of the Greeks graph (one fused forward+adjoint launch) plus, on N > 1
+GPUs, the NCCL all-reduce that recombines the four scalar outputs.
 
-Scaling is weak: rank r draws Philox counters [r*2^28, (r+1)*2^28) with the
-same seed, so N GPUs price N*2^28 distinct paths.
+Scaling is strong, as BASELINE configs[1] states it: the 2^28 paths are split
+N ways by counter range with the same seed, rank r pricing counters
+[r*2^28/N, (r+1)*2^28/N) -- the split Multi(..., counter_key="seed") makes
+(multi.path_range). Weak scaling (2^28 paths per rank) is reported under
+"secondary" for N > 1.
+
+`value` is device-timed with the inputs resident; `e2e` is the same metric
+through the plugin call a user makes, ccb_program_enqueue + ccb_program_wait
+with page-locked host inputs and outputs (Backend_cuda.run_async/wait), plus
+on N > 1 the all-reduce of the downloaded results, every step.
 
 Also measured in the same run (reported under "secondary"): the flat reduce
-and inclusive scan over 2^28 F32 values (HBM GB/s as a fraction of the
-measured copy peak), the other half of the reference metric. L2 is flushed
-before every timed step by a read-only pass over 256 MiB (twice the L2).
+and inclusive scan over 2^28 values, F32 ~N(0,1) and I32 U[0,16) (HBM GB/s as
+a fraction of the measured copy peak), and every other BASELINE
+configuration. L2 is flushed before every timed step by a read-only pass over
+256 MiB (twice the L2).
 
 --impl reference times the reference algorithm on the host cores: the oracle
 (the C++ restatement of the reference interpreter, the only runnable form of
@@ -36,7 +45,13 @@ sys.path.insert(0, ROOT)
 
 PATHS = 1 << 28
 SEED = 42
-SLOTS_PER_PATH_F64 = 300  # FP32-issue-slot equivalents per F64 path (Philox ~100 int, ~100 FP64 ops x2)
+# Warp instructions executed per path by the fused F64 Greeks kernel, from
+# ncu's smsp__inst_executed.sum over 2^20 paths (9,322,613 / 2^20):
+# profiles/mapreduce_bs_greeks_f64_2p20_instructions.md.
+INST_PER_PATH_F64 = 9322613 / (1 << 20)
+# DRAM bytes per launch of the same kernel (read 44,288, write 0; constant in
+# the path count), same capture.
+DRAM_BYTES_GREEKS_F64 = 44288
 
 
 def peaks():
@@ -140,9 +155,11 @@ def run_reference(args):
     line = {
         "impl": "reference", "metric": "MC paths/s (Black-Scholes price + pathwise Greeks)", "value": value,
         "unit": "paths/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": 1e3 * total / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "ms_per_step": 1e3 * total / args.steps, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": "f64", "data": "synthetic (Philox normals, seed 42)",
-        "config": {"workload": "bs_greeks_f64 (BASELINE configs[1])", "paths_per_step": cores * per, "note": "bounded host sample"},
+        "config": {"workload": "bs_greeks_f64 (BASELINE configs[1]; F32 under secondary)", "paths_total": PATHS,
+                   "paths_per_step": cores * per,
+                   "note": "bounded host sample of the same workload: paths/s is linear in the path count"},
         "cpu_baseline": {"value": value, "unit": "paths/s", "cores": cores, "kind": "port",
                          "sample": f"{cores} processes x {per} paths per step, oracle (C++ restatement of the reference interpreter)"},
         "e2e": {"value": value, "unit": "paths/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -163,39 +180,77 @@ def cpu_baseline_sample():
 
 
 def secondary_hbm(dev, stream_h, flush, pk):
-    """Flat reduce and inclusive scan over 2^28 F32 (1 GiB, > L2), device timed."""
+    """Flat reduce and inclusive scan over 2^28 values (config (a): F32
+    ~N(0,1); config (b): I32 U[0,16)), and saxpy + sum at 2^28 (F32 and F64,
+    x, y = 2U - 1), all larger than L2, device timed (median of 5 after 3
+    warm-ups, L2 flushed before each). Inputs are generated on the device by
+    the reference's own Rng graphs: seeds 3 (data), 1 (x), 2 (y)."""
     import numpy as np
     from cudacaml_b200 import backend_cuda as B
+    from cudacaml_b200 import dsl as D
+    from cudacaml_b200 import rng as Rng
     from cudacaml_b200 import runtime as R
     from cudacaml_b200 import examples as X
-    from cudacaml_b200.ir import F32
+    from cudacaml_b200.ir import F32, F64, I32, Graph
     n = 1 << 28
     res = {}
-    x = R.Buffer(4 * n)
-    R.check(R.lib().ccb_memset_d8(x.ptr, 0x3c, 4 * n, None))  # 0x3c3c3c3c = 0.0115 in every lane
-    R.check(R.lib().ccb_stream_synchronize(None))
-    for name, g, out_bytes, alg_bytes in (("reduce_f32_2p28", X.reduce_flat(n, F32), 4, 4 * n),
-                                          ("scan_f32_2p28", X.scan_flat(n, F32), 4 * n, 8 * n)):
-        c = B.compile_on(dev, g)
-        o = R.Buffer(out_bytes)
+    seed_buf = R.Buffer(4)
+
+    def gen(expr, nbytes, seed):
+        c = B.compile_on(dev, Graph("gen", [("x", expr)]))
+        out = R.Buffer(nbytes)
+        seed_buf.upload(np.array([seed], np.int32))
+        B.run_device_ptrs(c, [seed_buf.ptr], [out.ptr], None)
+        B.check_device(c, None)
+        B.release(c)
+        return out
+
+    def time_prog(c, ins, outs):
         s = c.lane_stream(0)
         e0, e1 = R.Event(), R.Event()
         ts = []
         for k in range(8):
             flush(s)
             e0.record(s)
-            B.run_device_ptrs(c, [x.ptr], [o.ptr], s)
+            B.run_device_ptrs(c, [b.ptr for b in ins], [b.ptr for b in outs], s)
             e1.record(s)
             e1.synchronize()
             if k >= 3:
                 ts.append(e0.elapsed_ms(e1))
         B.check_device(c, s)
-        t = statistics.median(ts) * 1e-3
-        gbs = alg_bytes / t / 1e9
-        res[name] = {"gbs": gbs, "frac_of_measured_hbm": gbs / pk["hbm_gbs"], "ms": t * 1e3, "alg_bytes": alg_bytes}
-        o.free()
+        return statistics.median(ts) * 1e-3
+
+    key = D.scalar("seed", I32)
+    inputs = (("f32", F32, 4, D.map(lambda v: D.cast(F32, v), Rng.normal(F64, key, (n,))), "~N(0,1)"),
+              ("i32", I32, 4, D.map(lambda w: D.bit_and(w, D.const(I32, 15)), Rng.u32(key, (n,))), "U[0,16)"))
+    for tag, dt, esz, expr, dist in inputs:
+        x = gen(expr, esz * n, 3)
+        for name, g, out_bytes, alg_bytes in ((f"reduce_{tag}_2p28", X.reduce_flat(n, dt), esz, esz * n),
+                                              (f"scan_{tag}_2p28", X.scan_flat(n, dt), esz * n, 2 * esz * n)):
+            c = B.compile_on(dev, g)
+            o = R.Buffer(out_bytes)
+            t = time_prog(c, [x], [o])
+            gbs = alg_bytes / t / 1e9
+            res[name] = {"gbs": gbs, "frac_of_measured_hbm": gbs / pk["hbm_gbs"], "ms": t * 1e3, "alg_bytes": alg_bytes,
+                         "input": f"{dist}, Rng seed 3"}
+            o.free()
+            B.release(c)
+        x.free()
+    for dt, esz in ((F32, 4), (F64, 8)):
+        u2 = lambda v: D.cast(dt, D.sub(D.mul(D.const(F64, 2.0), v), D.const(F64, 1.0)))  # noqa: E731
+        xs = gen(D.map(u2, Rng.uniform(F64, key, (n,))), esz * n, 1)
+        ys = gen(D.map(u2, Rng.uniform(F64, key, (n,))), esz * n, 2)
+        c = B.compile_on(dev, X.saxpy(n, 2.0, dt))
+        rb, sb = R.Buffer(esz * n), R.Buffer(esz)
+        t = time_prog(c, [xs, ys], [rb, sb])
+        gbs = 3 * esz * n / t / 1e9
+        res[f"saxpy_sum_2p28_{dt.value}"] = {"gbs": gbs, "frac_of_measured_hbm": gbs / pk["hbm_gbs"], "ms": t * 1e3,
+                                             "alg_bytes": 3 * esz * n, "launches": c.num_launches(),
+                                             "note": "r = 2x + y and s = sum(r) in one pass: read x, y, write r"}
+        for b in (xs, ys, rb, sb):
+            b.free()
         B.release(c)
-    x.free()
+    seed_buf.free()
     return res
 
 
@@ -355,23 +410,31 @@ def secondary_configs(dev, flush, pk, quick=False):
     return res
 
 
-def measure_greeks(args, dtype, rank, world, local, dist, comm, flush):
-    """Device-timed and end-to-end paths/s of the Greeks graph in `dtype`."""
+def measure_greeks(args, dtype, rank, world, local, dist, comm, flush, weak=False):
+    """Device-timed and end-to-end paths/s of the Greeks graph in `dtype`.
+
+    Strong scaling (default): the PATHS paths are split `world` ways by
+    counter range, rank r pricing counters [r*PATHS/world, (r+1)*PATHS/world)
+    with the same seed -- Multi's split (multi.path_range, offset_counters
+    with rows = the per-rank count). weak=True gives every rank PATHS paths of
+    its own (counters [r*PATHS, (r+1)*PATHS), which must stay below 2^31)."""
     import numpy as np
     from cudacaml_b200 import backend_cuda as B
     from cudacaml_b200 import examples as X
     from cudacaml_b200 import multi as M
     from cudacaml_b200 import runtime as R
 
-    g = X.call_greeks(PATHS, dtype)
+    total = PATHS * world if weak else PATHS
+    base, per = M.path_range(total, world, rank)
+    g = X.call_greeks(per, dtype)
     if world > 1:
-        g = M.offset_counters(g, "seed")
+        g = M.offset_counters(g, "seed", rows=per)
     c = B.compile_on(local, g)
     stream = c.lane_stream(0)
     fnp = dtype.np
     esz = np.dtype(fnp).itemsize
     host_in = {"s0": np.array([100.0], fnp), "vol": np.array([0.2], fnp), "rate": np.array([0.05], fnp),
-               "seed": np.array([SEED], np.int32), M.CTR_BASE: np.array([rank * PATHS], np.int32)}
+               "seed": np.array([SEED], np.int32), M.CTR_BASE: np.array([base], np.int32)}
     in_bufs = []
     for name, _, _ in c.params:
         b = R.Buffer(host_in[name].nbytes)
@@ -423,36 +486,52 @@ def measure_greeks(args, dtype, rank, world, local, dist, comm, flush):
     div = world if comm is not None else 1
     outs = {name: float(v) / div for (name, _, _), v in zip(c.outputs, h)}
 
-    # e2e through the C-ABI with host buffers: pinned inputs are copied in,
-    # the program runs (and, on N > 1, all-reduces), the four results are
-    # read back, every step, device-timed on the launching stream.
+    # e2e through the plugin call (Backend_cuda.run_async + wait): the
+    # program uploads the page-locked host inputs, runs and downloads its four
+    # results into page-locked host memory on its lane's stream; on N > 1 the
+    # downloaded results are then all-reduced (uploaded, NCCL, read back) on
+    # the same stream. Device-timed on that stream, every step.
+    L = R.lib()
     pin_in = [R.pinned_empty(host_in[name].shape, host_in[name].dtype) for name, _, _ in c.params]
     for a, (name, _, _) in zip(pin_in, c.params):
         a[...] = host_in[name]
     pin_out = R.pinned_empty((4,), fnp)
+    pin_res = R.pinned_empty((4,), fnp)
+    in_arr = B._ptr_array([a.ctypes.data for a in pin_in])
+    out_arr = B._ptr_array([pin_out.ctypes.data + j * esz for j in range(len(c.outputs))])
     h2d = sum(a.nbytes for a in pin_in)
     e2e_evs = [(R.Event(), R.Event()) for _ in range(args.steps)]
+    barrier()
     for k in range(args.warmup + args.steps):
         flush(stream)
-        if k >= args.warmup:
+        timed = k >= args.warmup
+        if timed:
             e2e_evs[k - args.warmup][0].record(stream)
-        for a, b in zip(pin_in, in_bufs):
-            R.check(R.lib().ccb_memcpy_h2d(b.ptr, a.ctypes.data, a.nbytes, stream))
-        step()
-        R.check(R.lib().ccb_memcpy_d2h(pin_out.ctypes.data, red.ptr, 4 * esz, stream))
-        if k >= args.warmup:
+        R.check(L.ccb_program_enqueue(c.h, 0, in_arr, out_arr))
+        if comm is not None:
+            R.check(L.ccb_memcpy_h2d(red.ptr, pin_out.ctypes.data, 4 * esz, stream))
+            R.check(L.ccb_allreduce(comm, red.ptr, red.ptr, 4, dt_code, 0, stream))
+            R.check(L.ccb_memcpy_d2h(pin_res.ctypes.data, red.ptr, 4 * esz, stream))
+        if timed:
             e2e_evs[k - args.warmup][1].record(stream)
-    R.check(R.lib().ccb_stream_synchronize(stream))
+        R.check(L.ccb_program_wait(c.h, 0))
+        R.check(L.ccb_stream_synchronize(stream))
     B.check_device(c, stream)
     t_e2e = max_over_ranks(sum(a.elapsed_ms(b) for a, b in e2e_evs) * 1e-3)
+    # the plugin call computed the same bits as the device-resident runs
+    e2e_res = pin_res if comm is not None else pin_out
+    assert np.array_equal(e2e_res, h, equal_nan=True), (e2e_res, h)
     n_launch = c.num_launches()
     for b in in_bufs:
         b.free()
     red.free()
     B.release(c)
-    return {"value": world * PATHS * args.steps / t_dev, "t_dev": t_dev, "ms_per_step": 1e3 * t_dev / args.steps,
-            "e2e": world * PATHS * args.steps / t_e2e, "h2d": h2d, "d2h": 4 * esz, "outs": outs, "clocks": clk,
-            "launches": n_launch}
+    paths_all = per * world
+    return {"value": paths_all * args.steps / t_dev, "t_dev": t_dev, "ms_per_step": 1e3 * t_dev / args.steps,
+            "e2e": paths_all * args.steps / t_e2e, "h2d": h2d + (4 * esz if comm is not None else 0),
+            # the four results, the program's 4-byte error word, and on N > 1 the all-reduced results
+            "d2h": 4 * esz + 4 + (4 * esz if comm is not None else 0), "outs": outs, "clocks": clk,
+            "launches": n_launch, "paths_per_rank": per}
 
 
 def measure_mlp_dp(rank, world, local, dist, comm, flush, pk):
@@ -615,12 +694,19 @@ def run_ours(args):
         f32 = measure_greeks(args, F32, rank, world, local, dist, comm, flush)
     secondary = None
     if world > 1 and not args.no_secondary:
+        weak = measure_greeks(args, F64, rank, world, local, dist, comm, flush, weak=True)
         try:
             mlp = measure_mlp_dp(rank, world, local, dist, comm, flush, pk)
         except Exception as e:  # noqa: BLE001 - reported, not fatal to the headline
             mlp = {"error": f"{type(e).__name__}: {e}"}
         if rank == 0:
-            secondary = {f"mlp_step_8192x4096x8192x1024_tf32_dp{world}": mlp}
+            secondary = {
+                "bs_greeks_f64_weak": {"value": weak["value"], "unit": "paths/s", "e2e": weak["e2e"],
+                                       "ms_per_step": weak["ms_per_step"], "paths_per_gpu": weak["paths_per_rank"],
+                                       "result": weak["outs"],
+                                       "note": "weak scaling: every rank prices 2^28 paths of its own "
+                                               "(counters [r*2^28, (r+1)*2^28)), 4-scalar NCCL all-reduce per step"},
+                f"mlp_step_8192x4096x8192x1024_tf32_dp{world}": mlp}
     if rank == 0 and world == 1 and not args.no_secondary:
         secondary = secondary_hbm(local, None, flush, pk)
         try:
@@ -634,29 +720,40 @@ def run_ours(args):
                     "(expected ~8 of 2^28 paths) and erfinv(1) = inf, so the F32 price is inf at this size in the "
                     "reference interpreter too (cudacaml_backend_interp.ml:130); throughput only"}
 
+    # Issue roofline from the measured instruction count: warp instructions
+    # per launch / launch time against 148 SMs x 4 sub-partitions x 1 warp
+    # instruction per cycle at the measured maximum SM clock.
     avg_launch = head["t_dev"] / args.steps
-    issue_peak = 148 * 128 * pk["sm_max_mhz"] * 1e6
-    achieved = SLOTS_PER_PATH_F64 * PATHS / avg_launch
-    roofline = {"bound": "issue", "achieved": achieved / 1e9, "peak": issue_peak / 1e9, "unit": "Gslot/s",
-                "frac": achieved / issue_peak, "traffic": None,
-                "note": f"Monte Carlo moves ~0 algorithmic bytes; {SLOTS_PER_PATH_F64} FP32-issue-slot equivalents per "
-                        f"F64 path (FP64 and conversions count 2) x 2^28 paths per launch, against 148 SMs x 128 lanes x "
-                        f"{pk['sm_max_mhz']:.0f} MHz ({pk['src']} clock)"}
+    issue_peak = 148 * 4 * pk["sm_max_mhz"] * 1e6
+    achieved = INST_PER_PATH_F64 * head["paths_per_rank"] / avg_launch
+    roofline = {"bound": "issue", "achieved": achieved / 1e9, "peak": issue_peak / 1e9, "unit": "Gwarp-inst/s",
+                "frac": achieved / issue_peak, "traffic": DRAM_BYTES_GREEKS_F64,
+                "note": f"Monte Carlo moves ~0 algorithmic bytes; {INST_PER_PATH_F64:.3f} warp instructions per path "
+                        f"(ncu smsp__inst_executed.sum, profiles/mapreduce_bs_greeks_f64_2p20_instructions.md) x "
+                        f"{head['paths_per_rank']} paths per launch / the average step, against 148 SMs x 4 "
+                        f"sub-partitions x 1 warp instruction/cycle x {pk['sm_max_mhz']:.0f} MHz ({pk['src']} max "
+                        f"clock); traffic = DRAM bytes per launch from the same ncu capture"
+                        + ("; the step includes the 4-scalar NCCL all-reduce" if world > 1 else "")}
     if rank == 0:
         line = {
             "metric": "MC paths/s (Black-Scholes price + pathwise Greeks)", "value": head["value"], "unit": "paths/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": head["ms_per_step"],
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f64",
             "data": "synthetic (Philox normals generated in registers, seed 42)",
-            "config": {"workload": "bs_greeks_f64 (BASELINE configs[1]; F32 under secondary)", "paths_per_gpu": PATHS,
-                       "parallelism": f"dp{world} (counter-range split, NCCL all-reduce of 4 scalars per step)" if world > 1 else "dp1",
-                       "l2": "flushed before every timed step (read-only pass over 256 MiB, twice L2)", "market": "S0=100 K=100 r=0.05 sigma=0.2 T=1"},
+            "config": {"workload": "bs_greeks_f64 (BASELINE configs[1]; F32 under secondary)", "paths_total": PATHS,
+                       "paths_per_gpu": head["paths_per_rank"],
+                       "parallelism": (f"dp{world} (counter range split {world} ways as Multi does, NCCL all-reduce "
+                                       f"of 4 scalars per step)") if world > 1 else "dp1",
+                       "l2": "flushed before every timed step (read-only pass over 256 MiB, twice L2)",
+                       "market": "S0=100 K=100 r=0.05 sigma=0.2 T=1"},
             "result": head["outs"], "result_ok_vs_closed_form": ok, "closed_form": cf,
             "gpu_launches": head["launches"] * args.steps,
             "roofline": roofline,
             "clocks": head["clocks"],
             "e2e": {"value": head["e2e"], "unit": "paths/s", "h2d_bytes_per_step": head["h2d"],
-                    "d2h_bytes_per_step": head["d2h"]},
+                    "d2h_bytes_per_step": head["d2h"],
+                    "path": "ccb_program_enqueue + ccb_program_wait with page-locked host buffers"
+                            + (" + NCCL all-reduce of the results" if world > 1 else "")},
         }
         if world == 1:
             line["cpu_baseline"] = cpu_baseline_sample()

@@ -270,11 +270,13 @@ def _rank_main(rank, world, port, q):
                             timeout=datetime.timedelta(seconds=60))
     try:
         res = {}
-        # Greeks: counter range [rank*per, (rank+1)*per) of one seed; every
-        # output is a mean over paths, so the ranks' sum / world is the mean
-        per = GREEKS_N // world
-        g = M.offset_counters(X.call_greeks(per, F64), "seed")
-        base = (M.CTR_BASE, Value.of_list(I32, (), [rank * per]))
+        # Greeks, split as bench.py splits its headline (strong scaling):
+        # counter range [rank*per, (rank+1)*per) of one seed, Multi's
+        # path_range and offset_counters; every output is a mean over paths,
+        # so the ranks' sum / world is the mean
+        first, per = M.path_range(GREEKS_N, world, rank)
+        g = M.offset_counters(X.call_greeks(per, F64), "seed", rows=per)
+        base = (M.CTR_BASE, Value.of_list(I32, (), [first]))
         out = run(g, X.bs_inputs(F64, seed=SEED) + [base])
         names = [nm for nm, _ in g.outputs]
         s = torch.tensor([out[nm].get(0) for nm in names], dtype=torch.float64)
@@ -311,6 +313,17 @@ def _rank_main(rank, world, port, q):
         q.put((rank, {"error": repr(e)}))
     finally:
         dist.destroy_process_group()
+
+
+def test_path_range_split_and_counter_limit():
+    assert [M.path_range(1 << 28, 8, i) for i in (0, 1, 7)] == [(0, 1 << 25), (1 << 25, 1 << 25), (7 << 25, 1 << 25)]
+    assert M.path_range(1 << 31, 8, 7) == (7 << 28, 1 << 28)  # weak scaling at 8 GPUs: counters up to 2^31 - 1
+    with pytest.raises(ValueError):
+        M.path_range((1 << 31) + 8, 8, 0)  # would wrap the I32 counters
+    with pytest.raises(ValueError):
+        M.path_range(100, 3, 0)
+    with pytest.raises(ValueError):
+        M.Multi([0, 0], (1 << 31) + 2, lambda k: X.call_mc(k, F64), counter_key="seed")
 
 
 def _free_port():
