@@ -3,7 +3,7 @@
 The reference hands its graph to OCaml code in the same process. This backend
 lowers graphs natively inside ``libccb.so``, so the graph travels as a small,
 line-oriented text that any host language can print (the OCaml printer a
-maintainer would add is in INTEGRATION.md). Expression DAGs keep their sharing:
+maintainer would add is ocaml/wire.ml). Expression DAGs keep their sharing:
 every expression node is written once, before its users, under its own id.
 
     ccbgraph 1

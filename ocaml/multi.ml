@@ -1,0 +1,275 @@
+(* Multi over libccb.so: data-parallel runs across the GPUs of one box,
+   behind the reference's signature (lib/backend_cuda/multi.mli:14-64) plus
+   optional additions.
+
+   NOT BUILT HERE: the build image has no OCaml toolchain. This file replaces
+   lib/backend_cuda/multi.ml. Its Python mirror is cudacaml_b200/multi.py,
+   which the repository's CPU (gloo, world size 2) and GPU (two B200s, NCCL)
+   tests exercise.
+
+   Additions, all optional:
+   - [?counter_key]: split a Monte-Carlo graph by Philox counter range with
+     the same seed (device d draws counters [d*n/D, (d+1)*n/D)) instead of
+     asking the caller to reseed each device (multi.mli:39-44);
+   - [?split]: slice only the named inputs by rows;
+   - [allreduce_sum] / [allreduce_mean]: recombine outputs on the devices
+     with NCCL (ccb_allreduce inside ccb_group_start/end) over NVLink. *)
+
+open Cudacaml_ir
+open Cudacaml_runtime
+module B = Program
+
+let ( !! ) = Lazy.force
+let ctr_base = "__ctr_base"
+
+(* Device i of d's share of n paths: (first path, count). Rng counters are
+   I32 flat indices, so the whole range must stay below 2^31. *)
+let path_range ~n ~d i =
+  if d <= 0 || i < 0 || i >= d then invalid_arg (Printf.sprintf "Multi: device %d of %d" i d);
+  if n mod d <> 0 then invalid_arg (Printf.sprintf "Multi.create: n = %d is not divisible by %d devices" n d);
+  if n > 1 lsl 31 then invalid_arg (Printf.sprintf "Multi: %d paths exceed the I32 counter range (2^31)" n);
+  (i * (n / d), n / d)
+
+(* Rewrite every Rng.u32 counter [map2 f (iota s) (broadcast s key)]
+   (lib/rng/rng.ml:49-59) whose leading dimension is [rows] to count from the
+   scalar parameter [__ctr_base] times the draw's elements per path. *)
+let offset_counters ~key ~rows (g : Graph.t) : Graph.t =
+  let base = Dsl.scalar ctr_base Dtype.I32 in
+  let memo : (int, Tensor.packed) Hashtbl.t = Hashtbl.create 256 in
+  let cast_as : type a b. a Tensor.t -> b Tensor.t -> b Tensor.t =
+   fun like x -> match Dtype.equal like.Tensor.dtype x.Tensor.dtype with Some Dtype.Equal -> x | None -> assert false
+  in
+  let is_key_broadcast : type b. b Tensor.t -> bool =
+   fun k ->
+    match k.Tensor.node with
+    | Tensor.Broadcast (_, p) -> ( match p.Tensor.node with Tensor.Param n -> n = key | _ -> false)
+    | _ -> false
+  in
+  let rec go : type a. a Tensor.t -> a Tensor.t =
+   fun t ->
+    let k = Uid.to_int t.Tensor.uid in
+    match Hashtbl.find_opt memo k with
+    | Some (Tensor.P t') -> cast_as t t'
+    | None ->
+        let t' = rebuild t in
+        Hashtbl.add memo k (Tensor.P t');
+        t'
+  and rebuild : type a. a Tensor.t -> a Tensor.t =
+   fun t ->
+    let mk node = Tensor.make t.Tensor.dtype t.Tensor.shape node in
+    match t.Tensor.node with
+    | Tensor.Param _ | Tensor.Iota -> t
+    | Tensor.Map (f, a) ->
+        let a' = go a in
+        if a' == a then t else mk (Tensor.Map (f, a'))
+    | Tensor.Map2 (f, a, b) -> (
+        let counter =
+          match (a.Tensor.node, Dtype.equal a.Tensor.dtype Dtype.I32) with
+          | Tensor.Iota, Some Dtype.Equal
+            when is_key_broadcast b
+                 && (match Shape.dims a.Tensor.shape with r :: _ -> r = rows | [] -> false) ->
+              let per_path = List.fold_left ( * ) 1 (List.tl (Shape.dims a.Tensor.shape)) in
+              let start =
+                if per_path = 1 then base
+                else Dsl.map (fun v -> Dsl.mul v (Dsl.const Dtype.I32 (Int32.of_int per_path))) base
+              in
+              let shifted = Dsl.map2 Dsl.add a (Dsl.broadcast a.Tensor.shape start) in
+              Some (mk (Tensor.Map2 (f, cast_as a shifted, b)))
+          | _ -> None
+        in
+        match counter with
+        | Some t' -> t'
+        | None ->
+            let a' = go a and b' = go b in
+            if a' == a && b' == b then t else mk (Tensor.Map2 (f, a', b')))
+    | Tensor.Reduce (f, init, a) ->
+        let a' = go a in
+        if a' == a then t else mk (Tensor.Reduce (f, init, a'))
+    | Tensor.Scan (f, init, a) ->
+        let a' = go a in
+        if a' == a then t else mk (Tensor.Scan (f, init, a'))
+    | Tensor.Gather (i, a) ->
+        let i' = go i and a' = go a in
+        if i' == i && a' == a then t else mk (Tensor.Gather (i', a'))
+    | Tensor.Scatter_add (i, a, s) ->
+        let i' = go i and a' = go a in
+        if i' == i && a' == a then t else mk (Tensor.Scatter_add (i', a', s))
+    | Tensor.Matmul (a, b) ->
+        let a' = go a and b' = go b in
+        if a' == a && b' == b then t else mk (Tensor.Matmul (a', b'))
+    | Tensor.Reshape (s, a) ->
+        let a' = go a in
+        if a' == a then t else mk (Tensor.Reshape (s, a'))
+    | Tensor.Broadcast (s, a) ->
+        let a' = go a in
+        if a' == a then t else mk (Tensor.Broadcast (s, a'))
+  in
+  Graph.create ~name:(Graph.name g) ~outputs:(List.map (fun (n, Tensor.P t) -> (n, Tensor.P (go t))) (Graph.outputs g))
+
+type t = {
+  slots : (int * B.compiled) array;  (** (ordinal, program) *)
+  n : int;
+  per : int;
+  counter : bool;
+  split : string list option;
+  mutable comms : Ccb.handle array option;
+  mutable released : bool;
+}
+
+let release t =
+  if not t.released then begin
+    t.released <- true;
+    Array.iter (fun (_, c) -> B.release c) t.slots;
+    Option.iter (Array.iter (fun h -> ignore (!!Ccb.comm_destroy h))) t.comms;
+    t.comms <- None
+  end
+
+let create ~devices ~n ?counter_key ?split build =
+  let d = List.length devices in
+  if d = 0 then invalid_arg "Multi.create: devices must not be empty";
+  if n mod d <> 0 then invalid_arg (Printf.sprintf "Multi.create: n = %d is not divisible by %d devices" n d);
+  if counter_key <> None then ignore (path_range ~n ~d 0);
+  let per = n / d in
+  let slots =
+    Array.of_list
+      (List.map
+         (fun ordinal ->
+           let g = build ~n:per in
+           let g = match counter_key with Some key -> offset_counters ~key ~rows:per g | None -> g in
+           (ordinal, B.compile_on ~device:ordinal g))
+         devices)
+  in
+  let t = { slots; n; per; counter = counter_key <> None; split; comms = None; released = false } in
+  Gc.finalise (fun t -> try release t with _ -> ()) t;
+  t
+
+let leading_dim (Value.P v) = match Shape.dims (Value.shape v) with d :: _ -> Some d | [] -> None
+
+(* Rows [i*per, (i+1)*per) of a value whose leading dimension is n: a
+   Bigarray sub-view, no host copy. *)
+let slice ~index ~per (Value.P v) =
+  let dims = Shape.dims (Value.shape v) in
+  let row = List.fold_left ( * ) 1 (List.tl dims) in
+  match Value.raw v with
+  | Value.Raw a ->
+      let sub = Bigarray.Array1.sub a (index * per * row) (per * row) in
+      Value.P (Value.of_raw (Value.dtype v) (Shape.of_dims (per :: List.tl dims)) (Value.Raw sub))
+
+let splits t name v =
+  match t.split with
+  | Some names ->
+      if List.mem name names && leading_dim v <> Some t.n then
+        invalid_arg (Printf.sprintf "Multi.run: input %s does not have leading dimension %d" name t.n);
+      List.mem name names
+  | None -> leading_dim v = Some t.n
+
+let inputs_for t i inputs =
+  let ins = List.map (fun (name, v) -> if splits t name v then (name, slice ~index:i ~per:t.per v) else (name, v)) inputs in
+  if t.counter then
+    let first, _ = path_range ~n:t.n ~d:(Array.length t.slots) i in
+    ins @ [ (ctr_base, Value.P (Value.of_list Dtype.I32 Shape.scalar [ Int32.of_int first ])) ]
+  else ins
+
+let run_per_device t ~inputs =
+  if t.released then failwith "Multi.run: this Multi.t has been released";
+  let jobs = Array.mapi (fun i (_, c) -> B.run_async c ~inputs:(inputs i)) t.slots in
+  Array.to_list (Array.map B.wait jobs)
+
+let run t ~inputs = run_per_device t ~inputs:(fun i -> inputs_for t i inputs)
+
+let concat vs =
+  match vs with
+  | [] -> invalid_arg "Multi.concat: no values to concatenate"
+  | Value.P first :: _ ->
+      let rest = match Shape.dims (Value.shape first) with [] -> invalid_arg "Multi.concat: a rank-0 value has no leading axis" | _ :: r -> r in
+      let lead =
+        List.fold_left
+          (fun acc (Value.P v) ->
+            match (Dtype.equal (Value.dtype v) (Value.dtype first), Shape.dims (Value.shape v)) with
+            | Some Dtype.Equal, d :: r when r = rest -> acc + d
+            | _ -> invalid_arg "Multi.concat: dtype or trailing shape mismatch")
+          0 vs
+      in
+      let out = Value.create (Value.dtype first) (Shape.of_dims (lead :: rest)) in
+      let k = ref 0 in
+      List.iter
+        (fun (Value.P v) ->
+          match Dtype.equal (Value.dtype v) (Value.dtype first) with
+          | Some Dtype.Equal ->
+              for j = 0 to Value.numel v - 1 do
+                Value.set out !k (Value.get v j);
+                incr k
+              done
+          | None -> assert false)
+        vs;
+      Value.P out
+
+let scalar_float (Value.P v) =
+  if Value.numel v <> 1 then invalid_arg "Multi.mean_scalar: not a scalar";
+  match Value.dtype v with
+  | Dtype.F32 -> Value.get v 0
+  | Dtype.F64 -> Value.get v 0
+  | Dtype.I32 -> Int32.to_float (Value.get v 0)
+  | Dtype.I64 -> Int64.to_float (Value.get v 0)
+  | Dtype.Bool -> invalid_arg "Multi.mean_scalar: a bool output has no mean"
+
+let mean_scalar = function
+  | [] -> invalid_arg "Multi.mean_scalar: no values to average"
+  | vs -> List.fold_left (fun acc v -> acc +. scalar_float v) 0.0 vs /. float_of_int (List.length vs)
+
+(* Run every device resident, then one grouped NCCL all-reduce (sum) per
+   named output, on the devices; the sums are read back from the first
+   device. Needs distinct ordinals (NCCL puts one rank on each GPU). *)
+let allreduce_sum t ~names ~inputs =
+  if t.released then failwith "Multi.run: this Multi.t has been released";
+  let ords = Array.map fst t.slots in
+  if List.length (List.sort_uniq compare (Array.to_list ords)) <> Array.length ords then
+    invalid_arg "Multi.allreduce: NCCL needs distinct devices; use mean_scalar for repeats";
+  let d = Array.length t.slots in
+  let comms =
+    match t.comms with
+    | Some c -> c
+    | None ->
+        let devs = Ctypes.CArray.of_list Ctypes.int (Array.to_list ords) in
+        let hs = Ctypes.CArray.make Ccb.handle d in
+        Ccb.check "ccb_comm_init_all" (!!Ccb.comm_init_all d (Ctypes.CArray.start devs) (Ctypes.CArray.start hs));
+        let c = Array.of_list (Ctypes.CArray.to_list hs) in
+        t.comms <- Some c;
+        c
+  in
+  let per_dev =
+    Array.mapi
+      (fun i (_, c) ->
+        let ins = List.map (fun (n, v) -> (n, B.upload v)) (inputs_for t i inputs) in
+        let outs = B.run_resident c ~inputs:ins in
+        List.iter (fun (_, r) -> B.free_resident r) ins;
+        outs)
+      t.slots
+  in
+  List.iter
+    (fun name ->
+      Ccb.check "ccb_group_start" (!!Ccb.group_start ());
+      Array.iteri
+        (fun i (ordinal, _) ->
+          let r = List.assoc name per_dev.(i) in
+          let count = Shape.numel r.B.shape in
+          let code = match r.B.dtype with Dtype.P dt -> Ccb.dtype_code dt in
+          Device.with_device ordinal (fun () ->
+              let p = Buffer.unsafe_ptr r.B.buf in
+              Ccb.check "ccb_allreduce"
+                (!!Ccb.allreduce comms.(i) p p (Unsigned.Size_t.of_int count) code 0 Stream.default)))
+        t.slots;
+      Ccb.check "ccb_group_end" (!!Ccb.group_end ()))
+    names;
+  Array.iter (fun (ordinal, _) -> Device.with_device ordinal Device.synchronize) t.slots;
+  let result =
+    List.map (fun name -> (name, Device.with_device (fst t.slots.(0)) (fun () -> B.download (List.assoc name per_dev.(0))))) names
+  in
+  Array.iteri
+    (fun i (ordinal, _) -> Device.with_device ordinal (fun () -> List.iter (fun (_, r) -> B.free_resident r) per_dev.(i)))
+    t.slots;
+  result
+
+let allreduce_mean t ~names ~inputs =
+  let d = float_of_int (Array.length t.slots) in
+  List.map (fun (n, v) -> (n, scalar_float v /. d)) (allreduce_sum t ~names ~inputs)
