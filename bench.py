@@ -410,6 +410,146 @@ def secondary_configs(dev, flush, pk, quick=False):
     return res
 
 
+def secondary_reference_nvrtc(dev, flush, ours):
+    """The reference's NVRTC backend, restated (baseline/ref_nvrtc.py: the
+    reference's buffer plan, kernel templates, launch geometry and C
+    spellings, compiled by NVRTC with no options and JIT-loaded), timed on the
+    same GPU, on the same synthetic inputs, device-resident, L2 flushed before
+    each run, median of 3 after 1 warm-up. `ours` holds this backend's
+    numbers from the same run; speedup = reference time / ours."""
+    import numpy as np
+    from baseline import ref_nvrtc as RN
+    from cudacaml_b200 import backend_cuda as B
+    from cudacaml_b200 import dsl as D
+    from cudacaml_b200 import examples as X
+    from cudacaml_b200 import rng as Rng
+    from cudacaml_b200 import runtime as R
+    from cudacaml_b200.ir import F32, F64, I32, Graph
+    from cuda.bindings import driver as cu
+
+    res = {}
+    seed_buf = R.Buffer(4)
+    key = D.scalar("seed", I32)
+
+    def gen(expr, nbytes, seed):
+        c = B.compile_on(dev, Graph("gen", [("x", expr)]))
+        out = R.Buffer(nbytes)
+        seed_buf.upload(np.array([seed], np.int32))
+        B.run_device_ptrs(c, [seed_buf.ptr], [out.ptr], None)
+        B.check_device(c, None)
+        B.release(c)
+        return out
+
+    stream = R.Stream()
+    e0, e1 = R.Event(), R.Event()
+
+    def time_ref(g, inputs, reps=3):
+        L = RN.Loaded(RN.Program(g))
+        try:
+            for name, buf in inputs.items():
+                RN._ck(cu.cuMemcpyDtoD(L.param_buffer(name), buf.ptr, buf.nbytes), "cuMemcpyDtoD")
+            ts = []
+            for k in range(1 + reps):
+                flush(stream.h)
+                e0.record(stream)
+                L.launch(stream.h)
+                e1.record(stream)
+                e1.synchronize()
+                if k >= 1:
+                    ts.append(e0.elapsed_ms(e1))
+            return statistics.median(ts), len(L.prog.kernels)
+        finally:
+            L.release()
+
+    def put(name, g, inputs, ours_ms, reps=3):
+        try:
+            ms, nk = time_ref(g, inputs, reps)
+            res[name] = {"ms": ms, "kernels": nk, "ours_ms": ours_ms,
+                         "speedup": (ms / ours_ms) if ours_ms else None}
+        except Exception as e:  # noqa: BLE001 - a baseline failure is reported, not fatal
+            res[name] = {"error": f"{type(e).__name__}: {e}"}
+
+    def ours_ms(k):
+        v = ours.get(k) or {}
+        return v.get("ms")
+
+    n = 1 << 28
+    u2 = lambda dt: (lambda v: D.cast(dt, D.sub(D.mul(D.const(F64, 2.0), v), D.const(F64, 1.0))))  # noqa: E731
+    xs = gen(D.map(u2(F32), Rng.uniform(F64, key, (n,))), 4 * n, 1)
+    ys = gen(D.map(u2(F32), Rng.uniform(F64, key, (n,))), 4 * n, 2)
+    put("saxpy_sum_2p28_f32", X.saxpy(n, 2.0), {"x": xs, "y": ys}, ours_ms("saxpy_sum_2p28_f32"))
+    xs.free()
+    ys.free()
+    xf = gen(D.map(lambda v: D.cast(F32, v), Rng.normal(F64, key, (n,))), 4 * n, 3)
+    put("reduce_f32_2p28", X.reduce_flat(n, F32), {"x": xf}, ours_ms("reduce_f32_2p28"))
+    put("scan_f32_2p28", X.scan_flat(n, F32), {"x": xf}, ours_ms("scan_f32_2p28"))
+    xf.free()
+    xi = gen(D.map(lambda w: D.bit_and(w, D.const(I32, 15)), Rng.u32(key, (n,))), 4 * n, 3)
+    put("reduce_i32_2p28", X.reduce_flat(n, I32), {"x": xi}, ours_ms("reduce_i32_2p28"))
+    put("scan_i32_2p28", X.scan_flat(n, I32), {"x": xi}, ours_ms("scan_i32_2p28"))
+    xi.free()
+    rows, rn = 65536, 4096
+    xr = gen(D.map(lambda v: D.cast(F32, v), Rng.normal(F64, key, (rows, rn))), 4 * rows * rn, 3)
+    xp = D.param("x", F32, (rows, rn))
+    put("reduce_rows_max_65536x4096", Graph("rmax", [("m", D.reduce_rows(D.max, D.const(F32, -3e38), xp))]), {"x": xr},
+        ours_ms("reduce_rows_max_65536x4096"))
+    put("scan_rows_add_65536x4096", Graph("rscan", [("p", D.scan_rows(D.add, D.const(F32, 0.0), xp))]), {"x": xr},
+        ours_ms("scan_rows_add_65536x4096"))
+    xr.free()
+    m, bins, tbl = 1 << 27, 1 << 20, 1 << 24
+    vb = gen(Rng.uniform(F32, key, (m,)), 4 * m, 3)
+    ib = gen(D.map(lambda w: D.bit_and(w, D.const(I32, bins - 1)), Rng.u32(key, (m,))), 4 * m, 4)
+    # Zipf indices as bench's own scatter line uses them (host inverse CDF)
+    u = gen(Rng.uniform(F64, key, (m,)), 8 * m, 4)
+    uh = np.empty(m, np.float64)
+    u.download(uh)
+    u.free()
+    w = 1.0 / np.power(np.arange(1, bins + 1, dtype=np.float64), 1.1)
+    cdf = np.cumsum(w)
+    cdf /= cdf[-1]
+    ib.upload(np.minimum(np.searchsorted(cdf, uh, side="left"), bins - 1).astype(np.int32))
+    del uh
+    put("scatter_add_zipf_2p27_into_2p20", X.scatter(m, bins), {"idx": ib, "v": vb},
+        ours_ms("scatter_add_zipf_2p27_into_2p20"))
+    ib.free()
+    vb.free()
+    gi = gen(D.map(lambda w_: D.bit_and(w_, D.const(I32, tbl - 1)), Rng.u32(key, (m,))), 4 * m, 4)
+    tb = gen(D.map(lambda v: D.cast(F32, v), Rng.normal(F64, key, (tbl,))), 4 * tbl, 3)
+    put("gather_2p27_from_2p24", X.gather(m, tbl), {"idx": gi, "table": tb}, ours_ms("gather_2p27_from_2p24"))
+    gi.free()
+    tb.free()
+    for dt, esz in ((F64, 8), (F32, 4)):
+        ins = {}
+        for name, val in (("s0", 100.0), ("vol", 0.2), ("rate", 0.05)):
+            b = R.Buffer(esz)
+            b.upload(np.array([val], dt.np))
+            ins[name] = b
+        sb = R.Buffer(4)
+        sb.upload(np.array([42], np.int32))
+        ins["seed"] = sb
+        put(f"bs_greeks_{dt.value}_2p28", X.call_greeks(PATHS, dt), ins, ours_ms(f"bs_greeks_{dt.value}_2p28"))
+        for b in ins.values():
+            b.free()
+    bsz, din, hid, dout = 8192, 4096, 8192, 1024
+    named = {"X": gen(D.map(lambda v: D.cast(F32, v), Rng.normal(F64, key, (bsz, din))), 4 * bsz * din, 5),
+             "W1": gen(D.map(lambda v: D.cast(F32, D.mul(v, D.const(F64, 1 / math.sqrt(din)))),
+                             Rng.normal(F64, key, (din, hid))), 4 * din * hid, 6),
+             "W2": gen(D.map(lambda v: D.cast(F32, D.mul(v, D.const(F64, 1 / math.sqrt(hid)))),
+                             Rng.normal(F64, key, (hid, dout))), 4 * hid * dout, 7),
+             "T": gen(D.map(lambda v: D.cast(F32, v), Rng.normal(F64, key, (bsz, dout))), 4 * bsz * dout, 8)}
+    put("mlp_step_8192x4096x8192x1024_f32", X.mlp_step(bsz, din, hid, dout), named,
+        ours_ms("mlp_step_8192x4096x8192x1024_tf32"), reps=1)
+    if "ms" in res["mlp_step_8192x4096x8192x1024_f32"]:
+        res["mlp_step_8192x4096x8192x1024_f32"]["ours_f32_ms"] = ours_ms("mlp_step_8192x4096x8192x1024_f32")
+        res["mlp_step_8192x4096x8192x1024_f32"]["note"] = ("ours_ms is this backend's tf32 step (tensor cores), "
+                                                            "ours_f32_ms its F32 (CUDA-core) step")
+    for b in named.values():
+        b.free()
+    seed_buf.free()
+    stream.destroy()
+    return res
+
+
 def measure_greeks(args, dtype, rank, world, local, dist, comm, flush, weak=False):
     """Device-timed and end-to-end paths/s of the Greeks graph in `dtype`.
 
@@ -715,10 +855,15 @@ def run_ours(args):
             secondary["configs_error"] = f"{type(e).__name__}: {e}"
         secondary["bs_greeks_f32_2p28"] = {
             "value": f32["value"], "unit": "paths/s", "e2e": f32["e2e"], "ms_per_step": f32["ms_per_step"],
-            "result": f32["outs"],
+            "ms": f32["ms_per_step"], "result": f32["outs"],
             "note": "the reference's F32 generator rounds (w + 0.5) * 2^-32 to 1.0f for w >= 2^32 - 2^7 "
                     "(expected ~8 of 2^28 paths) and erfinv(1) = inf, so the F32 price is inf at this size in the "
                     "reference interpreter too (cudacaml_backend_interp.ml:130); throughput only"}
+        secondary["bs_greeks_f64_2p28"] = {"ms": head["ms_per_step"]}
+        try:
+            secondary["reference_nvrtc_restated"] = secondary_reference_nvrtc(local, flush, secondary)
+        except Exception as e:  # noqa: BLE001 - the baseline is reported, not fatal
+            secondary["reference_nvrtc_restated"] = {"error": f"{type(e).__name__}: {e}"}
 
     # Issue roofline from the measured instruction count: warp instructions
     # per launch / launch time against 148 SMs x 4 sub-partitions x 1 warp

@@ -565,7 +565,9 @@ __device__ __forceinline__ void scan_flat_staged(const typename F::P& p) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const bool src_aligned = aligned16(src);
   const bool dst_aligned = aligned16(dst);
-  unsigned parity[NBUF] = {0u, 0u, 0u};
+  // The phase parity of each ring buffer's barrier, one bit per buffer in a
+  // register (an array indexed by k % NBUF would live in local memory).
+  unsigned parity = 0u;
 
   // thread 0: claim the next tile into buffer b and start its bulk load
   auto claim = [&](int b) {
@@ -610,8 +612,8 @@ __device__ __forceinline__ void scan_flat_staged(const typename F::P& p) {
       const long long base = (long long)tc * TILE;
       T* b = buf + (size_t)bc * TILE;
       if (s_tma[bc]) {
-        mbar_wait(&bars[bc], parity[bc], p.err);
-        parity[bc] ^= 1u;
+        mbar_wait(&bars[bc], (parity >> bc) & 1u, p.err);
+        parity ^= 1u << bc;
       } else {
         for (int e = tid; e < TILE; e += BLOCK) b[e] = (base + e < n) ? src[base + e] : F::identity();
         __syncthreads();
