@@ -39,9 +39,11 @@ def _band(got, want, tol):
 
 
 def test_saxpy_sum_two_pass_reduce():
+    # positive terms, so the F32 sum does not cancel and a relative band is
+    # meaningful for both summation orders (tree here, sequential in the oracle)
     n = 300_007
-    x = Value.of_array(F32, (n,), np.linspace(-1, 1, n, dtype=np.float32))
-    y = Value.of_array(F32, (n,), np.cos(np.arange(n)).astype(np.float32))
+    x = Value.of_array(F32, (n,), np.linspace(0, 1, n, dtype=np.float32))
+    y = Value.of_array(F32, (n,), (1.0 + np.cos(np.arange(n))).astype(np.float32))
     g = X.saxpy(n, 2.0)
     got, want = _run(g, [("x", x), ("y", y)]), _oracle(g, [("x", x), ("y", y)])
     _band(got["r"], want["r"], 1e-6)
