@@ -701,6 +701,169 @@ __device__ __forceinline__ void scan_flat_staged(const typename F::P& p) {
   }
 }
 
+// ---------------------------------------------------------------- staged rows (TMA)
+// Row reduction and row scan over [rows; n] of a 4-byte source buffer read at
+// the element index, n a multiple of 4 (so every row starts 16-byte aligned
+// when the buffer does). Each CTA walks its rows (blockIdx.x, + gridDim.x,
+// ...) as one sequence of chunks of up to ROW_STRIPS x 1024 elements; thread
+// 0 keeps ROW_RING chunks in flight by 1-D bulk copies (cp.async.bulk, the
+// TMA engine, never multicast), so the next row's first chunks are already
+// arriving while a row finishes. A chunk is consumed as strips of 1024
+// elements, thread t owning elements [4t, 4t + 4) of each strip (conflict-free
+// 16-byte shared reads). If the buffer is not 16-byte aligned the CTA stages
+// the chunks with plain loads instead. Every wait is bounded (ERR_TMA).
+// F provides T, identity(), combine(a,b), src(p); reductions store_row(p,r,v),
+// scans dst(p); P provides n, rows, err.
+constexpr int ROW_STRIPS = 4, ROW_RING = 4;
+constexpr int ROW_CHUNK = ROW_STRIPS * 1024;
+constexpr unsigned ROW_SMEM = ROW_RING * ROW_CHUNK * 4 + ROW_RING * 8;
+
+template <class F, bool SCAN>
+__device__ __forceinline__ void rows_staged(const typename F::P& p) {
+  typedef typename F::T T;
+  static_assert(sizeof(T) == 4, "staged rows are for 4-byte element types");
+  constexpr int BLOCK = 256, C = ROW_CHUNK, NB = ROW_RING, NW = BLOCK / 32;
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  T* ring = reinterpret_cast<T*>(smem_raw);
+  u64* bars = reinterpret_cast<u64*>(smem_raw + (size_t)NB * C * sizeof(T));
+  __shared__ T s_w[ROW_STRIPS * NW];  // warp totals per strip, (strip, warp) order
+  __shared__ T s_red[NW];
+  __shared__ T s_tot;  // a scanned chunk's total
+  static_assert(ROW_STRIPS * NW == 32, "one warp total per lane in the offset scan");
+  const long long n = p.n, rows = p.rows;
+  const T* src = F::src(p);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const long long cpr = (n + C - 1) / C;  // chunks per row
+  const long long mine = (long long)blockIdx.x < rows ? (rows - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+  const long long total = mine * cpr;
+  const bool tma = aligned16(src);
+  struct Chunk {
+    long long row, c0;
+    int cnt;
+  };
+  auto where = [&](long long q) {  // chunk q of this CTA's sequence
+    Chunk k;
+    k.row = blockIdx.x + (q / cpr) * (long long)gridDim.x;
+    k.c0 = (q % cpr) * (long long)C;
+    const long long left = n - k.c0;
+    k.cnt = (int)(left < C ? left : C);
+    return k;
+  };
+  auto issue = [&](long long q) {  // thread 0 only
+    const Chunk k = where(q);
+    const long long row = k.row, c0 = k.c0;
+    const int cnt = k.cnt;
+    const int b = (int)(q % NB);
+    fence_proxy_async_smem();
+    mbar_expect_tx(&bars[b], (unsigned)cnt * 4u);
+    bulk_load(ring + (size_t)b * C, src + row * n + c0, (unsigned)cnt * 4u, &bars[b]);
+  };
+  if (tid == 0) {
+    for (int b = 0; b < NB; ++b) mbar_init(&bars[b], 1);
+    mbar_fence_init();
+    if (tma)
+      for (long long q = 0; q < total && q < NB; ++q) issue(q);
+  }
+  __syncthreads();
+  unsigned parity = 0u;  // one phase bit per ring buffer
+  T acc = F::identity(), carry = F::identity();
+  for (long long q = 0; q < total; ++q) {
+    const Chunk k = where(q);
+    const long long row = k.row, c0 = k.c0;
+    const int cnt = k.cnt;
+    const int b = (int)(q % NB);
+    T* buf = ring + (size_t)b * C;
+    if (tma) {
+      mbar_wait(&bars[b], (parity >> b) & 1u, p.err);
+      parity ^= 1u << b;
+    } else {
+      for (int e = tid; e < cnt; e += BLOCK) buf[e] = src[row * n + c0 + e];
+      __syncthreads();
+    }
+    if constexpr (!SCAN) {
+#pragma unroll
+      for (int sI = 0; sI < ROW_STRIPS; ++sI) {
+        const int e = sI * 1024 + 4 * tid;
+        if (e < cnt) {
+          const V4<T> v = *reinterpret_cast<const V4<T>*>(buf + e);
+          acc = F::combine(acc, v.v[0]);
+          acc = F::combine(acc, v.v[1]);
+          acc = F::combine(acc, v.v[2]);
+          acc = F::combine(acc, v.v[3]);
+        }
+      }
+    } else {
+      // strip scan: thread totals -> warp scans -> (strip, warp) offsets
+      V4<T> v[ROW_STRIPS];
+      T excl[ROW_STRIPS];
+#pragma unroll
+      for (int sI = 0; sI < ROW_STRIPS; ++sI) {
+        const int e = sI * 1024 + 4 * tid;
+        if (e < cnt) {
+          v[sI] = *reinterpret_cast<const V4<T>*>(buf + e);
+        } else {
+#pragma unroll
+          for (int k = 0; k < 4; ++k) v[sI].v[k] = F::identity();
+        }
+#pragma unroll
+        for (int k = 1; k < 4; ++k) v[sI].v[k] = F::combine(v[sI].v[k - 1], v[sI].v[k]);
+        const T incl = warp_scan_incl<F>(v[sI].v[3], lane);
+        T ex = __shfl_up_sync(FULL, incl, 1);
+        excl[sI] = lane == 0 ? F::identity() : ex;
+        if (lane == 31) s_w[sI * NW + warp] = incl;
+      }
+      __syncthreads();
+      if (warp == 0) {  // the 32 warp totals in (strip, warp) order, one per lane
+        const T incl = warp_scan_incl<F>(s_w[lane], lane);
+        T ex = __shfl_up_sync(FULL, incl, 1);
+        if (lane == 0) ex = F::identity();
+        s_w[lane] = ex;
+        if (lane == 31) s_tot = incl;
+      }
+      __syncthreads();
+      const T chunk_total = s_tot;
+      T* dst = F::dst(p) + row * n + c0;
+      const bool vec = aligned16(dst);
+#pragma unroll
+      for (int sI = 0; sI < ROW_STRIPS; ++sI) {
+        const int e = sI * 1024 + 4 * tid;
+        const T pre = F::combine(carry, F::combine(s_w[sI * NW + warp], excl[sI]));
+        V4<T> o;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) o.v[k] = F::combine(pre, v[sI].v[k]);
+        if (e + 4 <= cnt && vec) {
+          st4(dst + e, o);
+        } else {
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            if (e + k < cnt) dst[e + k] = o.v[k];
+        }
+      }
+      carry = F::combine(carry, chunk_total);
+    }
+    __syncthreads();  // every thread is done with buf (and with s_w)
+    if (tma && tid == 0 && q + NB < total) issue(q + NB);
+    if (c0 + cnt >= n) {  // the row's last chunk
+      if constexpr (!SCAN) {
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) acc = F::combine(acc, __shfl_down_sync(FULL, acc, o));
+        if (lane == 0) s_red[warp] = acc;
+        __syncthreads();
+        if (warp == 0) {
+          T r = lane < NW ? s_red[lane] : F::identity();
+#pragma unroll
+          for (int o = 1; o < 32; o <<= 1) r = F::combine(r, __shfl_down_sync(FULL, r, o));
+          if (lane == 0) F::store_row(p, row, r);
+        }
+        __syncthreads();
+        acc = F::identity();
+      } else {
+        carry = F::identity();
+      }
+    }
+  }
+}
+
 // ---------------------------------------------------------------- transpose
 // A materialised Dsl.transpose of a buffer: src [rows; cols] -> dst
 // [cols; rows], in 32 x 32 tiles staged through shared memory so that both

@@ -2298,6 +2298,70 @@ class Lowerer {
     l.smem = (int)(3 * TILE * 4 + 64);
   }
 
+  // The staged (TMA) row kernels: a 4-byte row reduction or row scan whose
+  // source is a buffer read straight at the element index, over rows of at
+  // least 1024 elements and a multiple of 4 (so rows start 16-byte aligned).
+  // Opt-in with CCB_ROWS_STAGED=1: on the B200 the register-streaming row
+  // kernels are faster (65536 x 4096 F32: reduce_rows 0.157 vs 0.173 ms,
+  // scan_rows 0.342 vs 0.358 ms), so they stay the default.
+  bool staged_rows_source(const Group& gr, int t, int& src_buf) const {
+    const GTensor& x = g.ts[t];
+    if ((gr.kind != G_RED_ROWS && gr.kind != G_SCAN_ROWS) || dt_size(x.dt) != 4) return false;
+    if (gr.n < 1024 || gr.n % 4 != 0) return false;
+    const char* e = std::getenv("CCB_ROWS_STAGED");
+    if (!e || e[0] != '1') return false;
+    const KN& k = gr.ctx.n[gr.val];
+    if (k.op != K_LOAD || k.a != gr.ctx.index_node) return false;
+    src_buf = k.buf;
+    return true;
+  }
+
+  void emit_rows_staged(int gi, int srcb, bool scan) {
+    Group& gr = groups[gi];
+    const int t = gr.root;
+    const GTensor& x = g.ts[t];
+    const char* T = dt_ctype(x.dt);
+    const std::string F = "F" + std::to_string(gi);
+    const std::string fn = std::string(scan ? "ccb_scanrowsstaged_" : "ccb_redrowsstaged_") + std::to_string(gi) + kname_suffix();
+    node_buf[t] = add_buf("t" + std::to_string(x.uid), dt_size(x.dt), x.numel, BR_NODE, t, false);
+    std::vector<Field> fields;
+    fields.push_back(in_field(srcb));
+    fields.push_back(out_field(t));
+    fields.push_back(buf_field("unsigned* err", out->err_buf));
+    fields.push_back(i64_field("n", gr.n));
+    fields.push_back(i64_field("rows", gr.rows));
+    src << "// staged row " << (scan ? "scan " : "reduction ") << gi << ": " << gr.rows << " rows of " << gr.n << "\n";
+    src << "struct " << F << " {\n";
+    emit_struct(fields);
+    src << "  typedef " << T << " T;\n";
+    {
+      std::ostringstream tmp;
+      KCtx c;
+      int iv = init_knode(c, t);
+      Emitter e(c, tmp);
+      std::string v = e.val(iv);
+      src << "  static __device__ __forceinline__ T identity() {\n" << tmp.str() << "    return " << v << ";\n  }\n";
+    }
+    src << "  static __device__ __forceinline__ T combine(T a, T b) {\n";
+    if (is_plain_add(t))
+      src << "    return " << bin_text(x.dt, B_ADD, "a", "b") << "; }\n";
+    else
+      src << combine_body(t, "    ");
+    src << "  static __device__ __forceinline__ const T* src(const P& p) { return p.b" << srcb << "; }\n";
+    if (scan)
+      src << "  static __device__ __forceinline__ T* dst(const P& p) { return p.o" << t << "; }\n";
+    else
+      src << "  static __device__ __forceinline__ void store_row(const P& p, long long r, T v) { p.o" << t << "[r] = v; }\n";
+    src << "};\n";
+    src << "extern \"C\" __global__ void __launch_bounds__(256) " << fn << "(const " << F << "::P p) { ccb::rows_staged<" << F
+        << ", " << (scan ? "true" : "false") << ">(p); }\n\n";
+    LaunchSpec& l = add_launch(fn, fields);
+    l.mode = GM_PERSISTENT;
+    l.work = gr.rows;
+    l.per_block = 1;
+    l.smem = 4 * 16384 + 32;  // ccb::ROW_SMEM: a ring of 4 chunks of 4096 elements and their barriers
+  }
+
   void emit_scan(int gi) {
     Group& gr = groups[gi];
     const int t = gr.root;
@@ -2305,6 +2369,10 @@ class Lowerer {
       int srcb = -1;
       if (staged_scan_source(gr, t, srcb)) {
         emit_scan_staged(gi, srcb);
+        return;
+      }
+      if (gr.kind == G_SCAN_ROWS && gr.epi < 0 && gr.tstore < 0 && staged_rows_source(gr, t, srcb)) {
+        emit_rows_staged(gi, srcb, true);
         return;
       }
     }
@@ -2468,6 +2536,13 @@ class Lowerer {
   void emit_red_rows(int gi) {
     Group& gr = groups[gi];
     const int t = gr.root;
+    {
+      int srcb = -1;
+      if (staged_rows_source(gr, t, srcb)) {
+        emit_rows_staged(gi, srcb, false);
+        return;
+      }
+    }
     const GTensor& x = g.ts[t];
     const char* T = dt_ctype(x.dt);
     const std::string F = "F" + std::to_string(gi);

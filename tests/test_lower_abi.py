@@ -273,3 +273,23 @@ def test_offset_streams_are_vector_loads():
     rev = D.map(lambda p: D.sub(D.const(I32, n - 1), p), D.iota((n,)))
     src = B.lower_info(Graph("rev", [("r", D.gather(rev, D.reshape((rows * n,), m)))]))["source"]
     assert "K0 = " not in src
+
+
+def test_staged_row_kernels_are_opt_in_and_compile(monkeypatch):
+    """rows_staged (TMA-staged row tiles) is selected only with
+    CCB_ROWS_STAGED=1, only for 4-byte rows of >= 1024 elements and a multiple
+    of 4 read straight from a buffer, and its source compiles for sm_100a."""
+    from cudacaml_b200 import dsl as D
+    from cudacaml_b200.ir import F64, Graph
+    g = X.rows(256, 4096)
+    assert "rowsstaged" not in B.lower_info(g)["plan"]
+    monkeypatch.setenv("CCB_ROWS_STAGED", "1")
+    info = B.lower_info(g)
+    assert "ccb_redrowsstaged_" in info["plan"] and "ccb_scanrowsstaged_" in info["plan"]
+    assert nvrtc_ok(info["source"], "rows_staged") > 0
+    for dt, n in ((F64, 4096), (F32, 1022), (F32, 512)):  # 8-byte, ragged, short rows keep the plain kernels
+        x = D.param("x", dt, (64, n))
+        assert "rowsstaged" not in B.lower_info(Graph("r", [("r", D.reduce_rows(D.add, D.const(dt, 0.0), x))]))["plan"]
+    x = D.param("x", F32, (64, 4096))
+    mapped = Graph("r", [("r", D.reduce_rows(D.add, D.const(F32, 0.0), D.map(D.exp, x)))])
+    assert "rowsstaged" not in B.lower_info(mapped)["plan"]  # the source is an expression, not a buffer
