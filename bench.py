@@ -5,7 +5,8 @@ configuration the reference metric "MC paths/s" is quoted on (BASELINE
 configs[1]). F64 is the headline because at 2^28 paths the reference's own F32
 normal generator produces a few infinite normals (see "secondary"). One step =
 one run of the Greeks graph (one fused forward+adjoint launch) plus, on N > 1
-GPUs, the NCCL all-reduce that recombines the four scalar outputs.
+GPUs, the cross-rank sum that recombines the four scalar outputs over NVLink
+peer memory (multi.PeerSum, one 32-thread kernel per rank).
 
 Scaling is strong, as BASELINE configs[1] states it: the 2^28 paths are split
 N ways by counter range with the same seed, rank r pricing counters
@@ -550,7 +551,7 @@ def secondary_reference_nvrtc(dev, flush, ours):
     return res
 
 
-def measure_greeks(args, dtype, rank, world, local, dist, comm, flush, weak=False):
+def measure_greeks(args, dtype, rank, world, local, dist, peer, flush, weak=False):
     """Device-timed and end-to-end paths/s of the Greeks graph in `dtype`.
 
     Strong scaling (default): the PATHS paths are split `world` ways by
@@ -586,8 +587,8 @@ def measure_greeks(args, dtype, rank, world, local, dist, comm, flush, weak=Fals
 
     def step():
         B.run_device_ptrs(c, [b.ptr for b in in_bufs], out_ptrs, stream)
-        if comm is not None:
-            R.check(R.lib().ccb_allreduce(comm, red.ptr, red.ptr, 4, dt_code, 0, stream))
+        if peer is not None:
+            peer.sum(red.ptr, red.ptr, 4, dt_code, stream)
 
     def barrier():
         if dist is not None:
@@ -623,7 +624,9 @@ def measure_greeks(args, dtype, rank, world, local, dist, comm, flush, weak=Fals
     t_dev = max_over_ranks(sum(a.elapsed_ms(b) for a, b in evs) * 1e-3)
     h = np.empty(4, fnp)
     red.download(h)
-    div = world if comm is not None else 1
+    if peer is not None:
+        peer.check(stream)
+    div = world if peer is not None else 1
     outs = {name: float(v) / div for (name, _, _), v in zip(c.outputs, h)}
 
     # e2e through the plugin call (Backend_cuda.run_async + wait): the
@@ -648,9 +651,9 @@ def measure_greeks(args, dtype, rank, world, local, dist, comm, flush, weak=Fals
         if timed:
             e2e_evs[k - args.warmup][0].record(stream)
         R.check(L.ccb_program_enqueue(c.h, 0, in_arr, out_arr))
-        if comm is not None:
+        if peer is not None:
             R.check(L.ccb_memcpy_h2d(red.ptr, pin_out.ctypes.data, 4 * esz, stream))
-            R.check(L.ccb_allreduce(comm, red.ptr, red.ptr, 4, dt_code, 0, stream))
+            peer.sum(red.ptr, red.ptr, 4, dt_code, stream)
             R.check(L.ccb_memcpy_d2h(pin_res.ctypes.data, red.ptr, 4 * esz, stream))
         if timed:
             e2e_evs[k - args.warmup][1].record(stream)
@@ -659,7 +662,9 @@ def measure_greeks(args, dtype, rank, world, local, dist, comm, flush, weak=Fals
     B.check_device(c, stream)
     t_e2e = max_over_ranks(sum(a.elapsed_ms(b) for a, b in e2e_evs) * 1e-3)
     # the plugin call computed the same bits as the device-resident runs
-    e2e_res = pin_res if comm is not None else pin_out
+    if peer is not None:
+        peer.check(stream)
+    e2e_res = pin_res if peer is not None else pin_out
     assert np.array_equal(e2e_res, h, equal_nan=True), (e2e_res, h)
     n_launch = c.num_launches()
     for b in in_bufs:
@@ -668,9 +673,9 @@ def measure_greeks(args, dtype, rank, world, local, dist, comm, flush, weak=Fals
     B.release(c)
     paths_all = per * world
     return {"value": paths_all * args.steps / t_dev, "t_dev": t_dev, "ms_per_step": 1e3 * t_dev / args.steps,
-            "e2e": paths_all * args.steps / t_e2e, "h2d": h2d + (4 * esz if comm is not None else 0),
+            "e2e": paths_all * args.steps / t_e2e, "h2d": h2d + (4 * esz if peer is not None else 0),
             # the four results, the program's 4-byte error word, and on N > 1 the all-reduced results
-            "d2h": 4 * esz + 4 + (4 * esz if comm is not None else 0), "outs": outs, "clocks": clk,
+            "d2h": 4 * esz + 4 + (4 * esz if peer is not None else 0), "outs": outs, "clocks": clk,
             "launches": n_launch, "paths_per_rank": per}
 
 
@@ -772,6 +777,7 @@ def measure_mlp_dp(rank, world, local, dist, comm, flush, pk):
 
 def run_ours(args):
     from cudacaml_b200 import examples as X
+    from cudacaml_b200 import multi as M
     from cudacaml_b200 import runtime as R
     from cudacaml_b200.ir import F32, F64
 
@@ -826,15 +832,25 @@ def run_ours(args):
         if rc != 0:
             raise RuntimeError(R.lib().ccb_last_error().decode())
 
-    head = measure_greeks(args, F64, rank, world, local, dist, comm, flush)
+    # The four scalar results of every step are summed across the ranks over
+    # NVLink peer memory (PeerSum: one 32-thread kernel per rank, mailboxes
+    # mapped through CUDA IPC); NCCL stays for the MLP step's gradients.
+    peer = None
+    if world > 1:
+        def exchange(h):
+            got = [None] * world
+            dist.all_gather_object(got, h)
+            return got
+        peer = M.PeerSum(world, rank, exchange)
+    head = measure_greeks(args, F64, rank, world, local, dist, peer, flush)
     cf = X.analytic()
     ok = abs(head["outs"]["price"] - cf["price"]) < 0.02
     f32 = None
     if world == 1 and not args.no_secondary:
-        f32 = measure_greeks(args, F32, rank, world, local, dist, comm, flush)
+        f32 = measure_greeks(args, F32, rank, world, local, dist, peer, flush)
     secondary = None
     if world > 1 and not args.no_secondary:
-        weak = measure_greeks(args, F64, rank, world, local, dist, comm, flush, weak=True)
+        weak = measure_greeks(args, F64, rank, world, local, dist, peer, flush, weak=True)
         try:
             mlp = measure_mlp_dp(rank, world, local, dist, comm, flush, pk)
         except Exception as e:  # noqa: BLE001 - reported, not fatal to the headline
@@ -845,7 +861,7 @@ def run_ours(args):
                                        "ms_per_step": weak["ms_per_step"], "paths_per_gpu": weak["paths_per_rank"],
                                        "result": weak["outs"],
                                        "note": "weak scaling: every rank prices 2^28 paths of its own "
-                                               "(counters [r*2^28, (r+1)*2^28)), 4-scalar NCCL all-reduce per step"},
+                                               "(counters [r*2^28, (r+1)*2^28)), 4 scalars summed across ranks per step"},
                 f"mlp_step_8192x4096x8192x1024_tf32_dp{world}": mlp}
     if rank == 0 and world == 1 and not args.no_secondary:
         secondary = secondary_hbm(local, None, flush, pk)
@@ -878,7 +894,7 @@ def run_ours(args):
                         f"{head['paths_per_rank']} paths per launch / the average step, against 148 SMs x 4 "
                         f"sub-partitions x 1 warp instruction/cycle x {pk['sm_max_mhz']:.0f} MHz ({pk['src']} max "
                         f"clock); traffic = DRAM bytes per launch from the same ncu capture"
-                        + ("; the step includes the 4-scalar NCCL all-reduce" if world > 1 else "")}
+                        + ("; the step includes the cross-rank sum of the 4 scalars" if world > 1 else "")}
     if rank == 0:
         line = {
             "metric": "MC paths/s (Black-Scholes price + pathwise Greeks)", "value": head["value"], "unit": "paths/s",
@@ -887,8 +903,8 @@ def run_ours(args):
             "data": "synthetic (Philox normals generated in registers, seed 42)",
             "config": {"workload": "bs_greeks_f64 (BASELINE configs[1]; F32 under secondary)", "paths_total": PATHS,
                        "paths_per_gpu": head["paths_per_rank"],
-                       "parallelism": (f"dp{world} (counter range split {world} ways as Multi does, NCCL all-reduce "
-                                       f"of 4 scalars per step)") if world > 1 else "dp1",
+                       "parallelism": (f"dp{world} (counter range split {world} ways as Multi does, the 4 scalar "
+                                       f"results summed across ranks over NVLink peer memory per step)") if world > 1 else "dp1",
                        "l2": "flushed before every timed step (read-only pass over 256 MiB, twice L2)",
                        "market": "S0=100 K=100 r=0.05 sigma=0.2 T=1"},
             "result": head["outs"], "result_ok_vs_closed_form": ok, "closed_form": cf,
@@ -898,7 +914,7 @@ def run_ours(args):
             "e2e": {"value": head["e2e"], "unit": "paths/s", "h2d_bytes_per_step": head["h2d"],
                     "d2h_bytes_per_step": head["d2h"],
                     "path": "ccb_program_enqueue + ccb_program_wait with page-locked host buffers"
-                            + (" + NCCL all-reduce of the results" if world > 1 else "")},
+                            + (" + the cross-rank sum of the results" if world > 1 else "")},
         }
         if world == 1:
             line["cpu_baseline"] = cpu_baseline_sample()
@@ -907,6 +923,8 @@ def run_ours(args):
         print(json.dumps(line), flush=True)
     if dist is not None:
         dist.barrier()
+        if peer is not None:
+            peer.close()
         if comm is not None:
             R.lib().ccb_comm_destroy(comm)
         dist.destroy_process_group()

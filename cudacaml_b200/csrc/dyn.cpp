@@ -74,6 +74,11 @@ const Driver& driver() {
     S(cuModuleGetFunction, "cuModuleGetFunction")
     S(cuLaunchKernel, "cuLaunchKernel")
     S(cuFuncGetParamInfo, "cuFuncGetParamInfo")
+    S(cuIpcGetMemHandle, "cuIpcGetMemHandle")
+    S(cuIpcOpenMemHandle, "cuIpcOpenMemHandle_v2")
+    S(cuIpcCloseMemHandle, "cuIpcCloseMemHandle")
+    S(cuDeviceCanAccessPeer, "cuDeviceCanAccessPeer")
+    S(cuCtxEnablePeerAccess, "cuCtxEnablePeerAccess")
     S(cuFuncSetAttribute, "cuFuncSetAttribute")
     S(cuFuncGetAttribute, "cuFuncGetAttribute")
     S(cuOccupancyMaxActiveBlocksPerMultiprocessor, "cuOccupancyMaxActiveBlocksPerMultiprocessor")

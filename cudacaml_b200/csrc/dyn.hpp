@@ -51,6 +51,11 @@ struct Driver {
   CCB_DRV(cuModuleGetFunction)
   CCB_DRV(cuLaunchKernel)
   CCB_DRV(cuFuncGetParamInfo)
+  CCB_DRV(cuIpcGetMemHandle)
+  CCB_DRV(cuIpcOpenMemHandle)
+  CCB_DRV(cuIpcCloseMemHandle)
+  CCB_DRV(cuDeviceCanAccessPeer)
+  CCB_DRV(cuCtxEnablePeerAccess)
   CCB_DRV(cuFuncSetAttribute)
   CCB_DRV(cuFuncGetAttribute)
   CCB_DRV(cuOccupancyMaxActiveBlocksPerMultiprocessor)

@@ -245,6 +245,53 @@ int ccb_host_free(void* hptr) {
   return CCB_OK;
 }
 
+// ---------------------------------------------------------------- peer memory
+int ccb_ipc_mem_handle(void* dptr, unsigned char handle[64]) {
+  if (!dptr || !handle) return fail(CCB_ERR_INVALID, "ccb_ipc_mem_handle: null pointer");
+  CCB_TRY(ensure_current());
+  CUipcMemHandle h;
+  CCB_CU(driver().cuIpcGetMemHandle(&h, (CUdeviceptr)dptr));
+  std::memcpy(handle, h.reserved, 64);
+  return CCB_OK;
+}
+
+int ccb_ipc_mem_open(const unsigned char handle[64], void** dptr) {
+  if (!dptr || !handle) return fail(CCB_ERR_INVALID, "ccb_ipc_mem_open: null pointer");
+  CCB_TRY(ensure_current());
+  CUipcMemHandle h;
+  std::memcpy(h.reserved, handle, 64);
+  CUdeviceptr p = 0;
+  CCB_CU(driver().cuIpcOpenMemHandle(&p, h, CU_IPC_MEM_LAZY_ENABLE_PEER_ACCESS));
+  *dptr = (void*)p;
+  return CCB_OK;
+}
+
+int ccb_ipc_mem_close(void* dptr) {
+  if (!dptr) return CCB_OK;
+  CCB_TRY(ensure_current());
+  CCB_CU(driver().cuIpcCloseMemHandle((CUdeviceptr)dptr));
+  return CCB_OK;
+}
+
+int ccb_peer_access_enable(int peer) {
+  CCB_TRY(ensure_current());
+  const int self = current_device();
+  if (peer == self) return CCB_OK;
+  CCB_TRY(ensure_context(peer));  // retain the peer's primary context
+  CUcontext peer_ctx = nullptr;
+  CCB_CU(driver().cuCtxGetCurrent(&peer_ctx));
+  CCB_TRY(ensure_context(self));
+  CUdevice a, b;
+  CCB_CU(driver().cuDeviceGet(&a, self));
+  CCB_CU(driver().cuDeviceGet(&b, peer));
+  int can = 0;
+  CCB_CU(driver().cuDeviceCanAccessPeer(&can, a, b));
+  if (!can) return fail(CCB_ERR_UNSUPPORTED, "device " + std::to_string(self) + " cannot access device " + std::to_string(peer));
+  const CUresult r = driver().cuCtxEnablePeerAccess(peer_ctx, 0);
+  if (r != CUDA_SUCCESS && r != CUDA_ERROR_PEER_ACCESS_ALREADY_ENABLED) return cu_fail(r, "cuCtxEnablePeerAccess");
+  return CCB_OK;
+}
+
 int ccb_stream_create(ccb_stream_t* s) {
   CCB_TRY(ensure_current());
   CUstream st;

@@ -16,8 +16,9 @@ Additions, all opt-in:
   add a scalar ``__ctr_base`` parameter (the device's first path) to every
   per-path Rng counter, scaled by the draw's elements per path, so
   multi-step grids split correctly too.
-* ``allreduce_mean(names, inputs)`` recombines scalar outputs with one NCCL
-  all-reduce over NVLink instead of a host loop.
+* ``allreduce_mean(names, inputs)`` recombines scalar outputs on the devices
+  with a cross-device sum over NVLink peer memory (``PeerSum``) instead of a
+  host loop.
 * ``allreduce_sum(names, inputs)`` sums whole outputs across the devices on
   the devices (one NCCL all-reduce per output, grouped): a loss and the weight
   gradients of a batch split by rows, as in the MLP training step.
@@ -127,6 +128,112 @@ def mean_scalar(values) -> float:
     return sum(float(v.data[0]) for v in values) / len(values)
 
 
+class PeerSum:
+    """Cross-rank sum of a few scalars over NVLink peer memory
+    (ccb_xrank_sum), for ranks on distinct GPUs of one box: one 32-thread
+    kernel per rank writes its values into every rank's mailbox and sums
+    what arrives, in rank order, so every rank gets the same bits. It
+    replaces a library all-reduce of the 4 scalars a split Monte-Carlo run
+    recombines per step, whose launch and protocol latency grows with the
+    rank count.
+
+    ``PeerSum(nranks, rank, exchange)``: one process per rank. The mailbox is
+    allocated and zero-filled here, then ``exchange(handle_bytes)`` must
+    return every rank's 64-byte IPC handle in rank order (for example
+    ``torch.distributed.all_gather_object``); it is a collective, so no rank
+    can write into a mailbox that its owner has not zeroed yet.
+    ``PeerSum.in_process(devices)``: one process driving several GPUs, each
+    device a rank, peer access enabled between them.
+    """
+
+    ERR_XRANK = 32
+
+    def __init__(self, nranks, rank, exchange=None, _devices=None):
+        L = R.lib()
+        self.nranks, self.rank = nranks, rank
+        self.epoch = 0
+        size = ctypes.c_size_t()
+        R.check(L.ccb_xrank_mailbox_bytes(nranks, ctypes.byref(size)))
+        self._opened = []
+        if _devices is None:
+            self.own = R.Buffer(size.value)
+            R.check(L.ccb_memset_d8(self.own.ptr, 0, size.value, None))
+            self.err = R.Buffer(4)
+            R.check(L.ccb_memset_d8(self.err.ptr, 0, 4, None))
+            R.check(L.ccb_stream_synchronize(None))
+            h = (ctypes.c_ubyte * 64)()
+            R.check(L.ccb_ipc_mem_handle(self.own.ptr, h))
+            handles = exchange(bytes(h))
+            ptrs = []
+            for q, hq in enumerate(handles):
+                if q == rank:
+                    ptrs.append(self.own.ptr)
+                    continue
+                p = ctypes.c_void_p()
+                R.check(L.ccb_ipc_mem_open((ctypes.c_ubyte * 64).from_buffer_copy(hq), ctypes.byref(p)))
+                self._opened.append(p.value)
+                ptrs.append(p.value)
+            self.mailboxes = (ctypes.c_void_p * nranks)(*ptrs)
+            self.devices = None
+
+    @classmethod
+    def in_process(cls, devices):
+        """One PeerSum per device of ``devices`` (distinct ordinals), sharing
+        mailboxes through peer access; returns the list, rank = position."""
+        devices = list(devices)
+        if len(set(devices)) != len(devices):
+            raise ValueError("PeerSum: every rank needs its own GPU")
+        L = R.lib()
+        n = len(devices)
+        size = ctypes.c_size_t()
+        R.check(L.ccb_xrank_mailbox_bytes(n, ctypes.byref(size)))
+        own, errs = [], []
+        for d in devices:
+            with R.with_device(d):
+                for q in devices:
+                    if q != d:
+                        R.check(L.ccb_peer_access_enable(q))
+                b, e = R.Buffer(size.value), R.Buffer(4)
+                R.check(L.ccb_memset_d8(b.ptr, 0, size.value, None))
+                R.check(L.ccb_memset_d8(e.ptr, 0, 4, None))
+                R.check(L.ccb_stream_synchronize(None))
+                own.append(b)
+                errs.append(e)
+        out = []
+        for r, d in enumerate(devices):
+            ps = cls(n, r, _devices=devices)
+            ps.own, ps.err, ps.devices = own[r], errs[r], devices
+            ps.mailboxes = (ctypes.c_void_p * n)(*[b.ptr for b in own])
+            out.append(ps)
+        return out
+
+    def sum(self, in_ptr, out_ptr, count, dtype_code, stream=None):
+        """Issue one sum on ``stream`` (the current device must be this
+        rank's); every rank must issue the same sums in the same order."""
+        self.epoch += 1
+        R.check(R.lib().ccb_xrank_sum(in_ptr, out_ptr, count, dtype_code, self.nranks, self.rank, self.mailboxes,
+                                      self.epoch, self.err.ptr, stream))
+
+    def check(self, stream=None):
+        """Synchronise ``stream`` and raise if a wait gave up."""
+        R.check(R.lib().ccb_stream_synchronize(stream))
+        w = np.empty(1, np.uint32)
+        self.err.download(w)
+        if int(w[0]) & self.ERR_XRANK:
+            raise R.CcbError("cross-rank sum: a peer did not publish its values (bounded wait gave up)")
+
+    def close(self):
+        """Unmap the peers' mailboxes and free this rank's. Every rank must
+        have finished its last sum (synchronised) first."""
+        for p in self._opened:
+            R.lib().ccb_ipc_mem_close(p)
+        self._opened = []
+        if getattr(self, "own", None) is not None:
+            self.own.free()
+            self.err.free()
+            self.own = None
+
+
 class Multi:
     def __init__(self, devices, n: int, build, counter_key: str | None = None, split=None, matmul=None):
         devices = list(devices)
@@ -184,15 +291,70 @@ class Multi:
         return self.run_per_device(lambda i: self._inputs_for(i, inputs))
 
     def allreduce_mean(self, names, inputs):
-        """Run every device resident, all-reduce the named scalar outputs with
-        NCCL (sum) across devices, and return {name: sum / d}. Needs distinct
-        device ordinals (NCCL puts one rank on each GPU)."""
-        d = len(self.devices)
-        sums = self.allreduce_sum(names, inputs)
-        for name, v in sums.items():
-            if v.numel != 1:
+        """Run every device resident, sum the named scalar outputs across the
+        devices on the devices, and return {name: sum / d}. The sum runs over
+        NVLink peer memory (PeerSum: one small kernel per device, every
+        device gets the same bits). Needs distinct device ordinals."""
+        if self.released:
+            raise RuntimeError("Multi.run: this Multi.t has been released")
+        if len(set(self.devices)) != len(self.devices):
+            raise ValueError("Multi.allreduce: a cross-device sum needs distinct devices; use mean_scalar for repeats")
+        outs = self.slots[0].outputs
+        for name in names:
+            js = [k for k, (n, _, shape) in enumerate(outs) if n == name]
+            if not js:
+                raise ValueError(f"Multi.allreduce: no output named {name}")
+            if numel(outs[js[0]][2]) != 1:
                 raise ValueError(f"Multi.allreduce_mean: output {name} is not a scalar")
-        return {name: float(v.data[0]) / d for name, v in sums.items()}
+        d = len(self.devices)
+        if getattr(self, "_peer", None) is None:
+            self._peer = PeerSum.in_process(self.devices)
+        inputs = list(inputs)
+        keep = self._run_all_resident(inputs)
+        for name in names:
+            j = [k for k, (n, _, _) in enumerate(outs) if n == name][0]
+            dt = outs[j][1]
+            for i, c in enumerate(self.slots):
+                with R.with_device(c.device):
+                    ptr = keep[i][1][j].ptr
+                    self._peer[i].sum(ptr, ptr, 1, R.DT_CODE[dt.value], c.lane_stream(0))
+        result = {}
+        for i, c in enumerate(self.slots):
+            with R.with_device(c.device):
+                self._peer[i].check(c.lane_stream(0))
+                B.check_device(c, c.lane_stream(0))
+        for name in names:
+            j = [k for k, (n, _, _) in enumerate(outs) if n == name][0]
+            dt = outs[j][1]
+            host = np.empty(1, dtype=dt.np)
+            with R.with_device(self.slots[0].device):
+                keep[0][1][j].download(host)
+            result[name] = float(host[0]) / d
+        self._free_resident(keep)
+        return result
+
+    def _run_all_resident(self, inputs):
+        """Upload every device's inputs and run it resident on its lane
+        stream; returns [(input buffers, output buffers)] per device."""
+        keep = []
+        for i, c in enumerate(self.slots):
+            with R.with_device(c.device):
+                bound = dict(self._inputs_for(i, inputs))
+                in_bufs = []
+                for pname, dt, shape in c.params:
+                    buf = R.Buffer(bound[pname].byte_size)
+                    buf.upload(bound[pname].data)
+                    in_bufs.append(buf)
+                out_bufs = [R.Buffer(numel(shape) * dt.size_in_bytes) for _, dt, shape in c.outputs]
+                B.run_device_ptrs(c, [b.ptr for b in in_bufs], [b.ptr for b in out_bufs], c.lane_stream(0))
+                keep.append((in_bufs, out_bufs))
+        return keep
+
+    def _free_resident(self, keep):
+        for c, (ib, ob) in zip(self.slots, keep):
+            with R.with_device(c.device):
+                for b in ib + ob:
+                    b.free()
 
     def allreduce_sum(self, names, inputs):
         """Run every device resident, all-reduce the named outputs with NCCL
@@ -215,20 +377,8 @@ class Multi:
             R.check(L.ccb_comm_init_all(d, arr, comms))
             self._comms = [comms[i] for i in range(d)]
         inputs = list(inputs)
-        outs_dev = []
-        keep = []
-        for i, c in enumerate(self.slots):
-            with R.with_device(c.device):
-                bound = dict(self._inputs_for(i, inputs))
-                in_bufs = []
-                for pname, dt, shape in c.params:
-                    buf = R.Buffer(bound[pname].byte_size)
-                    buf.upload(bound[pname].data)
-                    in_bufs.append(buf)
-                out_bufs = [R.Buffer(numel(shape) * dt.size_in_bytes) for _, dt, shape in c.outputs]
-                B.run_device_ptrs(c, [b.ptr for b in in_bufs], [b.ptr for b in out_bufs], c.lane_stream(0))
-                keep.append((in_bufs, out_bufs))
-                outs_dev.append(out_bufs)
+        keep = self._run_all_resident(inputs)
+        outs_dev = [ob for _, ob in keep]
         result = {}
         for name in names:
             j = [k for k, (n, _, _) in enumerate(self.slots[0].outputs) if n == name][0]
@@ -247,10 +397,7 @@ class Multi:
             with R.with_device(self.slots[0].device):
                 outs_dev[0][j].download(host)
             result[name] = Value(dt, tuple(shape), host)
-        for c, (ib, ob) in zip(self.slots, keep):
-            with R.with_device(c.device):
-                for b in ib + ob:
-                    b.free()
+        self._free_resident(keep)
         return result
 
     def release(self):
@@ -258,6 +405,10 @@ class Multi:
             self.released = True
             for c in self.slots:
                 B.release(c)
+            for ps in getattr(self, "_peer", None) or []:
+                with R.with_device(self.devices[ps.rank]):
+                    ps.close()
+            self._peer = None
             if self._comms:
                 for h in self._comms:
                     R.lib().ccb_comm_destroy(h)

@@ -111,6 +111,12 @@ def _declare(L):
         "ccb_comm_destroy": (I, [P]),
         "ccb_allreduce": (I, [P, P, P, SZ, I, I, P]),
         "ccb_sum_f32_noalloc": (I, [P, c.c_longlong, P, P]),
+        "ccb_ipc_mem_handle": (I, [P, c.POINTER(c.c_ubyte)]),
+        "ccb_ipc_mem_open": (I, [c.POINTER(c.c_ubyte), c.POINTER(P)]),
+        "ccb_ipc_mem_close": (I, [P]),
+        "ccb_peer_access_enable": (I, [I]),
+        "ccb_xrank_mailbox_bytes": (I, [I, c.POINTER(SZ)]),
+        "ccb_xrank_sum": (I, [P, P, I, I, I, I, c.POINTER(P), c.c_ulonglong, P, P]),
         "ccb_group_start": (I, []),
         "ccb_group_end": (I, []),
         "ccb_graph_begin": (I, [P]),

@@ -204,6 +204,34 @@ int ccb_graph_destroy(ccb_graph_t graph);
  * CCB_ERR_DRIVER, with the message in ccb_last_error(). */
 int ccb_sum_f32_noalloc(const float* x, long long n, float* out, void* stream);
 
+/* ---------------------------------------------------------------- peer memory and the cross-rank sum
+ * New: the reference has no collective (lib/backend_cuda/multi.ml:51-109
+ * combines per-device results on the host). A rank exports a device
+ * allocation of its own with ccb_ipc_mem_handle (64 opaque bytes, cuIpc),
+ * another process of the same box maps it with ccb_ipc_mem_open (peer access
+ * over NVLink enabled lazily) and unmaps it with ccb_ipc_mem_close. In one
+ * process, ccb_peer_access_enable(peer) lets the current device read and
+ * write `peer`'s allocations directly. */
+int ccb_ipc_mem_handle(void* dptr, unsigned char handle[64]);
+int ccb_ipc_mem_open(const unsigned char handle[64], void** dptr);
+int ccb_ipc_mem_close(void* dptr);
+int ccb_peer_access_enable(int peer);
+/* out[k] = sum over ranks r = 0..nranks-1, in rank order, of rank r's in[k],
+ * k < count <= 8, dtype codes as above, for ranks on distinct GPUs of one box:
+ * one 32-thread kernel per rank on `stream` writes this rank's values into
+ * every rank's mailbox over peer memory and sums what the local mailbox
+ * receives (so every rank gets the same bits). mailboxes[q] is rank q's
+ * mailbox as this rank addresses it (ccb_xrank_mailbox_bytes(nranks) bytes,
+ * zero-filled by its owner before any rank's first call), nranks <= 16.
+ * `epoch` is the same on every rank for one sum and increases from 1 with
+ * every call. A peer that never publishes makes the bounded wait give up:
+ * bit 32 is raised in the device word *err and `out` is left untouched. Two
+ * ranks must never share one GPU (their kernels wait on each other). No
+ * counterpart in the reference. */
+int ccb_xrank_mailbox_bytes(int nranks, size_t* bytes);
+int ccb_xrank_sum(const void* in, void* out, int count, int dtype, int nranks, int rank, void* const* mailboxes,
+                  unsigned long long epoch, unsigned* err, void* stream);
+
 /* ---------------------------------------------------------------- NCCL
  * New: the reference has no collective (lib/backend_cuda/multi.ml:51-109
  * combines on the host). Multi recombines per-device partial results with an

@@ -156,6 +156,19 @@ let graph_destroy = fn "ccb_graph_destroy" (handle @-> returning int)
 (* ---------------------------------------------------------------- allocation-free sum (no reference counterpart) *)
 let sum_f32_noalloc = fn "ccb_sum_f32_noalloc" (ptr float @-> llong @-> ptr float @-> handle @-> returning int)
 
+(* ---------------------------------------------------------------- peer memory and the cross-rank sum
+   (no reference counterpart) *)
+let ipc_mem_handle = fn "ccb_ipc_mem_handle" (ptr void @-> ptr uchar @-> returning int)
+let ipc_mem_open = fn "ccb_ipc_mem_open" (ptr uchar @-> ptr (ptr void) @-> returning int)
+let ipc_mem_close = fn "ccb_ipc_mem_close" (ptr void @-> returning int)
+let peer_access_enable = fn "ccb_peer_access_enable" (int @-> returning int)
+let xrank_mailbox_bytes = fn "ccb_xrank_mailbox_bytes" (int @-> ptr size_t @-> returning int)
+
+let xrank_sum =
+  fn "ccb_xrank_sum"
+    (ptr void @-> ptr void @-> int @-> int @-> int @-> int @-> ptr (ptr void) @-> ullong @-> ptr uint @-> handle
+   @-> returning int)
+
 (* ---------------------------------------------------------------- NCCL (no reference counterpart:
    lib/backend_cuda/multi.ml:51-109 combines on the host) *)
 let comm_init_all = fn "ccb_comm_init_all" (int @-> ptr int @-> ptr handle @-> returning int)

@@ -12,8 +12,10 @@
      the same seed (device d draws counters [d*n/D, (d+1)*n/D)) instead of
      asking the caller to reseed each device (multi.mli:39-44);
    - [?split]: slice only the named inputs by rows;
-   - [allreduce_sum] / [allreduce_mean]: recombine outputs on the devices
-     with NCCL (ccb_allreduce inside ccb_group_start/end) over NVLink. *)
+   - [allreduce_sum]: recombine whole outputs on the devices with NCCL
+     (ccb_allreduce inside ccb_group_start/end) over NVLink;
+   - [allreduce_mean]: recombine scalar outputs with the cross-device sum
+     over NVLink peer memory (ccb_xrank_sum). *)
 
 open Cudacaml_ir
 open Cudacaml_runtime
@@ -270,6 +272,85 @@ let allreduce_sum t ~names ~inputs =
     t.slots;
   result
 
+(* Scalar outputs are recombined over NVLink peer memory instead: one
+   mailbox per device (zero-filled before any device's first sum), peer
+   access between the devices, then per named output one ccb_xrank_sum per
+   device (a 32-thread kernel; every device gets the same bits). *)
+type peer = { boxes : unit Ctypes.ptr Ctypes.CArray.t; errs : Buffer.t array; owned : Buffer.t array;
+              mutable epoch : int }
+
+let peers : (int list, peer) Hashtbl.t = Hashtbl.create 4
+
+let peer_of ords =
+  let key = Array.to_list ords in
+  match Hashtbl.find_opt peers key with
+  | Some p -> p
+  | None ->
+      let n = Array.length ords in
+      let bytes = Ccb.out Ctypes.size_t (fun p -> Ccb.check "ccb_xrank_mailbox_bytes" (!!Ccb.xrank_mailbox_bytes n p)) in
+      let bytes = Unsigned.Size_t.to_int bytes in
+      let owned, errs =
+        Array.split
+          (Array.map
+             (fun d ->
+               Device.with_device d (fun () ->
+                   Array.iter (fun q -> if q <> d then Ccb.check "ccb_peer_access_enable" (!!Ccb.peer_access_enable q)) ords;
+                   let b = Buffer.alloc ~bytes and e = Buffer.alloc ~bytes:4 in
+                   Ccb.check "ccb_memset_d8" (!!Ccb.memset_d8 (Buffer.unsafe_ptr b) (Unsigned.UChar.of_int 0) (Unsigned.Size_t.of_int bytes) Stream.default);
+                   Ccb.check "ccb_memset_d8" (!!Ccb.memset_d8 (Buffer.unsafe_ptr e) (Unsigned.UChar.of_int 0) (Unsigned.Size_t.of_int 4) Stream.default);
+                   Device.synchronize ();
+                   (b, e)))
+             ords)
+      in
+      let boxes = Ctypes.CArray.of_list (Ctypes.ptr Ctypes.void) (Array.to_list (Array.map Buffer.unsafe_ptr owned)) in
+      let p = { boxes; errs; owned; epoch = 0 } in
+      Hashtbl.add peers key p;
+      p
+
 let allreduce_mean t ~names ~inputs =
-  let d = float_of_int (Array.length t.slots) in
-  List.map (fun (n, v) -> (n, scalar_float v /. d)) (allreduce_sum t ~names ~inputs)
+  if t.released then failwith "Multi.run: this Multi.t has been released";
+  let ords = Array.map fst t.slots in
+  if List.length (List.sort_uniq compare (Array.to_list ords)) <> Array.length ords then
+    invalid_arg "Multi.allreduce: a cross-device sum needs distinct devices; use mean_scalar for repeats";
+  let n = Array.length ords in
+  let pe = peer_of ords in
+  let per_dev =
+    Array.mapi
+      (fun i (_, c) ->
+        let ins = List.map (fun (nm, v) -> (nm, B.upload v)) (inputs_for t i inputs) in
+        let outs = B.run_resident c ~inputs:ins in
+        List.iter (fun (_, r) -> B.free_resident r) ins;
+        outs)
+      t.slots
+  in
+  List.iter
+    (fun name ->
+      pe.epoch <- pe.epoch + 1;
+      Array.iteri
+        (fun i ordinal ->
+          let r = List.assoc name per_dev.(i) in
+          if Shape.numel r.B.shape <> 1 then invalid_arg ("Multi.allreduce_mean: output " ^ name ^ " is not a scalar");
+          let code = match r.B.dtype with Dtype.P dt -> Ccb.dtype_code dt in
+          Device.with_device ordinal (fun () ->
+              let p = Buffer.unsafe_ptr r.B.buf in
+              Ccb.check "ccb_xrank_sum"
+                (!!Ccb.xrank_sum p p 1 code n i (Ctypes.CArray.start pe.boxes) (Unsigned.ULLong.of_int pe.epoch)
+                   (Ctypes.from_voidp Ctypes.uint (Buffer.unsafe_ptr pe.errs.(i))) Stream.default)))
+        ords)
+    names;
+  Array.iter (fun d -> Device.with_device d Device.synchronize) ords;
+  Array.iteri
+    (fun i d ->
+      Device.with_device d (fun () ->
+          let w = Value.create Dtype.I32 (Shape.of_dims [ 1 ]) in
+          Buffer.download pe.errs.(i) (Value.P w);
+          if Int32.logand (Value.get w 0) 32l <> 0l then failwith "Multi.allreduce_mean: a peer did not publish (bounded wait gave up)"))
+    ords;
+  let result =
+    List.map
+      (fun name ->
+        (name, scalar_float (Device.with_device ords.(0) (fun () -> B.download (List.assoc name per_dev.(0)))) /. float_of_int n))
+      names
+  in
+  Array.iteri (fun i d -> Device.with_device d (fun () -> List.iter (fun (_, r) -> B.free_resident r) per_dev.(i))) ords;
+  result
