@@ -117,13 +117,30 @@ __device__ __forceinline__ void reduce_finish(const typename F::P& p, typename F
   if (!am_last) return;
   // Last block: every partial is published. Fold them in a fixed order
   // (thread t takes blocks t, t+B, ... ascending, then the ordered tree), so
-  // the result is reproducible for a given grid.
+  // the result is reproducible for a given grid. The partials of KB blocks
+  // are loaded before any is combined, so their L2 round trips overlap: this
+  // fold is the serial tail of every launch (one round trip instead of KB).
   __threadfence();
+  constexpr int WORDS = R * (int)(sizeof(T) / 4);
+  constexpr int KB = WORDS >= 32 ? 1 : (32 / WORDS > 8 ? 8 : 32 / WORDS);
+  const unsigned G = gridDim.x;
 #pragma unroll
-  for (int r = 0; r < R; ++r) {
-    T v = F::identity(r);
-    for (unsigned b = threadIdx.x; b < gridDim.x; b += blockDim.x) v = F::combine(r, v, ld_cg(&p.partials[(u64)b * R + r]));
-    acc[r] = v;
+  for (int r = 0; r < R; ++r) acc[r] = F::identity(r);
+  for (unsigned b0 = threadIdx.x; b0 < G; b0 += KB * blockDim.x) {
+    T x[KB][R];
+#pragma unroll
+    for (int k = 0; k < KB; ++k) {
+      const unsigned b = b0 + k * blockDim.x;
+#pragma unroll
+      for (int r = 0; r < R; ++r) x[k][r] = b < G ? ld_cg(&p.partials[(u64)b * R + r]) : F::identity(r);
+    }
+#pragma unroll
+    for (int k = 0; k < KB; ++k) {
+      if (b0 + k * blockDim.x < G) {
+#pragma unroll
+        for (int r = 0; r < R; ++r) acc[r] = F::combine(r, acc[r], x[k][r]);
+      }
+    }
   }
   __syncthreads();
 #pragma unroll
