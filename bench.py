@@ -6,18 +6,23 @@ configs[1]). F64 is the headline because at 2^28 paths the reference's own F32
 normal generator produces a few infinite normals (see "secondary"). One step =
 one run of the Greeks graph (one fused forward+adjoint launch) plus, on N > 1
 GPUs, the cross-rank sum that recombines the four scalar outputs over NVLink
-peer memory (multi.PeerSum, one 32-thread kernel per rank).
+peer memory inside that same kernel.
 
-Scaling is strong, as BASELINE configs[1] states it: the 2^28 paths are split
-N ways by counter range with the same seed, rank r pricing counters
-[r*2^28/N, (r+1)*2^28/N) -- the split Multi(..., counter_key="seed") makes
-(multi.path_range). Weak scaling (2^28 paths per rank) is reported under
-"secondary" for N > 1.
+Scaling is strong, as BASELINE configs[1] states it: on N > 1 GPUs every rank
+compiles the unsplit 2^28-path graph as one rank of a sharded program
+(compile_on(..., shard=(r, N))): rank r prices counters
+[r*2^28/N, (r+1)*2^28/N) with the same seed -- the split
+Multi(..., counter_key="seed") makes (multi.path_range) -- and the kernel's
+last block combines the four totals of all ranks over NVLink peer memory
+(multi.ShardPeers), so each step is one launch per GPU and every rank ends it
+with the whole run's results. Weak scaling (2^28 paths per rank, the results
+summed after the kernel by multi.PeerSum) is reported under "secondary" for
+N > 1.
 
 `value` is device-timed with the inputs resident; `e2e` is the same metric
 through the plugin call a user makes, ccb_program_enqueue + ccb_program_wait
-with page-locked host inputs and outputs (Backend_cuda.run_async/wait), plus
-on N > 1 the all-reduce of the downloaded results, every step.
+with page-locked host inputs and outputs (Backend_cuda.run_async/wait), every
+step (on N > 1 the results it downloads are already the whole run's).
 
 Also measured in the same run (reported under "secondary"): the flat reduce
 and inclusive scan over 2^28 values, F32 ~N(0,1) and I32 U[0,16) (HBM GB/s as
@@ -551,26 +556,37 @@ def secondary_reference_nvrtc(dev, flush, ours):
     return res
 
 
-def measure_greeks(args, dtype, rank, world, local, dist, peer, flush, weak=False):
+def measure_greeks(args, dtype, rank, world, local, dist, peer, flush, weak=False, exchange=None):
     """Device-timed and end-to-end paths/s of the Greeks graph in `dtype`.
 
-    Strong scaling (default): the PATHS paths are split `world` ways by
-    counter range, rank r pricing counters [r*PATHS/world, (r+1)*PATHS/world)
-    with the same seed -- Multi's split (multi.path_range, offset_counters
-    with rows = the per-rank count). weak=True gives every rank PATHS paths of
-    its own (counters [r*PATHS, (r+1)*PATHS), which must stay below 2^31)."""
+    Strong scaling (default): the unsplit 2^28-path graph compiled as rank r
+    of a sharded program (shard=(r, world)): the kernel walks paths
+    [r*PATHS/world, (r+1)*PATHS/world) -- the counters Multi's split gives
+    rank r -- and its last block combines all ranks' totals over NVLink peer
+    memory (multi.ShardPeers), so every rank ends each step with the whole
+    run's results and no collective follows. weak=True gives every rank
+    PATHS paths of its own (counters [r*PATHS, (r+1)*PATHS), which must stay
+    below 2^31, offset_counters) and sums the four results across the ranks
+    after the kernel (multi.PeerSum)."""
     import numpy as np
     from cudacaml_b200 import backend_cuda as B
     from cudacaml_b200 import examples as X
     from cudacaml_b200 import multi as M
     from cudacaml_b200 import runtime as R
 
+    sharded = world > 1 and not weak
     total = PATHS * world if weak else PATHS
     base, per = M.path_range(total, world, rank)
-    g = X.call_greeks(per, dtype)
-    if world > 1:
-        g = M.offset_counters(g, "seed", rows=per)
-    c = B.compile_on(local, g)
+    shard_peers = None
+    if sharded:
+        c = B.compile_on(local, X.call_greeks(PATHS, dtype), shard=(rank, world))
+        shard_peers = M.ShardPeers(c, exchange)
+        peer = None
+    else:
+        g = X.call_greeks(per, dtype)
+        if world > 1:
+            g = M.offset_counters(g, "seed", rows=per)
+        c = B.compile_on(local, g)
     stream = c.lane_stream(0)
     fnp = dtype.np
     esz = np.dtype(fnp).itemsize
@@ -670,6 +686,9 @@ def measure_greeks(args, dtype, rank, world, local, dist, peer, flush, weak=Fals
     for b in in_bufs:
         b.free()
     red.free()
+    if shard_peers is not None:
+        barrier()  # every rank finished its last run before a mailbox goes away
+        shard_peers.close()
     B.release(c)
     paths_all = per * world
     return {"value": paths_all * args.steps / t_dev, "t_dev": t_dev, "ms_per_step": 1e3 * t_dev / args.steps,
@@ -832,9 +851,11 @@ def run_ours(args):
         if rc != 0:
             raise RuntimeError(R.lib().ccb_last_error().decode())
 
-    # The four scalar results of every step are summed across the ranks over
-    # NVLink peer memory (PeerSum: one 32-thread kernel per rank, mailboxes
-    # mapped through CUDA IPC); NCCL stays for the MLP step's gradients.
+    # Mailboxes are mapped between the ranks through CUDA IPC (`exchange`
+    # trades the handles): the headline's sharded program combines its four
+    # totals in its own last block (ShardPeers); the weak-scaling line sums
+    # its four results after the kernel (PeerSum, one 32-thread kernel per
+    # rank); NCCL stays for the MLP step's gradients.
     peer = None
     if world > 1:
         def exchange(h):
@@ -842,7 +863,7 @@ def run_ours(args):
             dist.all_gather_object(got, h)
             return got
         peer = M.PeerSum(world, rank, exchange)
-    head = measure_greeks(args, F64, rank, world, local, dist, peer, flush)
+    head = measure_greeks(args, F64, rank, world, local, dist, peer, flush, exchange=exchange if world > 1 else None)
     cf = X.analytic()
     ok = abs(head["outs"]["price"] - cf["price"]) < 0.02
     f32 = None
@@ -903,8 +924,9 @@ def run_ours(args):
             "data": "synthetic (Philox normals generated in registers, seed 42)",
             "config": {"workload": "bs_greeks_f64 (BASELINE configs[1]; F32 under secondary)", "paths_total": PATHS,
                        "paths_per_gpu": head["paths_per_rank"],
-                       "parallelism": (f"dp{world} (counter range split {world} ways as Multi does, the 4 scalar "
-                                       f"results summed across ranks over NVLink peer memory per step)") if world > 1 else "dp1",
+                       "parallelism": (f"dp{world} (sharded program: rank r walks paths [r*2^28/{world}, "
+                                       f"(r+1)*2^28/{world}), the 4 reductions combined across ranks in the kernel's "
+                                       f"last block over NVLink peer memory)") if world > 1 else "dp1",
                        "l2": "flushed before every timed step (read-only pass over 256 MiB, twice L2)",
                        "market": "S0=100 K=100 r=0.05 sigma=0.2 T=1"},
             "result": head["outs"], "result_ok_vs_closed_form": ok, "closed_form": cf,
@@ -914,7 +936,7 @@ def run_ours(args):
             "e2e": {"value": head["e2e"], "unit": "paths/s", "h2d_bytes_per_step": head["h2d"],
                     "d2h_bytes_per_step": head["d2h"],
                     "path": "ccb_program_enqueue + ccb_program_wait with page-locked host buffers"
-                            + (" + the cross-rank sum of the results" if world > 1 else "")},
+                            + (" (the cross-rank combine runs inside the kernel)" if world > 1 else "")},
         }
         if world == 1:
             line["cpu_baseline"] = cpu_baseline_sample()

@@ -33,8 +33,8 @@ def set_matmul_precision(p: str) -> None:
     matmul_precision = p
 
 
-def _wire(graph: Graph, matmul) -> bytes:
-    return to_wire(graph, matmul or matmul_precision).encode()
+def _wire(graph: Graph, matmul, shard=None) -> bytes:
+    return to_wire(graph, matmul or matmul_precision, shard).encode()
 
 _CODE_DT = {0: Dtype.F32, 1: Dtype.F64, 2: Dtype.I32, 3: Dtype.I64}
 
@@ -58,7 +58,7 @@ def _io_specs(h, count_fn, get_fn):
 class Compiled:
     """A program compiled for one device, with ``streams`` executors."""
 
-    def __init__(self, graph: Graph, device: int, streams: int, matmul=None):
+    def __init__(self, graph: Graph, device: int, streams: int, matmul=None, shard=None):
         if streams < 1:
             raise ValueError("Backend_cuda.compile_on: streams must be >= 1")
         self.graph = graph
@@ -66,7 +66,7 @@ class Compiled:
         self.streams = streams
         self.next = 0
         h = ctypes.c_void_p()
-        R.check(R.lib().ccb_program_create(_wire(graph, matmul), device, streams, ctypes.byref(h)))
+        R.check(R.lib().ccb_program_create(_wire(graph, matmul, shard), device, streams, ctypes.byref(h)))
         self.h = h.value
         self.params = _io_specs(self.h, "ccb_program_num_params", "ccb_program_param")
         self.outputs = _io_specs(self.h, "ccb_program_num_outputs", "ccb_program_output")
@@ -129,10 +129,10 @@ def _ptr_array(ptrs):
     return a
 
 
-def source(graph: Graph, matmul=None) -> str:
+def source(graph: Graph, matmul=None, shard=None) -> str:
     """The generated CUDA C++ for a graph, without compiling it."""
     h = ctypes.c_void_p()
-    R.check(R.lib().ccb_program_lower(_wire(graph, matmul), ctypes.byref(h)))
+    R.check(R.lib().ccb_program_lower(_wire(graph, matmul, shard), ctypes.byref(h)))
     try:
         s = ctypes.c_char_p()
         R.check(R.lib().ccb_program_source(h.value, ctypes.byref(s)))
@@ -141,11 +141,11 @@ def source(graph: Graph, matmul=None) -> str:
         R.lib().ccb_program_destroy(h.value)
 
 
-def lower_info(graph: Graph, matmul=None) -> dict:
+def lower_info(graph: Graph, matmul=None, shard=None) -> dict:
     """Kernel count, launches per run and the host plan, without a device."""
     L = R.lib()
     h = ctypes.c_void_p()
-    R.check(L.ccb_program_lower(_wire(graph, matmul), ctypes.byref(h)))
+    R.check(L.ccb_program_lower(_wire(graph, matmul, shard), ctypes.byref(h)))
     try:
         k = ctypes.c_int()
         n = ctypes.c_int()
@@ -160,8 +160,32 @@ def lower_info(graph: Graph, matmul=None) -> dict:
         L.ccb_program_destroy(h.value)
 
 
-def compile_on(device: int, graph: Graph, streams: int = 1, matmul=None) -> Compiled:
-    return Compiled(graph, device, streams, matmul)
+def compile_on(device: int, graph: Graph, streams: int = 1, matmul=None, shard=None) -> Compiled:
+    """``shard=(rank, world)``: rank ``rank`` of a sharded Monte-Carlo
+    program (bind_peers before the first run)."""
+    return Compiled(graph, device, streams, matmul, shard)
+
+
+def shard_of(c: Compiled) -> tuple[int, int]:
+    """(rank, world) of a sharded program; (0, 1) otherwise."""
+    r, w = ctypes.c_int(), ctypes.c_int()
+    R.check(R.lib().ccb_program_shard(c.h, ctypes.byref(r), ctypes.byref(w)))
+    return r.value, w.value
+
+
+def mailbox_bytes(c: Compiled) -> int:
+    """Bytes of one rank's mailbox for a sharded program (0 otherwise)."""
+    n = ctypes.c_size_t()
+    R.check(R.lib().ccb_program_mailbox_bytes(c.h, ctypes.byref(n)))
+    return n.value
+
+
+def bind_peers(c: Compiled, mailboxes) -> None:
+    """Bind every rank's mailbox (device pointers as this rank addresses
+    them, rank order) to a sharded program; each owner zero-fills its own
+    before any rank's first run."""
+    arr = (ctypes.c_void_p * max(len(mailboxes), 1))(*mailboxes)
+    R.check(R.lib().ccb_program_bind_peers(c.h, arr, len(mailboxes)))
 
 
 def compile_with(streams: int, graph: Graph, matmul=None) -> Compiled:

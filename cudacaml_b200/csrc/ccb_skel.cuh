@@ -81,12 +81,130 @@ __device__ __forceinline__ T warp_reduce(int r, T v) {
   return v;
 }
 
+// ---------------------------------------------------------------- sharded passes
+// A Monte-Carlo estimator pass compiled for rank XRANK of XWORLD GPUs of one
+// box walks only its slice [XLO, XHI) of the index space (Philox counters are
+// the global element index, so the slices together draw exactly the unsplit
+// program's numbers). Its last block then combines the block totals of all
+// ranks over NVLink peer memory before the scalar tails run, so every rank
+// ends with the unsplit program's outputs (up to the summation order) and no
+// collective follows the kernel.
+//
+// Mailboxes: rank q owns one in its own HBM, [2 halves][XWORLD ranks]
+// [XSLOT_WORDS u64] (flag = epoch, then the values as 64-bit patterns); P
+// carries every rank's as this rank addresses it (xmb[q]: an IPC mapping or a
+// peer-enabled allocation) and the run's epoch (xepoch, the same on every
+// rank, 1, 2, 3, ... per run). Warp 0 of the last block: lane q writes this
+// rank's totals into slot [e & 1][XRANK] of rank q's mailbox, fences at system
+// scope and release-stores e into the slot's flag; lane q then polls slot
+// [e & 1][q] of the local mailbox (acquire, system scope) until it reads e;
+// value r is folded over the ranks in rank order with the pass's own
+// combiner, so every rank computes the same bits. Halves alternate by epoch
+// parity: a rank writes epoch e + 2 only after every rank published e + 1,
+// i.e. after every rank finished reading epoch e. The wait is bounded: after
+// XRANK_SPIN polls it raises ERR_XRANK and the scalar tails are skipped (the
+// outputs keep their old contents); the kernel returns.
+constexpr unsigned ERR_XRANK = 32u;
+constexpr int XSLOT_WORDS = 33;  // flag + at most 32 reductions
+#ifndef CCB_XRANK_SPIN_LIMIT
+#define CCB_XRANK_SPIN_LIMIT (1u << 22)
+#endif
+
+template <class...>
+using void_t = void;
+template <class F, class = void>
+struct Shard {
+  static constexpr int WORLD = 1, RANK = 0;
+  static constexpr long long LO = 0, HI = -1;  // HI < 0: the whole index space [0, n)
+};
+template <class F>
+struct Shard<F, void_t<decltype(F::XWORLD)>> {
+  static constexpr int WORLD = F::XWORLD, RANK = F::XRANK;
+  static constexpr long long LO = F::XLO, HI = F::XHI;
+};
+
+__device__ __forceinline__ void st_release_sys_u64(u64* p, u64 v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ u64 ld_acquire_sys_u64(const u64* p) {
+  u64 v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+template <class T>
+__device__ __forceinline__ u64 to_bits64(T v) {
+  union {
+    T t;
+    u64 u;
+  } x;
+  x.u = 0;
+  x.t = v;
+  return x.u;
+}
+template <class T>
+__device__ __forceinline__ T from_bits64(u64 u) {
+  union {
+    T t;
+    u64 u;
+  } x;
+  x.u = u;
+  return x.t;
+}
+
+// Warp 0 of the last block of a sharded pass; tot[r] holds this rank's total
+// of reduction r on entry and the all-rank total on a true return.
+template <class F, class T>
+__device__ __forceinline__ bool xrank_combine(const typename F::P& p, T (*tot)[33]) {
+  constexpr int R = F::NRED, W = Shard<F>::WORLD, ME = Shard<F>::RANK;
+  static_assert(R <= XSLOT_WORDS - 1, "a sharded pass exchanges at most 32 reductions");
+  static_assert(W <= 32, "at most 32 ranks");
+  const int lane = threadIdx.x & 31;
+  const u64 e = p.xepoch;
+  const u64 half = (e & 1ull) * (u64)W * XSLOT_WORDS;
+  if (lane < W) {
+    u64* slot = p.xmb[lane] + half + (u64)ME * XSLOT_WORDS;
+#pragma unroll
+    for (int r = 0; r < R; ++r) slot[1 + r] = to_bits64(tot[r][32]);
+    __threadfence_system();
+    st_release_sys_u64(slot, e);
+  }
+  bool ok = true;
+  if (lane < W) {
+    const u64* flag = p.xmb[ME] + half + (u64)lane * XSLOT_WORDS;
+    unsigned it = 0;
+    while (ld_acquire_sys_u64(flag) != e) {
+      if (++it > CCB_XRANK_SPIN_LIMIT) {
+        ok = false;
+        break;
+      }
+      __nanosleep(32);
+    }
+  }
+  if (!__all_sync(FULL, ok)) {
+    if (lane == 0) raise_error(p.err, ERR_XRANK);
+    return false;
+  }
+  // every flag reads e; each lane acquires the slots it reads itself
+  for (int r = lane; r < R; r += 32) {
+    const u64* box = p.xmb[ME] + half;
+    (void)ld_acquire_sys_u64(box);
+    T v = from_bits64<T>(*(volatile const u64*)(box + 1 + r));
+    for (int q = 1; q < W; ++q) {
+      (void)ld_acquire_sys_u64(box + (u64)q * XSLOT_WORDS);
+      v = F::combine(r, v, from_bits64<T>(*(volatile const u64*)(box + (u64)q * XSLOT_WORDS + 1 + r)));
+    }
+    tot[r][32] = v;
+  }
+  return true;
+}
+
 // ---------------------------------------------------------------- map / map-reduce
 // F provides:
 //   struct P { ...; long long n; acc_t* partials; unsigned* ticket; unsigned* err; }
 //   typedef acc_t; static constexpr int NRED, VEC, UNROLL; static constexpr bool TAIL;
 //   init(acc_t*), identity(r), combine(r,a,b), elem(p,i,acc), elem4(p,i,acc),
 //   vec_ok(p), epilogue(p, const acc_t* res)
+// and, for a sharded pass, XWORLD, XRANK, XLO, XHI and P::xmb[XWORLD], P::xepoch.
 template <class F>
 __device__ __forceinline__ void reduce_finish(const typename F::P& p, typename F::acc_t* acc) {
   typedef typename F::acc_t T;
@@ -158,11 +276,23 @@ __device__ __forceinline__ void reduce_finish(const typename F::P& p, typename F
     }
   }
   __syncthreads();
+  bool combined = true;
+  if constexpr (Shard<F>::WORLD > 1) {
+    __shared__ int xok;
+    if (warp == 0) {
+      const bool ok = xrank_combine<F>(p, sh);
+      if (lane == 0) xok = ok;
+    }
+    __syncthreads();
+    combined = xok != 0;
+  }
   if (threadIdx.x == 0) {
-    T res[R];
+    if (combined) {
+      T res[R];
 #pragma unroll
-    for (int r = 0; r < R; ++r) res[r] = sh[r][32];
-    F::epilogue(p, res);
+      for (int r = 0; r < R; ++r) res[r] = sh[r][32];
+      F::epilogue(p, res);
+    }
     *p.ticket = 0u;  // ready for the next launch
     __threadfence();
   }
@@ -178,8 +308,10 @@ __device__ __forceinline__ void map_reduce(const typename F::P& p) {
   // grid-stride step adds far less than 2^31, so `i + step` never wraps
   // before the bound check. A signed index would overflow past INT_MAX for n
   // near 2^31 and pass `i < n` with a negative value.
-  const unsigned n = (unsigned)p.n;
-  const unsigned tid = blockIdx.x * blockDim.x + threadIdx.x;
+  // A sharded pass walks its slice [LO, HI) of the global index space.
+  static_assert(Shard<F>::WORLD == 1 || (F::VEC == 0 && R > 0), "only estimator passes are sharded");
+  const unsigned n = Shard<F>::HI < 0 ? (unsigned)p.n : (unsigned)Shard<F>::HI;
+  const unsigned tid = (unsigned)Shard<F>::LO + blockIdx.x * blockDim.x + threadIdx.x;
   const unsigned nth = gridDim.x * blockDim.x;
   if (F::VEC && F::vec_ok(p)) {
     constexpr unsigned U = F::UNROLL;

@@ -136,8 +136,18 @@ int parse_graph(const char* text, GGraph& g) {
         ls >> g.name;
         g.name = wire_name(g.name);
       } else if (tag == "opt") {
-        std::string key, val;
-        ls >> key >> val;
+        std::string key;
+        ls >> key;
+        if (key == "shard") {
+          long long r = -1, w = 0;
+          if (!(ls >> r >> w) || w < 1 || w > 32 || r < 0 || r >= w)
+            bad("wire: opt shard <rank> <world> needs 0 <= rank < world <= 32");
+          g.shard_rank = (int)r;
+          g.shard_world = (int)w;
+          continue;
+        }
+        std::string val;
+        ls >> val;
         if (key != "matmul") bad("wire: unknown option " + key);
         if (val == "f32") g.matmul = MM_F32;
         else if (val == "tf32") g.matmul = MM_TF32;
@@ -1837,6 +1847,7 @@ class Lowerer {
 
   // ------------------------------------------------------------ code generation
   Lowered* out = nullptr;
+  int sharded_passes = 0;  // reduction passes of a sharded program (at most one)
   std::ostringstream src;
   std::vector<int> node_buf;  // tensor -> buffer index
 
@@ -1867,7 +1878,8 @@ class Lowerer {
 
   void emit_struct(const std::vector<Field>& f) {
     src << "  struct P {\n";
-    for (auto& x : f) src << "    " << x.decl << ";\n";
+    for (auto& x : f)
+      if (!x.decl.empty()) src << "    " << x.decl << ";\n";  // an empty decl: a further word of the previous array
     src << "  };\n";
   }
 
@@ -2009,21 +2021,6 @@ class Lowerer {
       partials = add_buf("g" + std::to_string(gi) + "_partials", dt_size(acc), (int64_t)max_grid * R, BR_SCRATCH, -1, false);
       ticket = add_buf("g" + std::to_string(gi) + "_ticket", 4, 1, BR_SCRATCH, -1, true);
     }
-    std::vector<Field> fields;
-    for (int b : loads_of(gr.ctx)) fields.push_back(in_field(b));
-    for (auto& s : gr.stores) fields.push_back(out_field(s.first));
-    for (int t : red_t) fields.push_back(out_field(t));
-    for (auto& s : gr.tails) fields.push_back(out_field(s.first));
-    fields.push_back(buf_field(std::string(at) + "* partials", partials));
-    fields.push_back(buf_field("unsigned* ticket", ticket));
-    fields.push_back(buf_field("unsigned* err", out->err_buf));
-    fields.push_back(i64_field("n", gr.domain));
-
-    src << "// pass " << gi << ": " << gr.stores.size() << " element stores, " << R << " reductions, " << gr.tails.size()
-        << " scalar tails over " << gr.domain << " elements\n";
-    src << "struct " << F << " {\n";
-    emit_struct(fields);
-    src << "  typedef " << at << " acc_t;\n";
     std::vector<int> roots;
     for (auto& s : gr.stores) roots.push_back(s.second);
     for (auto& r : gr.reds) roots.push_back(r.var);
@@ -2035,6 +2032,60 @@ class Lowerer {
     // loops) overflow the instruction cache: it runs one element at a time
     // (F64 Greeks 2^28 paths: 2.68 -> 2.60 ms).
     const bool scalar_only = direct.empty() && offs.empty() && gr.stores.empty();
+    // Sharded program (wire "opt shard"): its one reduction pass walks this
+    // rank's slice of the index space and combines the block totals of every
+    // rank in its last block (ccb::xrank_combine); passes without reductions
+    // only evaluate scalar tails, identically on every rank.
+    const int W = g.shard_world;
+    const bool sharded = W > 1 && R > 0;
+    int64_t xlo = 0, xhi = gr.domain;
+    if (W > 1) {
+      if (!gr.stores.empty())
+        unsupported("shard: pass " + std::to_string(gi) + " stores elements; a sharded program's passes produce scalars only");
+      if (sharded) {
+        if (!scalar_only)
+          unsupported("shard: pass " + std::to_string(gi) +
+                      " loads elements by index; only Monte-Carlo estimator passes (reductions of values computed from the "
+                      "index, scalar inputs and Rng draws) are sharded");
+        if (R > 32) unsupported("shard: a sharded pass exchanges at most 32 reductions, this one has " + std::to_string(R));
+        if (++sharded_passes > 1) unsupported("shard: a sharded program has one reduction pass, this one has more");
+        xlo = gr.domain * g.shard_rank / W;
+        xhi = gr.domain * (g.shard_rank + 1) / W;
+      }
+    }
+    std::vector<Field> fields;
+    for (int b : loads_of(gr.ctx)) fields.push_back(in_field(b));
+    for (auto& s : gr.stores) fields.push_back(out_field(s.first));
+    for (int t : red_t) fields.push_back(out_field(t));
+    for (auto& s : gr.tails) fields.push_back(out_field(s.first));
+    fields.push_back(buf_field(std::string(at) + "* partials", partials));
+    fields.push_back(buf_field("unsigned* ticket", ticket));
+    fields.push_back(buf_field("unsigned* err", out->err_buf));
+    fields.push_back(i64_field("n", gr.domain));
+    if (sharded) {
+      for (int q = 0; q < W; ++q) {
+        Field f;
+        if (q == 0) f.decl = "unsigned long long* xmb[" + std::to_string(W) + "]";
+        f.slot.kind = SL_XMB;
+        f.slot.val = q;
+        fields.push_back(f);
+      }
+      Field f;
+      f.decl = "unsigned long long xepoch";
+      f.slot.kind = SL_XEPOCH;
+      fields.push_back(f);
+    }
+
+    src << "// pass " << gi << ": " << gr.stores.size() << " element stores, " << R << " reductions, " << gr.tails.size()
+        << " scalar tails over " << gr.domain << " elements";
+    if (sharded) src << ", rank " << g.shard_rank << " of " << W << ": elements [" << xlo << ", " << xhi << ")";
+    src << "\n";
+    src << "struct " << F << " {\n";
+    emit_struct(fields);
+    src << "  typedef " << at << " acc_t;\n";
+    if (sharded)
+      src << "  static constexpr int XWORLD = " << W << ", XRANK = " << g.shard_rank << ";\n  static constexpr long long XLO = "
+          << xlo << "LL, XHI = " << xhi << "LL;\n";
     src << "  static constexpr int NRED = " << R << ";\n  static constexpr int VEC = " << (scalar_only ? 0 : 1) << ";\n";
     // F64 estimators take two elements per iteration (F64 Greeks 2.59 ->
     // 2.53 ms; no gain in F32)
@@ -2164,7 +2215,7 @@ class Lowerer {
         << "::P p) { ccb::map_reduce<" << F << ">(p); }\n\n";
     LaunchSpec& l = add_launch(fn, fields);
     l.mode = GM_PERSISTENT;
-    l.work = gr.domain;
+    l.work = xhi - xlo;
     l.per_block = 256 * 8;
     l.max_grid = R ? max_grid : (1 << 20);
     if (R == 0 && gr.stores.empty()) {
@@ -2857,6 +2908,8 @@ class Lowerer {
   void generate(Lowered& o) {
     out = &o;
     o.name = g.name;
+    o.shard_rank = g.shard_rank;
+    o.shard_world = g.shard_world;
     node_buf.assign(g.ts.size(), -1);
     o.err_buf = add_buf("err", 4, 1, BR_SCRATCH, -1, true);
     // params first, in graph order (lib/lower/lower.ml:977-987)
@@ -2878,6 +2931,9 @@ class Lowerer {
     }
     src << "// generated by cudacaml-b200 for sm_100a: " << g.name << "\n#include \"ccb_skel.cuh\"\n\n";
     for (int gi = 0; gi < (int)groups.size(); ++gi) {
+      if (g.shard_world > 1 && groups[gi].kind != G_MAPRED)
+        unsupported("shard: a sharded program is one Monte-Carlo estimator pass (and scalar tails); pass " + std::to_string(gi) +
+                    " is a scan, row reduction, scatter, product or transpose");
       switch (groups[gi].kind) {
         case G_MAPRED:
           if (groups[gi].fused_into < 0) emit_mapred(gi);
@@ -2893,6 +2949,7 @@ class Lowerer {
           break;
       }
     }
+    if (g.shard_world > 1 && sharded_passes == 0) unsupported("shard: the program has no reduction pass to shard");
     for (auto& op : g.outputs) {
       const GTensor& x = g.ts[op.second];
       IOSpec io;

@@ -47,6 +47,9 @@ enum MatmulMode { MM_F32 = 0, MM_TF32 = 1 };
 struct GGraph {
   std::string name;
   int matmul = MM_F32;  // wire "opt matmul": precision of F32 products
+  // wire "opt shard <rank> <world>": this rank's slice of the program's one
+  // Monte-Carlo estimator pass, combined across the world in its last block
+  int shard_rank = 0, shard_world = 1;
   std::vector<GExpr> ex;
   std::vector<GTensor> ts;
   std::vector<std::pair<std::string, int>> outputs;
@@ -70,7 +73,10 @@ struct BufSpec {
 // parameter block) over buffer `buf`, 2-D fp32, swizzle `tswizzle`: inner
 // extent tdim[0], outer tdim[1], outer stride tstride bytes, box tbox[0] x
 // tbox[1]. The executor encodes it against the buffer the run binds.
-enum SlotKind { SL_BUF = 0, SL_I64 = 1, SL_EPOCH = 2, SL_TMAP = 3 };
+// SL_XMB: the mailbox of rank `val` of a sharded program (as bound by
+// ccb_program_bind_peers); SL_XEPOCH: the program's cross-rank epoch of this
+// run (1, 2, 3, ... per run, the same on every rank).
+enum SlotKind { SL_BUF = 0, SL_I64 = 1, SL_EPOCH = 2, SL_TMAP = 3, SL_XMB = 4, SL_XEPOCH = 5 };
 struct Slot {
   int kind = SL_BUF;
   int buf = -1;
@@ -120,6 +126,7 @@ struct Lowered {
   std::vector<IOSpec> params, outputs;
   int err_buf = -1;
   int num_kernels = 0;
+  int shard_rank = 0, shard_world = 1;  // see GGraph
   std::string plan_text;
 };
 

@@ -38,7 +38,16 @@ struct Program {
   std::vector<unsigned> gx, gy;
   std::vector<Lane> lanes;
   int num_launch_ops = 0;
+  // Sharded programs: every rank's mailbox as this rank addresses it, and the
+  // cross-rank epoch of the last run (ccb_program_bind_peers resets it).
+  std::vector<CUdeviceptr> peers;
+  uint64_t xepoch = 0;
 };
+
+// Words of one mailbox slot of a sharded program (flag + 32 values) and the
+// whole mailbox of a world: ccb::XSLOT_WORDS in the skeleton header.
+constexpr int kXslotWords = 33;
+size_t mailbox_bytes(int world) { return (size_t)2 * world * kXslotWords * sizeof(uint64_t); }
 
 // The device error word of a lane accumulates over runs until a check
 // reports it; then it is cleared, so a chain of runs checked once reports any
@@ -69,6 +78,7 @@ int lane_check(Program& P, int lane, CUstream stream, bool fresh) {
   if (e & 4u) m += " scan look-back wait gave up (bounded spin exhausted);";
   if (e & 8u) m += " bulk-copy (TMA) wait gave up (bounded spin exhausted);";
   if (e & 16u) m += " tensor-core pipeline wait gave up (bounded spin exhausted);";
+  if (e & 32u) m += " cross-rank combine gave up: a peer rank did not publish its totals (bounded wait);";
   *P.lanes[lane].host_err = 0;
   return fail(CCB_ERR_DEVICE_CHECK, m);
 }
@@ -164,9 +174,18 @@ int issue(Program& P, int lane, const void* const* h_in, void* const* h_out, con
   const bool capturing = cs != CU_STREAM_CAPTURE_STATUS_NONE;
   if (capturing)
     for (const LaunchSpec& l : P.L.launches)
-      for (const Slot& sl : l.slots)
+      for (const Slot& sl : l.slots) {
         if (sl.kind == SL_EPOCH)
           return fail(CCB_ERR_INVALID, "graph capture: " + l.fn + " (a flat scan) cannot be replayed from a graph");
+        if (sl.kind == SL_XEPOCH)
+          return fail(CCB_ERR_INVALID, "graph capture: " + l.fn + " (a sharded pass) cannot be replayed from a graph");
+      }
+  if (P.L.shard_world > 1) {
+    if ((int)P.peers.size() != P.L.shard_world)
+      return fail(CCB_ERR_INVALID, "sharded program (rank " + std::to_string(P.L.shard_rank) + " of " +
+                                       std::to_string(P.L.shard_world) + "): ccb_program_bind_peers has not been called");
+    ++P.xepoch;
+  }
   ln.epoch = ln.epoch % ((1u << 30) - 2) + 1;
   // output j's event goes right after the last op that references its
   // buffer (no later op touches it); outputs copied out after the launches
@@ -216,7 +235,13 @@ int issue(Program& P, int lane, const void* const* h_in, void* const* h_out, con
         blk.insert(blk.end(), w, w + 16);
         continue;
       }
-      blk.push_back(sl.kind == SL_BUF ? (uint64_t)ptr[sl.buf] : sl.kind == SL_I64 ? (uint64_t)sl.val : ln.epoch);
+      switch (sl.kind) {
+        case SL_BUF: blk.push_back((uint64_t)ptr[sl.buf]); break;
+        case SL_I64: blk.push_back((uint64_t)sl.val); break;
+        case SL_XMB: blk.push_back((uint64_t)P.peers[sl.val]); break;
+        case SL_XEPOCH: blk.push_back(P.xepoch); break;
+        default: blk.push_back(ln.epoch); break;
+      }
     }
     blk.resize((blk.size() + 7) & ~(size_t)7, 0);  // a block with tensor maps is padded to 64 bytes
     void* args[] = {blk.data()};
@@ -509,6 +534,40 @@ int ccb_program_check(ccb_program_t prog, int lane, ccb_stream_t stream) {
   const CUstream s = stream ? (CUstream)stream : P->lanes[lane].stream;
   CCB_CU(driver().cuStreamSynchronize(s));
   return lane_check(*P, lane, s, true);
+}
+
+int ccb_program_shard(ccb_program_t prog, int* rank, int* world) {
+  Program* P = as_prog(prog);
+  if (!P || !rank || !world) return fail(CCB_ERR_INVALID, "ccb_program_shard: null argument");
+  *rank = P->L.shard_rank;
+  *world = P->L.shard_world;
+  return CCB_OK;
+}
+
+int ccb_program_mailbox_bytes(ccb_program_t prog, size_t* bytes) {
+  Program* P = as_prog(prog);
+  if (!P || !bytes) return fail(CCB_ERR_INVALID, "ccb_program_mailbox_bytes: null argument");
+  *bytes = P->L.shard_world > 1 ? mailbox_bytes(P->L.shard_world) : 0;
+  return CCB_OK;
+}
+
+int ccb_program_bind_peers(ccb_program_t prog, void* const* mailboxes, int nranks) {
+  Program* P = as_prog(prog);
+  if (!P || !mailboxes) return fail(CCB_ERR_INVALID, "ccb_program_bind_peers: null argument");
+  if (P->L.shard_world < 2) return fail(CCB_ERR_INVALID, "ccb_program_bind_peers: the program is not sharded");
+  if (nranks != P->L.shard_world)
+    return fail(CCB_ERR_INVALID, "ccb_program_bind_peers: " + std::to_string(nranks) + " mailboxes for a world of " +
+                                     std::to_string(P->L.shard_world));
+  std::vector<CUdeviceptr> v(nranks);
+  for (int q = 0; q < nranks; ++q) {
+    if (!mailboxes[q]) return fail(CCB_ERR_INVALID, "ccb_program_bind_peers: mailbox of rank " + std::to_string(q) + " is null");
+    if ((uintptr_t)mailboxes[q] & 7)
+      return fail(CCB_ERR_INVALID, "ccb_program_bind_peers: mailbox of rank " + std::to_string(q) + " is not 8-byte aligned");
+    v[q] = (CUdeviceptr)mailboxes[q];
+  }
+  P->peers = v;
+  P->xepoch = 0;
+  return CCB_OK;
 }
 
 int ccb_program_lane_stream(ccb_program_t prog, int lane, ccb_stream_t* stream) {

@@ -19,6 +19,11 @@ Additions, all opt-in:
 * ``allreduce_mean(names, inputs)`` recombines scalar outputs on the devices
   with a cross-device sum over NVLink peer memory (``PeerSum``) instead of a
   host loop.
+* ``sharded=True`` compiles the unsplit graph on every device as one rank of
+  a sharded program: each device walks its slice of the paths and the
+  kernel's last block combines all devices' totals over NVLink, so the
+  recombination is part of the kernel (``ShardPeers`` does the same for one
+  process per GPU).
 * ``allreduce_sum(names, inputs)`` sums whole outputs across the devices on
   the devices (one NCCL all-reduce per output, grouped): a loss and the weight
   gradients of a batch split by rows, as in the MLP training step.
@@ -128,6 +133,77 @@ def mean_scalar(values) -> float:
     return sum(float(v.data[0]) for v in values) / len(values)
 
 
+def _ipc_mailbox(nbytes, nranks, rank, exchange):
+    """Allocate and zero-fill this rank's mailbox, then trade IPC handles with
+    ``exchange`` (a collective returning every rank's 64-byte handle in rank
+    order, so no rank can write into a mailbox its owner has not zeroed yet)
+    and map every peer's. Returns (own buffer, pointers in rank order, the
+    mapped peer pointers to close)."""
+    L = R.lib()
+    own = R.Buffer(nbytes)
+    R.check(L.ccb_memset_d8(own.ptr, 0, nbytes, None))
+    R.check(L.ccb_stream_synchronize(None))
+    h = (ctypes.c_ubyte * 64)()
+    R.check(L.ccb_ipc_mem_handle(own.ptr, h))
+    handles = exchange(bytes(h))
+    ptrs, opened = [], []
+    for q, hq in enumerate(handles):
+        if q == rank:
+            ptrs.append(own.ptr)
+            continue
+        p = ctypes.c_void_p()
+        R.check(L.ccb_ipc_mem_open((ctypes.c_ubyte * 64).from_buffer_copy(hq), ctypes.byref(p)))
+        opened.append(p.value)
+        ptrs.append(p.value)
+    return own, ptrs, opened
+
+
+def _peer_mailboxes(devices, nbytes):
+    """One zero-filled mailbox on each of ``devices`` (distinct ordinals, one
+    process), with peer access enabled between all of them."""
+    if len(set(devices)) != len(devices):
+        raise ValueError("every rank needs its own GPU")
+    L = R.lib()
+    own = []
+    for d in devices:
+        with R.with_device(d):
+            for q in devices:
+                if q != d:
+                    R.check(L.ccb_peer_access_enable(q))
+            b = R.Buffer(nbytes)
+            R.check(L.ccb_memset_d8(b.ptr, 0, nbytes, None))
+            R.check(L.ccb_stream_synchronize(None))
+            own.append(b)
+    return own
+
+
+class ShardPeers:
+    """The mailboxes of a sharded program (compiled with ``shard=(rank,
+    world)``) in a process-per-GPU job: this rank's mailbox is allocated and
+    zero-filled here, mapped by every peer through CUDA IPC (``exchange`` as
+    for PeerSum), and all of them are bound to the program. Every rank then
+    runs the program the same number of times in the same order; each run's
+    last block combines the ranks' totals over NVLink, so no collective
+    follows the kernel."""
+
+    def __init__(self, c, exchange):
+        rank, world = B.shard_of(c)
+        if world < 2:
+            raise ValueError("ShardPeers: the program is not sharded")
+        self.own, ptrs, self._opened = _ipc_mailbox(B.mailbox_bytes(c), world, rank, exchange)
+        B.bind_peers(c, ptrs)
+
+    def close(self):
+        """Unmap the peers' mailboxes and free this rank's; every rank must
+        have finished its last run (synchronised) first."""
+        for p in self._opened:
+            R.lib().ccb_ipc_mem_close(p)
+        self._opened = []
+        if self.own is not None:
+            self.own.free()
+            self.own = None
+
+
 class PeerSum:
     """Cross-rank sum of a few scalars over NVLink peer memory
     (ccb_xrank_sum), for ranks on distinct GPUs of one box: one 32-thread
@@ -156,23 +232,9 @@ class PeerSum:
         R.check(L.ccb_xrank_mailbox_bytes(nranks, ctypes.byref(size)))
         self._opened = []
         if _devices is None:
-            self.own = R.Buffer(size.value)
-            R.check(L.ccb_memset_d8(self.own.ptr, 0, size.value, None))
             self.err = R.Buffer(4)
             R.check(L.ccb_memset_d8(self.err.ptr, 0, 4, None))
-            R.check(L.ccb_stream_synchronize(None))
-            h = (ctypes.c_ubyte * 64)()
-            R.check(L.ccb_ipc_mem_handle(self.own.ptr, h))
-            handles = exchange(bytes(h))
-            ptrs = []
-            for q, hq in enumerate(handles):
-                if q == rank:
-                    ptrs.append(self.own.ptr)
-                    continue
-                p = ctypes.c_void_p()
-                R.check(L.ccb_ipc_mem_open((ctypes.c_ubyte * 64).from_buffer_copy(hq), ctypes.byref(p)))
-                self._opened.append(p.value)
-                ptrs.append(p.value)
+            self.own, ptrs, self._opened = _ipc_mailbox(size.value, nranks, rank, exchange)
             self.mailboxes = (ctypes.c_void_p * nranks)(*ptrs)
             self.devices = None
 
@@ -187,17 +249,13 @@ class PeerSum:
         n = len(devices)
         size = ctypes.c_size_t()
         R.check(L.ccb_xrank_mailbox_bytes(n, ctypes.byref(size)))
-        own, errs = [], []
+        own = _peer_mailboxes(devices, size.value)
+        errs = []
         for d in devices:
             with R.with_device(d):
-                for q in devices:
-                    if q != d:
-                        R.check(L.ccb_peer_access_enable(q))
-                b, e = R.Buffer(size.value), R.Buffer(4)
-                R.check(L.ccb_memset_d8(b.ptr, 0, size.value, None))
+                e = R.Buffer(4)
                 R.check(L.ccb_memset_d8(e.ptr, 0, 4, None))
                 R.check(L.ccb_stream_synchronize(None))
-                own.append(b)
                 errs.append(e)
         out = []
         for r, d in enumerate(devices):
@@ -235,13 +293,26 @@ class PeerSum:
 
 
 class Multi:
-    def __init__(self, devices, n: int, build, counter_key: str | None = None, split=None, matmul=None):
+    """``sharded=True`` (Monte-Carlo estimators): every device compiles the
+    unsplit graph ``build(n)`` as one rank of a sharded program
+    (include/ccb.h, sharded programs): device i walks paths
+    [i*n/D, (i+1)*n/D) and the kernel's last block combines the devices'
+    totals over NVLink peer memory, so each device's outputs are already the
+    whole run's (the same bits on every device) and no recombination step
+    follows. Needs distinct devices; inputs are not sliced."""
+
+    def __init__(self, devices, n: int, build, counter_key: str | None = None, split=None, matmul=None,
+                 sharded: bool = False):
         devices = list(devices)
         d = len(devices)
         if d == 0:
             raise ValueError("Multi.create: devices must not be empty")
         if n % d != 0:
             raise ValueError(f"Multi.create: n = {n} is not divisible by {d} devices")
+        if sharded and (counter_key is not None or split is not None):
+            raise ValueError("Multi.create: a sharded Multi splits the index space itself (no counter_key, no split)")
+        if sharded and len(set(devices)) != d:
+            raise ValueError("Multi.create: a sharded Multi needs distinct devices (its ranks wait on each other)")
         if counter_key is not None:
             path_range(n, d, 0)  # the split counter range must fit the I32 counters
         self.devices = devices
@@ -249,13 +320,22 @@ class Multi:
         self.per = n // d
         self.counter_key = counter_key
         self.split = None if split is None else set(split)
+        self.sharded = sharded and d > 1
         self.released = False
         self.slots = []
-        for ordinal in devices:
+        self._mailboxes = []
+        for i, ordinal in enumerate(devices):
+            if self.sharded:
+                self.slots.append(B.compile_on(ordinal, build(n), matmul=matmul, shard=(i, d)))
+                continue
             g = build(self.per)
             if counter_key is not None:
                 g = offset_counters(g, counter_key, rows=self.per)
             self.slots.append(B.compile_on(ordinal, g, matmul=matmul))
+        if self.sharded:
+            self._mailboxes = _peer_mailboxes(devices, B.mailbox_bytes(self.slots[0]))
+            for c in self.slots:
+                B.bind_peers(c, [b.ptr for b in self._mailboxes])
         self._comms = None
 
     def _splits(self, name, v) -> bool:
@@ -266,6 +346,8 @@ class Multi:
         return bool(len(v.shape)) and v.shape[0] == self.n
 
     def _inputs_for(self, i: int, inputs):
+        if self.sharded:
+            return list(inputs)
         out = []
         for name, v in inputs:
             if self._splits(name, v):
@@ -307,9 +389,22 @@ class Multi:
             if numel(outs[js[0]][2]) != 1:
                 raise ValueError(f"Multi.allreduce_mean: output {name} is not a scalar")
         d = len(self.devices)
+        inputs = list(inputs)
+        if self.sharded:  # every device's outputs are already the whole run's
+            keep = self._run_all_resident(inputs)
+            for c in self.slots:
+                B.check_device(c, c.lane_stream(0))
+            result = {}
+            for name in names:
+                j = [k for k, (n, _, _) in enumerate(outs) if n == name][0]
+                host = np.empty(1, dtype=outs[j][1].np)
+                with R.with_device(self.slots[0].device):
+                    keep[0][1][j].download(host)
+                result[name] = float(host[0])
+            self._free_resident(keep)
+            return result
         if getattr(self, "_peer", None) is None:
             self._peer = PeerSum.in_process(self.devices)
-        inputs = list(inputs)
         keep = self._run_all_resident(inputs)
         for name in names:
             j = [k for k, (n, _, _) in enumerate(outs) if n == name][0]
@@ -405,6 +500,10 @@ class Multi:
             self.released = True
             for c in self.slots:
                 B.release(c)
+            for i, b in enumerate(self._mailboxes):
+                with R.with_device(self.devices[i]):
+                    b.free()
+            self._mailboxes = []
             for ps in getattr(self, "_peer", None) or []:
                 with R.with_device(self.devices[ps.rank]):
                     ps.close()

@@ -105,6 +105,9 @@ def _declare(L):
         "ccb_program_check": (I, [P, I, P]),
         "ccb_program_run_device_events": (I, [P, I, c.POINTER(P), c.POINTER(P), P, c.POINTER(P)]),
         "ccb_program_lane_stream": (I, [P, I, c.POINTER(P)]),
+        "ccb_program_shard": (I, [P, c.POINTER(I), c.POINTER(I)]),
+        "ccb_program_mailbox_bytes": (I, [P, c.POINTER(SZ)]),
+        "ccb_program_bind_peers": (I, [P, c.POINTER(P), I]),
         "ccb_comm_init_all": (I, [I, c.POINTER(I), c.POINTER(P)]),
         "ccb_comm_unique_id": (I, [c.POINTER(c.c_ubyte)]),
         "ccb_comm_init_rank": (I, [I, c.POINTER(c.c_ubyte), I, c.POINTER(P)]),

@@ -9,6 +9,7 @@ every expression node is written once, before its users, under its own id.
     ccbgraph 1
     name <graph name>
     opt matmul <f32|tf32>                optional; F32 product precision (default f32)
+    opt shard <rank> <world>             optional; rank's slice of a sharded Monte-Carlo program
     e <eid> <dtype> const <value>        f32/f64 value = IEEE-754 double bits (hex)
     e <eid> <dtype> arg <i>
     e <eid> i32 index
@@ -48,15 +49,23 @@ def _const_text(e: Expr) -> str:
 MATMUL_PRECISIONS = ("f32", "tf32")
 
 
-def to_wire(g: Graph, matmul: str = "f32") -> str:
+def to_wire(g: Graph, matmul: str = "f32", shard=None) -> str:
     """``matmul`` selects how F32 products are computed: "f32" keeps F32
     arithmetic (the reference's), "tf32" runs them on the tensor cores with
-    TF32 operands and F32 accumulation (error bound in ccb_skel.cuh)."""
+    TF32 operands and F32 accumulation (error bound in ccb_skel.cuh).
+    ``shard=(rank, world)`` lowers the graph as rank ``rank`` of a sharded
+    Monte-Carlo program (include/ccb.h, sharded programs)."""
     if matmul not in MATMUL_PRECISIONS:
         raise ValueError(f"matmul precision must be one of {MATMUL_PRECISIONS}, got {matmul!r}")
     lines = ["ccbgraph 1", f"name {_check_name(g.name)}"]
     if matmul != "f32":
         lines.append(f"opt matmul {matmul}")
+    if shard is not None:
+        rank, world = (int(x) for x in shard)
+        if not (1 <= world <= 32 and 0 <= rank < world):
+            raise ValueError(f"shard must be (rank, world) with 0 <= rank < world <= 32, got {shard!r}")
+        if world > 1:
+            lines.append(f"opt shard {rank} {world}")
     written = set()
 
     def emit_expr(root: Expr):

@@ -168,6 +168,36 @@ int ccb_program_check(ccb_program_t prog, int lane, ccb_stream_t stream);
 /* Kernel launches per run (for the bench's gpu_launches count). */
 int ccb_program_lane_stream(ccb_program_t prog, int lane, ccb_stream_t* stream);
 
+/* ---------------------------------------------------------------- sharded programs
+ * Replaces the recombination half of Multi (lib/backend_cuda/multi.ml:95-109,
+ * mean_scalar of per-device results on the host) for Monte-Carlo estimators.
+ * A graph lowered with the wire option `opt shard <rank> <world>` (one process
+ * or one device per rank, each rank on its own GPU of one box) is the unsplit
+ * graph: its one reduction pass walks only this rank's slice
+ * [n*rank/world, n*(rank+1)/world) of the index space -- Philox counters are
+ * the global element index, so the slices draw exactly the unsplit program's
+ * numbers -- and its last block sums the block totals of every rank in rank
+ * order over NVLink peer memory before the scalar tails run. Every rank's
+ * outputs are then the unsplit program's (up to summation order), the same
+ * bits on every rank, with no collective after the kernel. Programs with
+ * element loads or stores, scans, products or more than one reduction pass
+ * are refused (CCB_ERR_UNSUPPORTED).
+ *
+ * ccb_program_mailbox_bytes: bytes of one rank's mailbox (0 if not sharded).
+ * ccb_program_bind_peers: mailboxes[q] is rank q's mailbox as this rank
+ * addresses it (its own allocation, an IPC mapping from ccb_ipc_mem_open, or
+ * a peer allocation after ccb_peer_access_enable), 8-byte aligned; every
+ * owner zero-fills its mailbox before any rank's first run after binding,
+ * and every rank runs the program the same number of times in the same
+ * order, one run at a time. A run before binding is CCB_ERR_INVALID; a run
+ * under stream capture is refused. A peer that never runs makes the bounded
+ * wait give up: ccb_program_check / wait report CCB_ERR_DEVICE_CHECK and the
+ * scalar outputs keep their previous contents. No counterpart in the
+ * reference. */
+int ccb_program_shard(ccb_program_t prog, int* rank, int* world);
+int ccb_program_mailbox_bytes(ccb_program_t prog, size_t* bytes);
+int ccb_program_bind_peers(ccb_program_t prog, void* const* mailboxes, int nranks);
+
 /* ---------------------------------------------------------------- CUDA graphs
  * No counterpart in the reference (its executor launches every kernel from
  * the host). Work issued on `s` between ccb_graph_begin and ccb_graph_end

@@ -147,6 +147,12 @@ let program_run_device_events =
 let program_check = fn "ccb_program_check" (handle @-> int @-> handle @-> returning int)
 let program_lane_stream = fn "ccb_program_lane_stream" (handle @-> int @-> ptr handle @-> returning int)
 
+(* ---------------------------------------------------------------- sharded programs (no reference counterpart:
+   lib/backend_cuda/multi.ml:95-109 averages per-device results on the host) *)
+let program_shard = fn "ccb_program_shard" (handle @-> ptr int @-> ptr int @-> returning int)
+let program_mailbox_bytes = fn "ccb_program_mailbox_bytes" (handle @-> ptr size_t @-> returning int)
+let program_bind_peers = fn "ccb_program_bind_peers" (handle @-> ptr (ptr void) @-> int @-> returning int)
+
 (* ---------------------------------------------------------------- CUDA graphs (no reference counterpart) *)
 let graph_begin = fn "ccb_graph_begin" (handle @-> returning int)
 let graph_end = fn "ccb_graph_end" (handle @-> ptr handle @-> returning int)

@@ -63,10 +63,12 @@ let release c =
     Ccb.check "ccb_program_destroy" (!!Ccb.program_destroy c.prog)
   end
 
-let compile_on ~device ?(streams = 1) graph =
+(* ?shard:(rank, world): rank [rank] of a sharded Monte-Carlo program
+   (include/ccb.h, sharded programs); bind_peers before its first run. *)
+let compile_on ~device ?(streams = 1) ?shard graph =
   if streams < 1 then invalid_arg "Backend_cuda.compile_on: streams must be >= 1";
   let prog =
-    Ccb.get_handle "ccb_program_create" (!!Ccb.program_create (Wire.to_wire graph) device streams)
+    Ccb.get_handle "ccb_program_create" (!!Ccb.program_create (Wire.to_wire ?shard graph) device streams)
   in
   let c =
     {
@@ -81,6 +83,17 @@ let compile_on ~device ?(streams = 1) graph =
   in
   Gc.finalise (fun c -> try release c with _ -> ()) c;
   c
+
+let mailbox_bytes c =
+  Unsigned.Size_t.to_int
+    (Ccb.out Ctypes.size_t (fun p -> Ccb.check "ccb_program_mailbox_bytes" (!!Ccb.program_mailbox_bytes c.prog p)))
+
+(* Every rank's mailbox as this rank addresses it, in rank order; each owner
+   zero-fills its own before any rank's first run. *)
+let bind_peers c (mailboxes : unit Ctypes.ptr list) =
+  let arr = Ctypes.CArray.of_list (Ctypes.ptr Ctypes.void) mailboxes in
+  Ccb.check "ccb_program_bind_peers"
+    (!!Ccb.program_bind_peers c.prog (Ctypes.CArray.start arr) (List.length mailboxes))
 
 let compile_with ~streams graph = compile_on ~device:0 ~streams graph
 let compile graph = compile_on ~device:0 graph

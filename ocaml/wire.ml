@@ -14,6 +14,7 @@
      ccbgraph 1
      name <graph name>
      opt matmul tf32                      only when allow_tf32 is set
+     opt shard <rank> <world>             only for ~shard:(rank, world) with world > 1
      e <eid> <dtype> <expression node>    post-order, each shared node once
      t <tid> <dtype> <rank> <dims> <kind> <operands>   Graph.topological_order
      o <output name> <tid>                Graph.outputs order
@@ -90,7 +91,7 @@ let const_text : type a. a Dtype.t -> a -> string =
   | Dtype.I64 -> Int64.to_string v
   | Dtype.Bool -> if v then "1" else "0"
 
-let to_wire (g : Graph.t) : string =
+let to_wire ?shard (g : Graph.t) : string =
   let b = Buffer.create 8192 in
   let line fmt = Printf.kbprintf (fun b -> Buffer.add_char b '\n') b fmt in
   let seen : (int, unit) Hashtbl.t = Hashtbl.create 1024 in
@@ -178,6 +179,7 @@ let to_wire (g : Graph.t) : string =
   line "ccbgraph 1";
   line "name %s" (wire_name (Graph.name g));
   if !allow_tf32 then line "opt matmul tf32";
+  (match shard with Some (r, w) when w > 1 -> line "opt shard %d %d" r w | _ -> ());
   List.iter tensor (Graph.topological_order g);
   List.iter (fun (n, p) -> line "o %s %d" (wire_name n) (tid p)) (Graph.outputs g);
   line "end";
