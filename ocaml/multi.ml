@@ -15,7 +15,12 @@
    - [allreduce_sum]: recombine whole outputs on the devices with NCCL
      (ccb_allreduce inside ccb_group_start/end) over NVLink;
    - [allreduce_mean]: recombine scalar outputs with the cross-device sum
-     over NVLink peer memory (ccb_xrank_sum). *)
+     over NVLink peer memory (ccb_xrank_sum);
+   - [?sharded]: compile the unsplit graph on every device as one rank of a
+     sharded Monte-Carlo program (ccb_program_bind_peers): device i walks
+     paths [i*n/D, (i+1)*n/D) and the kernel's last block combines all
+     devices' totals over NVLink, so every device's outputs are already the
+     whole run's. *)
 
 open Cudacaml_ir
 open Cudacaml_runtime
@@ -114,6 +119,8 @@ type t = {
   per : int;
   counter : bool;
   split : string list option;
+  sharded : bool;
+  mailboxes : (int * Buffer.t) array;  (** sharded: (ordinal, mailbox) per device *)
   mutable comms : Ccb.handle array option;
   mutable released : bool;
 }
@@ -122,26 +129,56 @@ let release t =
   if not t.released then begin
     t.released <- true;
     Array.iter (fun (_, c) -> B.release c) t.slots;
+    Array.iter (fun (d, b) -> Device.with_device d (fun () -> Buffer.free b)) t.mailboxes;
     Option.iter (Array.iter (fun h -> ignore (!!Ccb.comm_destroy h))) t.comms;
     t.comms <- None
   end
 
-let create ~devices ~n ?counter_key ?split build =
+let create ~devices ~n ?counter_key ?split ?(sharded = false) build =
   let d = List.length devices in
   if d = 0 then invalid_arg "Multi.create: devices must not be empty";
   if n mod d <> 0 then invalid_arg (Printf.sprintf "Multi.create: n = %d is not divisible by %d devices" n d);
+  if sharded && (counter_key <> None || split <> None) then
+    invalid_arg "Multi.create: a sharded Multi splits the index space itself (no counter_key, no split)";
+  if sharded && List.length (List.sort_uniq compare devices) <> d then
+    invalid_arg "Multi.create: a sharded Multi needs distinct devices (its ranks wait on each other)";
   if counter_key <> None then ignore (path_range ~n ~d 0);
   let per = n / d in
+  let sharded = sharded && d > 1 in
   let slots =
     Array.of_list
-      (List.map
-         (fun ordinal ->
-           let g = build ~n:per in
-           let g = match counter_key with Some key -> offset_counters ~key ~rows:per g | None -> g in
-           (ordinal, B.compile_on ~device:ordinal g))
+      (List.mapi
+         (fun i ordinal ->
+           if sharded then (ordinal, B.compile_on ~device:ordinal ~shard:(i, d) (build ~n))
+           else
+             let g = build ~n:per in
+             let g = match counter_key with Some key -> offset_counters ~key ~rows:per g | None -> g in
+             (ordinal, B.compile_on ~device:ordinal g))
          devices)
   in
-  let t = { slots; n; per; counter = counter_key <> None; split; comms = None; released = false } in
+  let mailboxes =
+    if not sharded then [||]
+    else begin
+      let bytes = B.mailbox_bytes (snd slots.(0)) in
+      let ords = Array.of_list devices in
+      let boxes =
+        Array.map
+          (fun dv ->
+            Device.with_device dv (fun () ->
+                Array.iter (fun q -> if q <> dv then Ccb.check "ccb_peer_access_enable" (!!Ccb.peer_access_enable q)) ords;
+                let b = Buffer.alloc ~bytes in
+                Ccb.check "ccb_memset_d8"
+                  (!!Ccb.memset_d8 (Buffer.unsafe_ptr b) (Unsigned.UChar.of_int 0) (Unsigned.Size_t.of_int bytes) Stream.default);
+                Device.synchronize ();
+                (dv, b)))
+          ords
+      in
+      let ptrs = Array.to_list (Array.map (fun (_, b) -> Buffer.unsafe_ptr b) boxes) in
+      Array.iter (fun (_, c) -> B.bind_peers c ptrs) slots;
+      boxes
+    end
+  in
+  let t = { slots; n; per; counter = counter_key <> None; split; sharded; mailboxes; comms = None; released = false } in
   Gc.finalise (fun t -> try release t with _ -> ()) t;
   t
 
@@ -166,6 +203,7 @@ let splits t name v =
   | None -> leading_dim v = Some t.n
 
 let inputs_for t i inputs =
+  if t.sharded then inputs else
   let ins = List.map (fun (name, v) -> if splits t name v then (name, slice ~index:i ~per:t.per v) else (name, v)) inputs in
   if t.counter then
     let first, _ = path_range ~n:t.n ~d:(Array.length t.slots) i in
@@ -309,6 +347,11 @@ let peer_of ords =
 
 let allreduce_mean t ~names ~inputs =
   if t.released then failwith "Multi.run: this Multi.t has been released";
+  if t.sharded then
+    (* every device's outputs are already the whole run's *)
+    let outs = List.hd (run t ~inputs) in
+    List.map (fun name -> (name, scalar_float (List.assoc name outs))) names
+  else
   let ords = Array.map fst t.slots in
   if List.length (List.sort_uniq compare (Array.to_list ords)) <> Array.length ords then
     invalid_arg "Multi.allreduce: a cross-device sum needs distinct devices; use mean_scalar for repeats";
