@@ -365,6 +365,23 @@ class Multi:
     def run_per_device(self, inputs_fn):
         if self.released:
             raise RuntimeError("Multi.run: this Multi.t has been released")
+        if self.sharded:
+            # A sharded kernel's last block waits for every device's totals, so
+            # every device's run is issued before the host waits on any of them
+            # (a host-buffer run would block in its pageable download first).
+            keep = self._issue_resident(inputs_fn)
+            out = []
+            for i, c in enumerate(self.slots):
+                with R.with_device(c.device):
+                    B.check_device(c, c.lane_stream(0))
+                    vals = []
+                    for (name, dt, shape), buf in zip(c.outputs, keep[i][1]):
+                        host = np.empty(numel(shape), dtype=dt.np)
+                        buf.download(host)
+                        vals.append((name, Value(dt, tuple(shape), host)))
+                    out.append(vals)
+            self._free_resident(keep)
+            return out
         jobs = [B.run_async(c, inputs_fn(i)) for i, c in enumerate(self.slots)]
         return [B.wait(j) for j in jobs]
 
@@ -429,12 +446,16 @@ class Multi:
         return result
 
     def _run_all_resident(self, inputs):
+        return self._issue_resident(lambda i: self._inputs_for(i, inputs))
+
+    def _issue_resident(self, inputs_fn):
         """Upload every device's inputs and run it resident on its lane
-        stream; returns [(input buffers, output buffers)] per device."""
+        stream, without waiting on any; returns [(input buffers, output
+        buffers)] per device."""
         keep = []
         for i, c in enumerate(self.slots):
             with R.with_device(c.device):
-                bound = dict(self._inputs_for(i, inputs))
+                bound = dict(inputs_fn(i))
                 in_bufs = []
                 for pname, dt, shape in c.params:
                     buf = R.Buffer(bound[pname].byte_size)

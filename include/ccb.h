@@ -189,8 +189,11 @@ int ccb_program_lane_stream(ccb_program_t prog, int lane, ccb_stream_t* stream);
  * a peer allocation after ccb_peer_access_enable), 8-byte aligned; every
  * owner zero-fills its mailbox before any rank's first run after binding,
  * and every rank runs the program the same number of times in the same
- * order, one run at a time. A run before binding is CCB_ERR_INVALID; a run
- * under stream capture is refused. A peer that never runs makes the bounded
+ * order, one run at a time. The ranks wait on each other inside the kernel,
+ * so a thread that drives several ranks issues every rank's run before it
+ * waits on any (a run whose outputs are pageable host memory blocks the
+ * issuing thread until its download is done). A run before binding is
+ * CCB_ERR_INVALID; a run under stream capture is refused. A peer that never runs makes the bounded
  * wait give up: ccb_program_check / wait report CCB_ERR_DEVICE_CHECK and the
  * scalar outputs keep their previous contents. No counterpart in the
  * reference. */

@@ -212,8 +212,31 @@ let inputs_for t i inputs =
 
 let run_per_device t ~inputs =
   if t.released then failwith "Multi.run: this Multi.t has been released";
-  let jobs = Array.mapi (fun i (_, c) -> B.run_async c ~inputs:(inputs i)) t.slots in
-  Array.to_list (Array.map B.wait jobs)
+  if t.sharded then begin
+    (* every device's run is issued before any is waited on: a sharded
+       kernel's last block waits for all devices' totals *)
+    let issued =
+      Array.mapi
+        (fun i (d, c) ->
+          Device.with_device d (fun () ->
+              let ins = List.map (fun (nm, v) -> (nm, B.upload v)) (inputs i) in
+              (ins, B.issue_resident c ~inputs:ins)))
+        t.slots
+    in
+    Array.to_list
+      (Array.mapi
+         (fun i (ins, outs) ->
+           let d, c = t.slots.(i) in
+           B.check c;
+           Device.with_device d (fun () ->
+               let vals = List.map (fun (nm, r) -> (nm, B.download r)) outs in
+               List.iter (fun (_, r) -> B.free_resident r) (ins @ outs);
+               vals))
+         issued)
+  end
+  else
+    let jobs = Array.mapi (fun i (_, c) -> B.run_async c ~inputs:(inputs i)) t.slots in
+    Array.to_list (Array.map B.wait jobs)
 
 let run t ~inputs = run_per_device t ~inputs:(fun i -> inputs_for t i inputs)
 

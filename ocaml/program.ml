@@ -176,9 +176,11 @@ let download r =
 let free_resident r = Buffer.free r.buf
 
 (* Zero-copy on the residents' pointers; outputs are freshly allocated
-   residents the caller owns. Lane 0, synchronised before it returns, the
-   lane's device error word checked (ccb_program_check). *)
-let run_resident c ~inputs =
+   residents the caller owns. issue_resident only issues the run on lane 0
+   (check synchronises and reads the lane's device error word); run_resident
+   does both. The ranks of a sharded program wait on each other inside the
+   kernel, so Multi issues every device's run before it checks any. *)
+let issue_resident c ~inputs =
   live c;
   Device.with_device c.device (fun () ->
       let ins =
@@ -206,5 +208,12 @@ let run_resident c ~inputs =
         (!!Ccb.program_run_device c.prog 0 (arr ins)
            (arr (List.map (fun (_, r) -> Buffer.unsafe_ptr r.buf) outs))
            Stream.default);
-      Ccb.check "ccb_program_check" (!!Ccb.program_check c.prog 0 Stream.default);
       outs)
+
+let check c =
+  Device.with_device c.device (fun () -> Ccb.check "ccb_program_check" (!!Ccb.program_check c.prog 0 Stream.default))
+
+let run_resident c ~inputs =
+  let outs = issue_resident c ~inputs in
+  check c;
+  outs
