@@ -1888,6 +1888,7 @@ class Lowerer {
     f.decl = std::string("const ") + dt_ctype(g.ts[t].dt) + "* __restrict__ b" + std::to_string(t);
     f.slot.kind = SL_BUF;
     f.slot.buf = node_buf[t];
+    f.slot.access = 0;
     return f;
   }
   Field out_field(int t) {
@@ -1895,6 +1896,7 @@ class Lowerer {
     f.decl = std::string(dt_ctype(g.ts[t].dt)) + "* __restrict__ o" + std::to_string(t);
     f.slot.kind = SL_BUF;
     f.slot.buf = node_buf[t];
+    f.slot.access = 1;
     return f;
   }
   static Field buf_field(const std::string& decl, int buf) {
@@ -2796,6 +2798,7 @@ class Lowerer {
     } else {  // B^T stored [N][K]: one 32 x 256 box (32 x 128 per CTA of a pair)
       fb.slot.tdim[0] = K, fb.slot.tdim[1] = N, fb.slot.tstride = K * 4, fb.slot.tbox[1] = pair ? 128 : 256;
     }
+    fa.slot.access = fb.slot.access = 0;  // operands are only ever loaded through their maps
     fields.push_back(fa);  // tensor maps first: 64-byte aligned in the block
     fields.push_back(fb);
     if (store_c) fields.push_back(buf_field("float* __restrict__ C", node_buf[t]));
@@ -2905,6 +2908,58 @@ class Lowerer {
     l.per_block = 1;
   }
 
+  // Launch order. The ops of a run execute in one stream, so any order that
+  // keeps every buffer hazard (two ops touching one buffer, at least one
+  // writing it; the shared error word, only ever OR-ed into, is exempt)
+  // computes the same bits. Among the ops whose predecessors have been
+  // issued, one that writes a program output goes first (then graph order),
+  // so a consumer of that output on another stream -- a gradient's
+  // all-reduce, started from the event ccb_program_run_device_events records
+  // after the output's last kernel -- overlaps the rest of the program: the
+  // MLP step's dW2 product now runs right after dY, ahead of dA1, dZ1, dW1.
+  void schedule_ops(Lowered& o) {
+    const int n = (int)o.ops.size();
+    std::vector<std::vector<std::pair<int, int>>> use(n);  // (buffer, access)
+    for (int i = 0; i < n; ++i) {
+      const OpSpec& op = o.ops[i];
+      if (op.kind == OP_ZERO) {
+        use[i].push_back({op.buf, 1});
+        continue;
+      }
+      for (const Slot& sl : o.launches[op.launch].slots)
+        if ((sl.kind == SL_BUF || sl.kind == SL_TMAP) && sl.buf >= 0 && sl.buf != o.err_buf) use[i].push_back({sl.buf, sl.access});
+    }
+    std::set<int> out_bufs;
+    for (const IOSpec& io : o.outputs) out_bufs.insert(io.buf);
+    std::vector<int> npred(n, 0), prio(n, 0);
+    std::vector<std::vector<int>> succ(n);
+    for (int j = 0; j < n; ++j) {
+      for (auto& u : use[j])
+        if (u.second != 0 && out_bufs.count(u.first)) prio[j] = 1;
+      for (int i = 0; i < j; ++i) {
+        bool dep = false;
+        for (auto& a : use[i])
+          for (auto& b : use[j])
+            if (a.first == b.first && (a.second != 0 || b.second != 0)) dep = true;
+        if (dep) {
+          succ[i].push_back(j);
+          ++npred[j];
+        }
+      }
+    }
+    std::vector<OpSpec> order;
+    std::vector<char> done(n, 0);
+    for (int k = 0; k < n; ++k) {
+      int pick = -1;
+      for (int i = 0; i < n; ++i)
+        if (!done[i] && npred[i] == 0 && (pick < 0 || prio[i] > prio[pick])) pick = i;
+      done[pick] = 1;
+      order.push_back(o.ops[pick]);
+      for (int j : succ[pick]) --npred[j];
+    }
+    o.ops = order;
+  }
+
   void generate(Lowered& o) {
     out = &o;
     o.name = g.name;
@@ -2962,6 +3017,7 @@ class Lowerer {
       o.outputs.push_back(io);
     }
     o.source = src.str();
+    schedule_ops(o);
     // plan text
     std::ostringstream pt;
     for (size_t b = 0; b < o.bufs.size(); ++b) {

@@ -80,6 +80,9 @@ enum SlotKind { SL_BUF = 0, SL_I64 = 1, SL_EPOCH = 2, SL_TMAP = 3, SL_XMB = 4, S
 struct Slot {
   int kind = SL_BUF;
   int buf = -1;
+  // how the kernel uses `buf` (SL_BUF, SL_TMAP): 0 reads it, 1 writes it,
+  // 2 both or unknown; the launch scheduler keeps every hazard it implies
+  int access = 2;
   int64_t val = 0;
   int64_t tdim[3] = {0, 0, 1};
   int64_t tstride = 0, tstride2 = 0;  // bytes between dim-1 / dim-2 steps

@@ -293,3 +293,19 @@ def test_staged_row_kernels_are_opt_in_and_compile(monkeypatch):
     x = D.param("x", F32, (64, 4096))
     mapped = Graph("r", [("r", D.reduce_rows(D.add, D.const(F32, 0.0), D.map(D.exp, x)))])
     assert "rowsstaged" not in B.lower_info(mapped)["plan"]  # the source is an expression, not a buffer
+
+
+def test_output_products_are_launched_as_soon_as_their_inputs_are_ready():
+    """The MLP step's dW2 = A1^T dY needs only the forward pass and dY, so it
+    is launched right after the dY/loss pass, ahead of dA1, dZ1 and dW1 (an
+    all-reduce of dW2 on another stream then overlaps them); every launch
+    still follows the ones whose buffers it reads."""
+    for prec in ("tf32", "f32"):
+        plan = B.lower_info(X.mlp_step(256, 128, 256, 64), matmul=prec)["plan"]
+        launches = [ln.split()[1] for ln in plan.splitlines() if ln.startswith("launch")]
+        idx = [int(re.match(r"ccb_[a-z0-9]+_(\d+)_", f).group(1)) for f in launches]
+        w2 = idx.index(max(idx))  # dW2: the last group of the graph
+        assert "mapreduce" in launches[w2 - 1], launches  # right after the dY / loss pass
+        assert "matmul" in launches[w2 + 1] and "mapreduce" in launches[w2 + 2], launches  # then dA1, dZ1
+        rest = [k for k in idx if k != max(idx)]
+        assert rest == sorted(rest), launches  # the others keep graph order
