@@ -1,3 +1,4 @@
+#include <cstdlib>
 #include "dyn.hpp"
 
 #include <dlfcn.h>
@@ -125,7 +126,15 @@ const Nccl& nccl() {
   static Nccl n;
   static std::once_flag once;
   std::call_once(once, [] {
-    void* h = open_first({"libnccl.so.2", "libnccl.so"}, n.why);
+    // One NCCL per process: a copy already loaded (by the host application,
+    // e.g. the framework that drives the other ranks) is used as it is, then
+    // the one CCB_NCCL_LIB names, then the loader's default. Loading a second,
+    // different libnccl.so.2 first would bind the application's later NCCL
+    // users to it.
+    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
+    if (!h)
+      if (const char* lib = std::getenv("CCB_NCCL_LIB")) h = dlopen(lib, RTLD_NOW | RTLD_GLOBAL);
+    if (!h) h = open_first({"libnccl.so.2", "libnccl.so"}, n.why);
     if (!h) return;
     bool ok = true;
 #define S(name) ok = ok && sym(h, n.name, #name, n.why);

@@ -140,10 +140,31 @@ def lib():
     if _LIB is None:
         if not os.path.exists(LIB_PATH):
             raise ImportError(f"libccb.so is not built at {LIB_PATH}; run cudacaml_b200.runtime.build()")
+        _preload_nccl()
         L = ctypes.CDLL(LIB_PATH)
         _declare(L)
         _LIB = L
     return _LIB
+
+
+def _preload_nccl():
+    """Load the NCCL that torch links against (the nvidia-nccl wheel), if it is
+    installed, before libccb.so opens one: libccb.so then reuses it, and a
+    later `import torch` in the same process does not find an older system
+    libnccl.so.2 already bound to the name."""
+    try:
+        import importlib.util
+        spec = importlib.util.find_spec("nvidia.nccl")
+    except (ImportError, ValueError):
+        return
+    for d in (spec.submodule_search_locations or []) if spec else []:
+        path = os.path.join(d, "lib", "libnccl.so.2")
+        if os.path.exists(path):
+            try:
+                ctypes.CDLL(path, mode=ctypes.RTLD_GLOBAL)
+            except OSError:
+                pass
+            return
 
 
 def exported_symbols():

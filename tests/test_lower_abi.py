@@ -309,3 +309,16 @@ def test_output_products_are_launched_as_soon_as_their_inputs_are_ready():
         assert "matmul" in launches[w2 + 1] and "mapreduce" in launches[w2 + 2], launches  # then dA1, dZ1
         rest = [k for k in idx if k != max(idx)]
         assert rest == sorted(rest), launches  # the others keep graph order
+
+
+def test_one_nccl_per_process():
+    """libccb.so binds the NCCL that torch links against when that wheel is
+    installed, so a test that imports torch after a collective of this
+    library does not meet an older libnccl.so.2 bound to the same name."""
+    import importlib.util
+    spec = importlib.util.find_spec("nvidia.nccl")
+    if spec is None:
+        pytest.skip("no nvidia-nccl wheel")
+    R.lib()
+    maps = [ln.split()[-1] for ln in open("/proc/self/maps") if "libnccl.so" in ln]
+    assert maps and all("nvidia/nccl/lib" in m for m in maps), sorted(set(maps))
