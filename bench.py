@@ -52,12 +52,12 @@ sys.path.insert(0, ROOT)
 PATHS = 1 << 28
 SEED = 42
 # Warp instructions executed per path by the fused F64 Greeks kernel, from
-# ncu's smsp__inst_executed.sum over 2^20 paths (9,322,613 / 2^20):
+# ncu's smsp__inst_executed.sum over 2^20 paths (9,226,495 / 2^20):
 # profiles/mapreduce_bs_greeks_f64_2p20_instructions.md.
-INST_PER_PATH_F64 = 9322613 / (1 << 20)
-# DRAM bytes per launch of the same kernel (read 44,288, write 0; constant in
+INST_PER_PATH_F64 = 9226495 / (1 << 20)
+# DRAM bytes per launch of the same kernel (read 42,496, write 0; constant in
 # the path count), same capture.
-DRAM_BYTES_GREEKS_F64 = 44288
+DRAM_BYTES_GREEKS_F64 = 42496
 
 
 def peaks():

@@ -288,7 +288,10 @@ int parse_graph(const char* text, GGraph& g) {
 // ===================================================================== kernel expression IR
 // A hash-consed DAG of scalar operations over loads, the loop index and (in
 // an epilogue) the final values of the pass's reductions.
-enum KOp { K_CONST, K_INDEX, K_LOAD, K_BIN, K_UN, K_CMP, K_LOGIC, K_NOT, K_SELECT, K_CAST, K_REDVAL, K_CHECK, K_ARG };
+// K_CAST with sub = 1: an I32 read as unsigned, to F64. K_FMA: a * b + c in
+// one rounding; only made where the exact result is representable (the
+// unsigned-word affine forms of fold()), so it equals the unfused chain.
+enum KOp { K_CONST, K_INDEX, K_LOAD, K_BIN, K_UN, K_CMP, K_LOGIC, K_NOT, K_SELECT, K_CAST, K_REDVAL, K_CHECK, K_ARG, K_FMA };
 
 struct KN {
   int op = K_CONST;
@@ -521,8 +524,107 @@ struct KCtx {
  private:
   static int64_t wrap(Dt dt, int64_t v) { return dt == DT_I32 ? (int64_t)(int32_t)(uint32_t)(uint64_t)v : v; }
 
+  // Rng turns its I32 word into a float by reading it as unsigned through a
+  // select on the sign (w < 0 ? double(w) + 2^32 : double(w)), then
+  // (u + 0.5) * 2^-32, and Rng.normal takes 2u - 1 (rng.ml:61-74). Every value
+  // of such a chain is U * s + t for the unsigned word U in [0, 2^32), a power
+  // of two s and a constant t, and is exact in F64 while its significant bits
+  // (from U * s's top bit down to the lowest bit of s and t) number at most
+  // 53; each step of the chain then rounds nothing, so the whole chain equals
+  // one unsigned conversion and one FMA of U, s and t, bit for bit. The
+  // select becomes K_CAST sub 1; each affine step on it becomes K_FMA(U, s, t).
+  bool unsigned_affine(int id, int& u, double& s, double& t) const {
+    const KN& x = n[id];
+    if (x.op == K_CAST && x.dt == DT_F64 && x.sub == 1) {
+      u = id, s = 1.0, t = 0.0;
+      return true;
+    }
+    if (x.op == K_CAST && x.dt == DT_F64 && n[x.a].dt == DT_F64) return unsigned_affine(x.a, u, s, t);
+    if (x.op == K_FMA && x.dt == DT_F64) {
+      u = x.a, s = n[x.b].f, t = n[x.c].f;
+      return true;
+    }
+    return false;
+  }
+  static bool exact_affine(double s, double t) {
+    int es = 0, et = 0;
+    if (!(s > 0) || std::frexp(s, &es) != 0.5) return false;  // s a power of two: s = 2^(es - 1)
+    const double top = 4294967296.0 * s + std::fabs(t);
+    if (!(top < 1e300)) return false;
+    int etop = 0;
+    std::frexp(top, &etop);
+    int low = es - 1;
+    if (t != 0) {
+      double m = std::frexp(t, &et);  // t = m * 2^et, 0.5 <= |m| < 1
+      int lb = et - 53;               // the lowest set bit of t
+      for (int i = 0; i < 53 && std::ldexp(m, 53 - i) == std::trunc(std::ldexp(m, 53 - i)); ++i) lb = et - 53 + i;
+      low = std::min(low, lb);
+    }
+    return etop - low <= 53 && low > -1000;
+  }
+  bool fold_unsigned_word(KN& k) {
+    auto cf = [&](int id, double& v) {
+      if (id < 0 || n[id].op != K_CONST || n[id].dt != DT_F64) return false;
+      v = n[id].f;
+      return true;
+    };
+    if (k.op == K_SELECT) {
+      const KN& c = n[k.a];
+      if (!(c.op == K_CMP && c.sub == C_LT && n[c.a].dt == DT_I32 && n[c.b].op == K_CONST && n[c.b].iv == 0)) return false;
+      const int w = c.a;
+      const KN& f = n[k.c];
+      if (!(f.op == K_CAST && f.sub == 0 && f.a == w)) return false;
+      const KN& g = n[k.b];
+      double big = 0;
+      if (!(g.op == K_BIN && g.sub == B_ADD && ((g.a == k.c && cf(g.b, big)) || (g.b == k.c && cf(g.a, big))) &&
+            big == 4294967296.0))
+        return false;
+      k = KN();
+      k.op = K_CAST;
+      k.dt = DT_F64;
+      k.a = w;
+      k.sub = 1;
+      return true;
+    }
+    if (k.op != K_BIN || (k.sub != B_ADD && k.sub != B_SUB && k.sub != B_MUL)) return false;
+    int u = -1;
+    double s = 0, t = 0, c = 0;
+    bool left = false;
+    if (unsigned_affine(k.a, u, s, t) && cf(k.b, c)) left = true;
+    else if (!(unsigned_affine(k.b, u, s, t) && cf(k.a, c))) return false;
+    double s2 = s, t2 = t;
+    if (k.sub == B_ADD) {
+      t2 = t + c;
+    } else if (k.sub == B_SUB) {
+      if (!left) return false;  // c - (U s + t) is not of the form
+      t2 = t - c;
+    } else {
+      int e = 0;
+      if (!(c > 0) || std::frexp(c, &e) != 0.5) return false;  // scaling by a power of two only
+      s2 = s * c;
+      t2 = t * c;
+    }
+    // t +- c must be exact (the rounding error of the sum, by Knuth's
+    // two-sum, is zero), and every value of both forms exact
+    if (k.sub != B_MUL) {
+      const double b = k.sub == B_ADD ? c : -c;
+      const double bv = t2 - t, av = t2 - bv;
+      if ((t - av) + (b - bv) != 0.0) return false;
+    }
+    if (!exact_affine(s2, t2) || !exact_affine(s, t)) return false;
+    KN r;
+    r.op = K_FMA;
+    r.dt = DT_F64;
+    r.a = u;
+    r.b = cfloat(DT_F64, s2);
+    r.c = cfloat(DT_F64, t2);
+    k = r;
+    return true;
+  }
+
   // Exact integer simplification only (float folding is left to the device
-  // compiler, which rounds exactly as the device does).
+  // compiler, which rounds exactly as the device does), and the exact
+  // unsigned-word chains above.
   void fold(KN& k) {
     auto is_c = [&](int id, int64_t v) { return id >= 0 && n[id].op == K_CONST && is_int(n[id].dt) && n[id].iv == v; };
     if (k.op == K_CAST && n[k.a].op == K_CONST && is_int(k.dt) && is_int(n[k.a].dt)) {
@@ -566,6 +668,7 @@ struct KCtx {
     if (k.op == K_BIN && k.a > k.b &&
         (k.sub == B_ADD || k.sub == B_MUL || (is_int(k.dt) && (k.sub == B_AND || k.sub == B_OR || k.sub == B_XOR))))
       std::swap(k.a, k.b);
+    if (k.dt == DT_F64 && fold_unsigned_word(k)) return;
     if (k.op == K_BIN && k.sub == B_MUL && is_float(k.dt)) {  // x * 1.0 == x exactly, NaN and -0 included
       auto one = [&](int id) { return n[id].op == K_CONST && n[id].f == 1.0; };
       if (one(k.a) || one(k.b)) {
@@ -914,7 +1017,12 @@ struct Emitter {
       case K_LOGIC: e = "(" + val(k.a) + (k.sub == 0 ? " && " : " || ") + val(k.b) + ")"; break;
       case K_NOT: e = "(!" + val(k.a) + ")"; break;
       case K_SELECT: e = "(" + val(k.a) + " ? " + val(k.b) + " : " + val(k.c) + ")"; break;
+      case K_FMA: e = "fma(" + val(k.a) + ", " + val(k.b) + ", " + val(k.c) + ")"; break;
       case K_CAST: {
+        if (k.sub == 1) {  // the word read as unsigned
+          e = "((double)(unsigned int)(" + val(k.a) + "))";
+          break;
+        }
         // (int)(((u64)zext(a) * (u64)zext(b)) >> 32) is the high word of the
         // 32x32 product: spell it __umulhi so it maps to one multiply.
         std::string ua, ub;
