@@ -52,12 +52,12 @@ sys.path.insert(0, ROOT)
 PATHS = 1 << 28
 SEED = 42
 # Warp instructions executed per path by the fused F64 Greeks kernel, from
-# ncu's smsp__inst_executed.sum over 2^20 paths (9,226,495 / 2^20):
+# ncu's smsp__inst_executed.sum over 2^20 paths (9,029,887 / 2^20):
 # profiles/mapreduce_bs_greeks_f64_2p20_instructions.md.
-INST_PER_PATH_F64 = 9226495 / (1 << 20)
-# DRAM bytes per launch of the same kernel (read 42,496, write 0; constant in
+INST_PER_PATH_F64 = 9029887 / (1 << 20)
+# DRAM bytes per launch of the same kernel (read 42,240, write 0; constant in
 # the path count), same capture.
-DRAM_BYTES_GREEKS_F64 = 42496
+DRAM_BYTES_GREEKS_F64 = 42240
 
 
 def peaks():

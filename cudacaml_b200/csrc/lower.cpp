@@ -984,11 +984,95 @@ struct Emitter {
     return zext32(m.a, a) && zext32(m.b, b);
   }
 
+  // Philox's mulhilo uses the high and the low word of one 32x32 product:
+  // the high word through the __umulhi spelling below, the low word as an I32
+  // multiply of the same operands. Such a pair is computed once, as a 64-bit
+  // product that both words are read from.
+  std::string opkey(int id) const {  // an I32 operand: a constant by value, any other node by id
+    const KN& x = c.n[id];
+    return x.op == K_CONST ? "c" + std::to_string(x.iv) : "n" + std::to_string(id);
+  }
+  bool zext32_key(int id, std::string& key) const {
+    const KN& k = c.n[id];
+    if (k.op == K_CONST && k.dt == DT_I64 && k.iv >= 0 && k.iv <= 0xFFFFFFFFLL) {
+      key = "c" + std::to_string((int64_t)(int32_t)(uint32_t)k.iv);
+      return true;
+    }
+    if (k.op == K_BIN && k.sub == B_AND && k.dt == DT_I64)
+      for (int s = 0; s < 2; ++s) {
+        const int m = s ? k.a : k.b, v = s ? k.b : k.a;
+        if (c.n[m].op == K_CONST && c.n[m].iv == 0xFFFFFFFFLL && c.n[v].op == K_CAST && c.n[c.n[v].a].dt == DT_I32) {
+          key = opkey(c.n[v].a);
+          return true;
+        }
+      }
+    return false;
+  }
+  static std::string pair_key(std::string a, std::string b) {
+    if (b < a) std::swap(a, b);
+    return a + "*" + b;
+  }
+  bool hi_key(int id, std::string& key) const {  // id: the I32 cast of SHR(MUL(zext a, zext b), 32)
+    const KN& k = c.n[id];
+    if (!(k.op == K_CAST && k.dt == DT_I32 && k.sub == 0)) return false;
+    const KN& s = c.n[k.a];
+    if (!(s.op == K_BIN && s.sub == B_SHR && s.dt == DT_I64 && c.n[s.b].op == K_CONST && c.n[s.b].iv == 32)) return false;
+    const KN& m = c.n[s.a];
+    std::string ka, kb;
+    if (!(m.op == K_BIN && m.sub == B_MUL && m.dt == DT_I64 && zext32_key(m.a, ka) && zext32_key(m.b, kb))) return false;
+    key = pair_key(ka, kb);
+    return true;
+  }
+  bool lo_key(int id, std::string& key) const {
+    const KN& k = c.n[id];
+    if (!(k.op == K_BIN && k.sub == B_MUL && k.dt == DT_I32)) return false;
+    key = pair_key(opkey(k.a), opkey(k.b));
+    return true;
+  }
+  bool scanned = false;
+  std::set<std::string> his, los;
+  std::unordered_map<std::string, std::string> wide;  // pair -> name of the 64-bit product
+  bool paired(const std::string& key) {
+    if (!scanned) {
+      scanned = true;
+      for (int i = 0; i < (int)c.n.size(); ++i) {
+        std::string kk;
+        if (hi_key(i, kk)) his.insert(kk);
+        if (lo_key(i, kk)) los.insert(kk);
+      }
+    }
+    return his.count(key) && los.count(key);
+  }
+  std::string wide_product(const std::string& key, const std::string& a, const std::string& b) {
+    auto it = wide.find(key);
+    if (it != wide.end()) return it->second;
+    const std::string nm = "w" + std::to_string(wide.size()) + suffix;
+    o << ind << "const unsigned long long " << nm << " = (unsigned long long)(unsigned int)(" << a << ") * (unsigned int)(" << b
+      << ");\n";
+    wide[key] = nm;
+    return nm;
+  }
+
   std::string val(int id) {
     auto it = name.find(id);
     if (it != name.end()) return it->second;
     const KN& k = c.n[id];
     std::string e;
+    std::string pk;
+    if (lo_key(id, pk) && paired(pk)) {
+      const std::string a = val(k.a), b = val(k.b);
+      e = "((int)(unsigned int)" + wide_product(pk, a, b) + ")";
+    } else if (hi_key(id, pk) && paired(pk)) {
+      std::string ua, ub;
+      mulhi_operands(k.a, ua, ub);
+      e = "((int)(" + wide_product(pk, ua, ub) + " >> 32))";
+    }
+    if (!e.empty()) {
+      std::string nm = "v" + std::to_string(id) + suffix;
+      o << ind << "const int " << nm << " = " << e << ";\n";
+      name[id] = nm;
+      return nm;
+    }
     switch (k.op) {
       case K_CONST: return lit(k);
       case K_INDEX: return index_text;

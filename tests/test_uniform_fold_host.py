@@ -41,3 +41,12 @@ def test_greeks_source_uses_the_folded_form():
         src = B.source(X.call_greeks(1 << 20, dt))
         assert "(double)(unsigned int)(" in src and "fma(" in src, dt
         assert "0x1p+32" not in src  # the sign fix-up select is gone
+
+
+def test_philox_high_and_low_words_share_one_product():
+    """Each Philox multiply whose high and low words are both used is
+    emitted once, as a 64-bit product both words are read from."""
+    src = B.source(X.call_greeks(1 << 20, F64))
+    body = src[src.find("void elem(const P& p, int i"):src.find("void elem4(")]
+    assert body.count("const unsigned long long w") >= 18  # 20 products per draw, 2 of them seed-only
+    assert body.count("__umulhi") == 0
