@@ -301,10 +301,63 @@ int compile_tuned(const Lowered& L, CUmodule& mod, std::vector<std::string>& rel
     if (local > 0) relaxed.push_back(l.fn);
   }
   if (relaxed.empty()) return CCB_OK;
+  std::vector<std::string> base = opts;
   for (const auto& fn : relaxed) opts.push_back("-DCCB_MINB_" + fn.substr(14) + "=1");
   d.cuModuleUnload(mod);
   mod = nullptr;
   CCB_TRY(nvrtc_compile_opts(L.source, name, opts, cubin, log));
+  CCB_CU(d.cuModuleLoadData(&mod, cubin.data()));
+  // Without the bound a pass runs at the occupancy its registers allow; one
+  // more resident block per SM often fits without local memory (the LSM date
+  // pass: 138 registers, 1 block/SM, unbounded; 128 registers, 2 blocks/SM,
+  // no spills, with the bound 2). Try that level for every relaxed pass and
+  // keep it where nothing spills.
+  std::vector<int> level(relaxed.size(), 1);
+  std::vector<std::string> up = base;
+  bool any = false;
+  for (size_t r = 0; r < relaxed.size(); ++r) {
+    CUfunction f;
+    CCB_CU(d.cuModuleGetFunction(&f, mod, relaxed[r].c_str()));
+    int occ = 1;
+    d.cuOccupancyMaxActiveBlocksPerMultiprocessor(&occ, f, 256, 0);
+    const int next = std::max(1, occ) + 1;
+    if (next < 8) {
+      level[r] = next;
+      any = true;
+    }
+    up.push_back("-DCCB_MINB_" + relaxed[r].substr(14) + "=" + std::to_string(level[r]));
+  }
+  if (!any) return CCB_OK;
+  std::string cubin2, log2;
+  CUmodule mod2 = nullptr;
+  CCB_TRY(nvrtc_compile_opts(L.source, name, up, cubin2, log2));
+  CCB_CU(d.cuModuleLoadData(&mod2, cubin2.data()));
+  std::vector<char> keep(relaxed.size(), 0);
+  int kept = 0;
+  for (size_t r = 0; r < relaxed.size(); ++r) {
+    if (level[r] == 1) continue;
+    CUfunction f;
+    int local = 0;
+    CCB_CU(d.cuModuleGetFunction(&f, mod2, relaxed[r].c_str()));
+    CCB_CU(d.cuFuncGetAttribute(&local, CU_FUNC_ATTRIBUTE_LOCAL_SIZE_BYTES, f));
+    keep[r] = local == 0;
+    kept += keep[r];
+  }
+  if (kept == 0) {
+    d.cuModuleUnload(mod2);
+    return CCB_OK;
+  }
+  int raised = 0;
+  for (size_t r = 0; r < relaxed.size(); ++r) raised += level[r] > 1;
+  d.cuModuleUnload(mod);
+  mod = mod2;
+  if (kept == raised) return CCB_OK;
+  std::vector<std::string> mixed = base;  // some passes spill one level up: those stay unbounded
+  for (size_t r = 0; r < relaxed.size(); ++r)
+    mixed.push_back("-DCCB_MINB_" + relaxed[r].substr(14) + "=" + std::to_string(keep[r] ? level[r] : 1));
+  d.cuModuleUnload(mod);
+  mod = nullptr;
+  CCB_TRY(nvrtc_compile_opts(L.source, name, mixed, cubin, log));
   CCB_CU(d.cuModuleLoadData(&mod, cubin.data()));
   return CCB_OK;
 }
