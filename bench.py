@@ -556,7 +556,60 @@ def secondary_reference_nvrtc(dev, flush, ours):
     return res
 
 
-def measure_greeks(args, dtype, rank, world, local, dist, peer, flush, weak=False, exchange=None):
+def sharded_probe(rank, world, local, dist, exchange):
+    """A small sharded Greeks run (2^20 paths, two runs, checked) before the
+    headline relies on sharded programs. Every rank reaches the same
+    collectives whatever fails, and learns whether all ranks succeeded (MIN
+    all-reduces), so a failure on any rank sends every rank to the split-then-
+    sum path instead of leaving ranks waiting on each other. Returns
+    (ok, reason)."""
+    import numpy as np
+    import torch
+    from cudacaml_b200 import backend_cuda as B
+    from cudacaml_b200 import examples as X
+    from cudacaml_b200 import multi as M
+    from cudacaml_b200 import runtime as R
+    from cudacaml_b200.ir import F64
+
+    def agree(ok):
+        t = torch.tensor([1.0 if ok else 0.0], device=f"cuda:{local}")
+        dist.all_reduce(t, op=dist.ReduceOp.MIN)
+        return float(t[0]) > 0.5
+
+    why, c, sp, bufs = None, None, None, []
+    try:
+        c = B.compile_on(local, X.call_greeks(1 << 20, F64), shard=(rank, world))
+    except Exception as e:  # noqa: BLE001 - reported, the headline falls back
+        why = f"compile: {type(e).__name__}: {e}"
+    if agree(why is None):
+        try:
+            sp = M.ShardPeers(c, exchange)  # a collective: every rank calls it
+            host = {"s0": 100.0, "vol": 0.2, "rate": 0.05}
+            for name, dt, _ in c.params:
+                b = R.Buffer(8 if dt.value == "f64" else 4)
+                b.upload(np.array([host[name]]) if name in host else np.array([SEED], np.int32))
+                bufs.append(b)
+            out = R.Buffer(32)
+            bufs.append(out)
+            for _ in range(2):
+                B.run_device_ptrs(c, [b.ptr for b in bufs[:-1]], [out.ptr + 8 * j for j in range(4)], None)
+            B.check_device(c, None)
+        except Exception as e:  # noqa: BLE001
+            why = f"run: {type(e).__name__}: {e}"
+    elif why is None:
+        why = "another rank failed"
+    ok = agree(why is None)
+    dist.barrier()
+    if sp is not None:
+        sp.close()
+    for b in bufs:
+        b.free()
+    if c is not None:
+        B.release(c)
+    return ok, why or ("" if ok else "another rank failed")
+
+
+def measure_greeks(args, dtype, rank, world, local, dist, peer, flush, weak=False, exchange=None, sharded_ok=True):
     """Device-timed and end-to-end paths/s of the Greeks graph in `dtype`.
 
     Strong scaling (default): the unsplit 2^28-path graph compiled as rank r
@@ -574,7 +627,7 @@ def measure_greeks(args, dtype, rank, world, local, dist, peer, flush, weak=Fals
     from cudacaml_b200 import multi as M
     from cudacaml_b200 import runtime as R
 
-    sharded = world > 1 and not weak
+    sharded = world > 1 and not weak and sharded_ok
     total = PATHS * world if weak else PATHS
     base, per = M.path_range(total, world, rank)
     shard_peers = None
@@ -863,7 +916,11 @@ def run_ours(args):
             dist.all_gather_object(got, h)
             return got
         peer = M.PeerSum(world, rank, exchange)
-    head = measure_greeks(args, F64, rank, world, local, dist, peer, flush, exchange=exchange if world > 1 else None)
+    sharded_ok, sharded_why = True, ""
+    if world > 1:
+        sharded_ok, sharded_why = sharded_probe(rank, world, local, dist, exchange)
+    head = measure_greeks(args, F64, rank, world, local, dist, peer, flush, exchange=exchange if world > 1 else None,
+                          sharded_ok=sharded_ok)
     cf = X.analytic()
     ok = abs(head["outs"]["price"] - cf["price"]) < 0.02
     f32 = None
@@ -924,9 +981,12 @@ def run_ours(args):
             "data": "synthetic (Philox normals generated in registers, seed 42)",
             "config": {"workload": "bs_greeks_f64 (BASELINE configs[1]; F32 under secondary)", "paths_total": PATHS,
                        "paths_per_gpu": head["paths_per_rank"],
-                       "parallelism": (f"dp{world} (sharded program: rank r walks paths [r*2^28/{world}, "
-                                       f"(r+1)*2^28/{world}), the 4 reductions combined across ranks in the kernel's "
-                                       f"last block over NVLink peer memory)") if world > 1 else "dp1",
+                       "parallelism": ((f"dp{world} (sharded program: rank r walks paths [r*2^28/{world}, "
+                                        f"(r+1)*2^28/{world}), the 4 reductions combined across ranks in the kernel's "
+                                        f"last block over NVLink peer memory)") if sharded_ok else
+                                       (f"dp{world} (counter range split {world} ways, the 4 results summed across "
+                                        f"ranks after the kernel over NVLink peer memory; the sharded program's probe "
+                                        f"failed: {sharded_why})")) if world > 1 else "dp1",
                        "l2": "flushed before every timed step (read-only pass over 256 MiB, twice L2)",
                        "market": "S0=100 K=100 r=0.05 sigma=0.2 T=1"},
             "result": head["outs"], "result_ok_vs_closed_form": ok, "closed_form": cf,
