@@ -323,16 +323,19 @@ __device__ __forceinline__ void map_reduce(const typename F::P& p) {
     }
     for (; g < n4; g += nth) F::elem4(p, (int)(g << 2), acc);
     for (unsigned i = (n4 << 2) + tid; i < n; i += nth) F::elem(p, (int)i, acc);
-  } else if constexpr (F::VEC == 0 && F::PAIRS) {
-    // two independent elements per iteration: two dependency chains for
-    // the scheduler, three copies of the body; each thread still folds its
-    // elements in the same order
+  } else if constexpr (F::VEC == 0 && F::ILP) {
+    // four independent elements per iteration: four dependency chains for
+    // the scheduler (F64 Greeks at 2^28 paths, four instead of two: 2.508 ->
+    // 2.442 ms on one box); each thread still folds its elements in
+    // ascending order, so the bits do not change
     unsigned i = tid;
-    for (; i + nth < n; i += 2 * nth) {
+    for (; i + 3 * nth < n; i += 4 * nth) {
       F::elem(p, (int)i, acc);
       F::elem(p, (int)(i + nth), acc);
+      F::elem(p, (int)(i + 2 * nth), acc);
+      F::elem(p, (int)(i + 3 * nth), acc);
     }
-    if (i < n) F::elem(p, (int)i, acc);
+    for (; i < n; i += nth) F::elem(p, (int)i, acc);
   } else {
     for (unsigned i = tid; i < n; i += nth) F::elem(p, (int)i, acc);
   }

@@ -67,7 +67,7 @@ struct FSum {
   static constexpr int NRED = 1;
   static constexpr int VEC = 1;
   static constexpr int UNROLL = 4;
-  static constexpr bool PAIRS = false;
+  static constexpr bool ILP = false;
   static constexpr bool TAIL = false;
   static __device__ __forceinline__ acc_t identity(int) { return 0.0f; }
   static __device__ __forceinline__ void init(acc_t* acc) { acc[0] = 0.0f; }
