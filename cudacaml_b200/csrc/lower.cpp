@@ -2412,6 +2412,7 @@ class Lowerer {
     l.mode = GM_PERSISTENT;
     l.work = xhi - xlo;
     l.per_block = 256 * 8;
+    l.streams = !scalar_only;
     l.max_grid = R ? max_grid : (1 << 20);
     if (R == 0 && gr.stores.empty()) {
       l.work = 1;  // tails only

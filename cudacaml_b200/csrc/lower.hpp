@@ -102,6 +102,10 @@ struct LaunchSpec {
   int block = 256;
   int smem = 0;  // dynamic shared memory bytes
   int grid_multiple = 1;  // persistent grids: the grid is a multiple of this (cluster size)
+  // map-reduce passes that stream element data: after a spill relaxes their
+  // bound, one more resident block is tried (latency hiding pays for
+  // streams; an instruction-bound estimator runs faster at its own occupancy)
+  bool streams = false;
   std::vector<Slot> slots;
 };
 

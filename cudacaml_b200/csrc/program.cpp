@@ -310,12 +310,22 @@ int compile_tuned(const Lowered& L, CUmodule& mod, std::vector<std::string>& rel
   // Without the bound a pass runs at the occupancy its registers allow; one
   // more resident block per SM often fits without local memory (the LSM date
   // pass: 138 registers, 1 block/SM, unbounded; 128 registers, 2 blocks/SM,
-  // no spills, with the bound 2). Try that level for every relaxed pass and
-  // keep it where nothing spills.
+  // no spills, with the bound 2: LSM price 5.86 -> 5.52 ms). Try that level
+  // for every relaxed pass that streams element data and keep it where
+  // nothing spills. Monte-Carlo estimators, bound by instruction issue, keep
+  // their own occupancy (F64 Greeks with two elements per iteration: 2.59 ms
+  // at 5 blocks/SM against 2.54 at 4, on one box).
   std::vector<int> level(relaxed.size(), 1);
   std::vector<std::string> up = base;
   bool any = false;
   for (size_t r = 0; r < relaxed.size(); ++r) {
+    bool streams = false;
+    for (const auto& l : L.launches)
+      if (l.fn == relaxed[r]) streams = l.streams;
+    if (!streams) {
+      up.push_back("-DCCB_MINB_" + relaxed[r].substr(14) + "=1");
+      continue;
+    }
     CUfunction f;
     CCB_CU(d.cuModuleGetFunction(&f, mod, relaxed[r].c_str()));
     int occ = 1;
