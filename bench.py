@@ -52,12 +52,13 @@ sys.path.insert(0, ROOT)
 PATHS = 1 << 28
 SEED = 42
 # Warp instructions executed per path by the fused F64 Greeks kernel, from
-# ncu's smsp__inst_executed.sum over 2^20 paths (9,029,887 / 2^20):
-# profiles/mapreduce_bs_greeks_f64_2p20_instructions.md.
-INST_PER_PATH_F64 = 9029887 / (1 << 20)
-# DRAM bytes per launch of the same kernel (read 42,240, write 0; constant in
+# ncu's smsp__inst_executed.sum over 2^26 paths (539,122,169 / 2^26; 443
+# paths per thread, the steady state of the 2^28-path launch):
+# profiles/mapreduce_bs_greeks_f64_2p26_instructions.md.
+INST_PER_PATH_F64 = 539122169 / (1 << 26)
+# DRAM bytes per launch of the same kernel (read 55,040, write 0; constant in
 # the path count), same capture.
-DRAM_BYTES_GREEKS_F64 = 42240
+DRAM_BYTES_GREEKS_F64 = 55040
 
 
 def peaks():
@@ -968,7 +969,7 @@ def run_ours(args):
     roofline = {"bound": "issue", "achieved": achieved / 1e9, "peak": issue_peak / 1e9, "unit": "Gwarp-inst/s",
                 "frac": achieved / issue_peak, "traffic": DRAM_BYTES_GREEKS_F64,
                 "note": f"Monte Carlo moves ~0 algorithmic bytes; {INST_PER_PATH_F64:.3f} warp instructions per path "
-                        f"(ncu smsp__inst_executed.sum, profiles/mapreduce_bs_greeks_f64_2p20_instructions.md) x "
+                        f"(ncu smsp__inst_executed.sum, profiles/mapreduce_bs_greeks_f64_2p26_instructions.md) x "
                         f"{head['paths_per_rank']} paths per launch / the average step, against 148 SMs x 4 "
                         f"sub-partitions x 1 warp instruction/cycle x {pk['sm_max_mhz']:.0f} MHz ({pk['src']} max "
                         f"clock); traffic = DRAM bytes per launch from the same ncu capture"
