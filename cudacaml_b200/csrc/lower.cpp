@@ -2283,7 +2283,8 @@ class Lowerer {
     src << "  static constexpr int NRED = " << R << ";\n  static constexpr int VEC = " << (scalar_only ? 0 : 1) << ";\n";
     // F64 estimators interleave four elements per iteration (F64 Greeks at
     // 2^28 paths: two instead of one 2.59 -> 2.53 ms; four instead of two
-    // 2.508 -> 2.442 ms on one box; the F32 pass gained nothing from two)
+    // 2.508 -> 2.442 ms on one box; eight 2.61 against four 2.436 on
+    // another; the F32 pass gained nothing from two or four)
     src << "  static constexpr bool ILP = " << (scalar_only && R > 0 && dt_size(acc) == 8 ? "true" : "false") << ";\n";
     // Passes that stream data keep 4 vector steps in flight; compute-bound
     // passes (Philox Monte Carlo) unroll 2 to keep the body small.
