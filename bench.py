@@ -572,8 +572,10 @@ def sharded_probe(rank, world, local, dist, exchange):
     from cudacaml_b200 import runtime as R
     from cudacaml_b200.ir import F64
 
+    dev = f"cuda:{local}" if dist.get_backend() == "nccl" else "cpu"
+
     def agree(ok):
-        t = torch.tensor([1.0 if ok else 0.0], device=f"cuda:{local}")
+        t = torch.tensor([1.0 if ok else 0.0], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MIN)
         return float(t[0]) > 0.5
 
