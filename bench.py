@@ -971,11 +971,14 @@ def run_ours(args):
     roofline = {"bound": "issue", "achieved": achieved / 1e9, "peak": issue_peak / 1e9, "unit": "Gwarp-inst/s",
                 "frac": achieved / issue_peak, "traffic": DRAM_BYTES_GREEKS_F64,
                 "note": f"Monte Carlo moves ~0 algorithmic bytes; {INST_PER_PATH_F64:.3f} warp instructions per path "
-                        f"(ncu smsp__inst_executed.sum, profiles/mapreduce_bs_greeks_f64_2p26_instructions.md) x "
+                        f"(ncu smsp__inst_executed.sum over 2^26 paths, 443 per thread: the steady state of this "
+                        f"launch; profiles/mapreduce_bs_greeks_f64_2p26_instructions.md) x "
                         f"{head['paths_per_rank']} paths per launch / the average step, against 148 SMs x 4 "
                         f"sub-partitions x 1 warp instruction/cycle x {pk['sm_max_mhz']:.0f} MHz ({pk['src']} max "
-                        f"clock); traffic = DRAM bytes per launch from the same ncu capture"
-                        + ("; the step includes the cross-rank sum of the 4 scalars" if world > 1 else "")}
+                        f"clock); ncu's issue-active on the same capture is 75 %; traffic = DRAM bytes per launch "
+                        f"from the same ncu capture"
+                        + ("; the step includes the cross-rank combine of the 4 totals inside the kernel"
+                           if world > 1 else "")}
     if rank == 0:
         line = {
             "metric": "MC paths/s (Black-Scholes price + pathwise Greeks)", "value": head["value"], "unit": "paths/s",
