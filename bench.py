@@ -684,6 +684,16 @@ def measure_greeks(args, dtype, rank, world, local, dist, peer, flush, weak=Fals
     clocks = ClockSampler(local)
     clocks.start()
     time.sleep(0.3)
+    # The ranks' steps are coupled (each step's cross-rank combine waits for
+    # every rank), so a rank whose host starts the timed loop late stalls
+    # the others' first timed step (on 8 GPUs the sampler's start-up skew
+    # once added ~2 ms per step on average). Every rank leaves one barrier
+    # right before the loop, and one untimed step on every GPU lines the
+    # GPUs up before the first timed one.
+    barrier()
+    if world > 1:
+        flush(stream)
+        step()
     for k in range(args.steps):
         flush(stream)
         evs[k][0].record(stream)
