@@ -768,8 +768,8 @@ def measure_mlp_dp(rank, world, local, dist, comm, flush, pk):
     """The MLP training step data-parallel over `world` GPUs (BASELINE
     configs: global batch 8192 split by rows, gradients combined by NCCL
     all-reduce): per rank the tf32 step on 8192/world rows; the NCCL
-    all-reduces (sum) of loss, dW1 and dW2 run on a second stream, each as
-    soon as its output is final, so dW1's overlaps the dW2 product. Device
+    all-reduces (sum) of loss, dW2 and dW1 run on a second stream, each as
+    soon as its output is final, so dW2's overlaps the dA1, dZ1 and dW1 work. Device
     time per step, max over ranks; inputs device-generated, rank-specific
     rows."""
     import math
@@ -817,12 +817,15 @@ def measure_mlp_dp(rank, world, local, dist, comm, flush, pk):
 
     # Each output's all-reduce runs on a communication stream as soon as the
     # output is final (an event recorded right after the kernel that writes
-    # it), in production order: the loss, dW1 while dW2 is being computed,
-    # then dW2. Every rank issues the same collectives in the same order.
+    # it), in production order -- the launch scheduler runs dW2's product
+    # right after the dY/loss pass: the loss, dW2 while dA1, dZ1 and dW1 are
+    # computed, then dW1 (collectives on one communicator run in issue order,
+    # so the issue order must follow production). Every rank issues the same
+    # collectives in the same order.
     cs = R.Stream()
     ev_out = [R.Event() for _ in c.outputs]
     ev_join = R.Event()
-    produced = ["loss", "dloss/dW1", "dloss/dW2"]
+    produced = ["loss", "dloss/dW2", "dloss/dW1"]
     pos = {nm: j for j, (nm, _, _) in enumerate(c.outputs)}
     e0, e1, e2 = R.Event(), R.Event(), R.Event()
     t_step, t_comp = [], []
@@ -854,8 +857,8 @@ def measure_mlp_dp(rank, world, local, dist, comm, flush, pk):
     fl = X.mlp_flops(bsz, din, hid, dout)
     return {"ms": ms, "tflops": fl / ms / 1e9, "compute_ms": ms_comp, "allreduce_ms": ms - ms_comp,
             "allreduce_bytes_per_rank": ar_bytes, "rows_per_gpu": per,
-            "note": "global batch 8192 split by rows; per rank the tf32 step; NCCL all-reduces (sum) of loss, dW1, "
-                    "dW2 on a second stream, each started when its output is final (dW1's overlaps the dW2 product); "
+            "note": "global batch 8192 split by rows; per rank the tf32 step; NCCL all-reduces (sum) of loss, dW2, "
+                    "dW1 on a second stream, each started when its output is final (dW2's overlaps dA1, dZ1, dW1); "
                     "compute_ms = the step's own kernels, allreduce_ms = what the collectives add; device time, max "
                     "over ranks, median of 10 after 3 warm-ups"}
 
