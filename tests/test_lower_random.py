@@ -209,3 +209,49 @@ def test_zero_size_tensors_lower_compile_and_evaluate(name, g):
         assert out["r"].to_list() == [2.0] * 4 and out["q"].shape == (4, 0) and out["t"].shape == (0, 4)
     if name.startswith("matmul"):
         assert not np.any(out["c"].data)
+
+
+def _kernel_io(src):
+    """{kernel: (nodes it reads, nodes it writes)} from the generated source:
+    a pass reads node t through a `const T* b<t>` field of its parameter
+    block and writes it through a `T* o<t>` field."""
+    import re
+    io, cur, fields = {}, None, {}
+    for line in src.splitlines():
+        m = re.match(r"struct (F\d+) \{", line)
+        if m:
+            cur = m.group(1)
+            fields[cur] = (set(), set())
+            continue
+        m = re.match(r"\s+const \w[\w ]*\* __restrict__ b(\d+);", line)
+        if m and cur:
+            fields[cur][0].add(int(m.group(1)))
+            continue
+        m = re.match(r"\s+\w[\w ]*\* __restrict__ o(\d+);", line)
+        if m and cur:
+            fields[cur][1].add(int(m.group(1)))
+            continue
+        m = re.search(r'extern "C" __global__ .* (ccb_\w+)\(const (?:__grid_constant__ )?(F\d+)::P p\)', line)
+        if m:
+            io[m.group(1)] = fields.get(m.group(2), (set(), set()))
+    return io
+
+
+@pytest.mark.parametrize("seed", range(0, 400, 7))
+def test_launch_order_keeps_every_producer_before_its_consumers(seed):
+    """The launch scheduler may move a launch that writes a program output
+    ahead of others; on random graphs every launch still comes after the
+    launch that writes each node it reads."""
+    rnd = random.Random(seed)
+    g, _, _ = random_graph(rnd, seed)
+    info = B.lower_info(g)
+    order = [ln.split()[1] for ln in info["plan"].splitlines() if ln.startswith("launch")]
+    io = _kernel_io(info["source"])
+    writer = {}
+    for k, fn in enumerate(order):
+        for t in io.get(fn, (set(), set()))[1]:
+            writer.setdefault(t, k)
+    for k, fn in enumerate(order):
+        for t in io.get(fn, (set(), set()))[0]:
+            if t in writer:
+                assert writer[t] < k, (fn, t, order)
